@@ -1,0 +1,412 @@
+#!/usr/bin/env python
+"""C-TARQ linear effective HBM GB/s on the Qwen2-7B decoder-linear stack (decode).
+
+One step = one decode pass of M tokens through every C-TARQ linear of Qwen2-7B
+(28 layers x {q 3584->3584, k 3584->512, v 3584->512, o 3584->3584, gate 3584->18944,
+up 3584->18944, down 18944->3584}), 1 % dW, a seeded 25 % of the calls routed.
+Weights total 3.3 GB, far above L2, so no flush is needed between steps.
+
+Effective bytes per call (the metric's numerator, independent of the device layout):
+    2*M*K (x) + N*K/2 (int4 base) + 2*N (f16 scales) + [any token routed]*(3*nnz + 4*(N+1)) + 2*M*N (y)
+value = bytes of all calls of all ranks / max-over-ranks device time (CUDA events).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M] [--impl reference]
+
+--impl reference times the reference's CPU algorithm (the oracle restatement of
+saccade-core's op.rs; the Rust reference cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "saccade-x2_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+HIDDEN, INTER, LAYERS, KV_DIM = 3584, 18944, 28, 512
+PROJ = [("q", 3584, HIDDEN), ("k", KV_DIM, HIDDEN), ("v", KV_DIM, HIDDEN), ("o", HIDDEN, 3584),
+        ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]  # (name, N, K)
+T4_BOOSTED = 8.0        # between the variance of N(0,1) tokens (~1) and x8 tokens (~64)
+T8_NEVER = float(np.finfo(np.float32).max)
+METRIC = "C-TARQ linear effective HBM GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--fill", type=float, default=0.01)
+    ap.add_argument("--route-frac", type=float, default=0.25)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def call_bytes(n, k, m, nnz, routed):
+    return 2 * m * k + n * k // 2 + 2 * n + (3 * nnz + 4 * (n + 1) if routed else 0) + 2 * m * n
+
+
+def stack_spec(layers, m, route_frac, seed):
+    """(layer, proj, N, K, boosted-token list) for every call of one step."""
+    rng = np.random.default_rng(seed)
+    calls = []
+    for li in range(layers):
+        for name, n, k in PROJ:
+            boosted = [t for t in range(m) if rng.random() < route_frac]
+            calls.append((li, name, n, k, boosted))
+    return calls
+
+
+def synth_compressed_np(n, k, fill, rng):
+    """Reference-format buffers with the value distributions of a packed N(0, 0.02) matrix."""
+    packed = rng.integers(0, 2 ** 32, size=(n, k // 8), dtype=np.uint32)
+    scale = (0.02 * (3.0 + np.abs(rng.standard_normal(n)) * 0.5) / 7.0).astype(np.float16)
+    nnz = int(round(n * k * fill))
+    flat = np.sort(rng.choice(n * k, size=nnz, replace=False))
+    rows, cols = flat // k, flat % k
+    row_ptrs = np.zeros(n + 1, dtype=np.uint32)
+    row_ptrs[1:] = np.cumsum(np.bincount(rows, minlength=n))
+    vals = rng.integers(-127, 128, size=nnz).astype(np.int8).view(np.uint8)
+    ds = np.float16(0.006 / 127.0)
+    return packed, scale, row_ptrs, cols.astype(np.uint32), vals, ds
+
+
+def make_x(m, k, boosted, rng):
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    for t in boosted:
+        x[t] *= 8.0
+    return x.astype(np.float16)
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ln in open(self.path).read().splitlines():
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ CPU (oracle) side
+
+def build_oracle_stack(calls, fill, seed, tokens):
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    items = []
+    for li, name, n, k, boosted in calls:
+        packed, scale, rp, cols, vals, ds = synth_compressed_np(n, k, fill, rng)
+        c = O.Compressed(packed, scale.view(np.uint16), rp, cols, vals, int(np.array([ds]).view(np.uint16)[0]), n, k)
+        op = O.OracleLinear(c, T4_BOOSTED, T8_NEVER)
+        x = make_x(tokens, k, boosted, rng).view(np.uint16)
+        items.append((op, x, call_bytes(n, k, tokens, c.nnz, len(boosted) > 0)))
+    return items
+
+
+def time_oracle(items, reps, native=True):
+    t0 = time.perf_counter()
+    nbytes = 0
+    for _ in range(reps):
+        for op, x, b in items:
+            op.forward(x, native=native)
+            nbytes += b
+    dt = time.perf_counter() - t0
+    return nbytes / dt / 1e9, dt
+
+
+def cpu_baseline(args):
+    """The oracle's op.rs restatement timed on the host cores over a bounded sample."""
+    from oracle import oracle as O
+    try:
+        O.lib(native=True)
+        native = True
+    except Exception:  # noqa: BLE001 - no compiler on the host: use the portable build
+        native = False
+    calls = stack_spec(1, args.tokens, args.route_frac, seed=1234)
+    items = build_oracle_stack(calls, args.fill, 99, args.tokens)
+    _, dt1 = time_oracle(items, 1, native)
+    reps = max(1, min(200, int(args.cpu_seconds / max(dt1, 1e-3))))
+    gbs, dt = time_oracle(items, reps, native)
+    cores = os.cpu_count()
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"1 Qwen2-7B decoder layer (7 linears, M={args.tokens}) x {reps} reps, {dt:.1f} s; "
+                      f"C restatement of op.rs, OpenMP over rows ({'-march=native' if native else 'x86-64-v3'})"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    try:
+        O.lib(native=True)
+        native = True
+    except Exception:  # noqa: BLE001
+        native = False
+    calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234)
+    items = build_oracle_stack(calls, args.fill, 99, args.tokens)
+    step_bytes = sum(b for _, _, b in items)
+    # one step is bounded: if the whole stack takes too long on this host, time a prefix of it
+    _, dt1 = time_oracle(items[: 7], 1, native)
+    per_step_est = dt1 * len(items) / 7
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    if per_step_est > budget:
+        keep = max(7, int(len(items) * budget / per_step_est) // 7 * 7)
+        items = items[:keep]
+        step_bytes = sum(b for _, _, b in items)
+    for _ in range(args.warmup):
+        time_oracle(items, 1, native)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        time_oracle(items, 1, native)
+    dt = time.perf_counter() - t0
+    value = step_bytes * args.steps / dt / 1e9
+    sample = (f"{len(items)} of {len(calls)} linears per step (Qwen2-7B stack, M={args.tokens}); "
+              f"C restatement of op.rs (Rust reference not buildable here), OpenMP over rows")
+    out = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+           "config": {"workload": "qwen2-7b decoder linear stack, decode", "tokens": args.tokens,
+                      "layers": args.layers, "dw_fill": args.fill, "route_frac": args.route_frac},
+           "impl": "reference",
+           "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+# ------------------------------------------------------------------ GPU side
+
+def run_ours(args, rank, world):
+    import torch
+    import torch.distributed as dist
+
+    import saccade_core as sc
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234 + rank)
+    ops, xs, step_bytes, big = [], [], 0, []
+    routed_calls = 0
+    for li, name, n, k, boosted in calls:
+        packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
+        scale = ((0.02 * (3.0 + torch.rand(n, device=dev, generator=gen))) / 7.0).to(torch.float16)
+        nnz = int(round(n * k * args.fill))
+        flat = torch.randperm(n * k, device=dev, generator=gen)[:nnz].sort().values if n * k < 2 ** 27 else \
+            torch.unique(torch.randint(0, n * k, (int(nnz * 1.02) + 16,), device=dev, generator=gen))[:nnz]
+        rows, cols = flat // k, flat % k
+        rp = torch.zeros(n + 1, dtype=torch.int64, device=dev)
+        rp[1:] = torch.cumsum(torch.bincount(rows, minlength=n), 0)
+        vals = torch.randint(-127, 128, (flat.numel(),), dtype=torch.int8, device=dev, generator=gen).view(torch.uint8)
+        sp = sc.SparseDeltaMatrix(rp.to(torch.int32), cols.to(torch.int32), vals,
+                                  torch.tensor([0.006 / 127.0], dtype=torch.float16))
+        op = sc.SaccadeLinearOp(packed, scale, sp, sc.SaccadeConfig(T4_BOOSTED, T8_NEVER), n, k, device=dev,
+                                mode=args.mode)
+        del packed, scale, flat, rows, cols, rp, vals
+        x = torch.randn((args.tokens, k), device=dev, generator=gen)
+        for t in boosted:
+            x[t] *= 8.0
+        x = x.to(torch.float16)
+        b = call_bytes(n, k, args.tokens, op.delta_nnz, len(boosted) > 0)
+        routed_calls += len(boosted) > 0
+        ops.append(op)
+        xs.append(x)
+        step_bytes += b
+        if name in ("gate", "up", "down"):
+            big.append((len(ops) - 1, b))
+    torch.cuda.synchronize()
+
+    ys = [None] * len(ops)
+
+    def step():
+        for i, op in enumerate(ops):
+            ys[i] = op.forward(xs[i])
+
+    def big_step():
+        for i, _ in big:
+            ys[i] = ops[i].forward(xs[i])
+
+    g_step = sc.CapturedStep(step, dev)
+    g_big = sc.CapturedStep(big_step, dev)
+
+    # end to end through the public API: pinned host inputs -> device -> C-TARQ -> host outputs
+    xs_host = [x.cpu().pin_memory() for x in xs]
+    ys_host = [torch.empty((args.tokens, op.out_features), dtype=torch.float16).pin_memory() for op in ops]
+    xs_dev = [torch.empty_like(x) for x in xs]
+
+    def e2e_step():
+        for i, op in enumerate(ops):
+            xs_dev[i].copy_(xs_host[i], non_blocking=True)
+            ys_host[i].copy_(op.forward(xs_dev[i]), non_blocking=True)
+
+    g_e2e = sc.CapturedStep(e2e_step, dev)
+    h2d = sum(x.numel() * 2 for x in xs)
+    d2h = sum(y.numel() * 2 for y in ys_host)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed(graph, steps, sync_each=False):
+        for _ in range(args.warmup):
+            graph.replay()
+        graph.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(graph.stream):
+            s.record()
+            for _ in range(steps):
+                graph.replay()
+                if sync_each:
+                    graph.synchronize()
+            e.record()
+        graph.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    ms = timed(g_step, args.steps)
+    clk = clocks.stop()
+    ms_big = timed(g_big, args.steps)
+    ms_e2e = timed(g_e2e, args.steps, sync_each=True)
+
+    # correctness guard on the timed configuration: no device-side error recorded
+    for op in ops[:7]:
+        op.check_device()
+
+    value = step_bytes * world / (ms / 1e3) / 1e9
+    big_bytes = sum(b for _, b in big)
+    achieved = big_bytes / (ms_big / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_tc_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
+        except ValueError:
+            traffic = None
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "qwen2-7b decoder linear stack, decode", "tokens": args.tokens,
+                   "layers": args.layers, "calls_per_step": len(ops), "routed_calls_per_step": routed_calls,
+                   "dw_fill": args.fill, "mode": args.mode, "bytes_per_step": step_bytes,
+                   "weights": "int4 base + i8 dW, f32 accumulation", "l2": "inputs > L2 (3.3 GB of weights)",
+                   "parallelism": f"replicas{world}", "graph": "one CUDA graph per step"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "k_decode_tc (+ its router) on the gate/up/down calls",
+                     "peak_kind": f"{peak_kind} hbm copy"},
+        "clocks": clk,
+        "e2e": {"value": round(step_bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "how": "pinned host x -> device, forward, y -> pinned host, captured step, host sync each step"},
+        "gpu_launches": 2 * len(ops) * args.steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(args)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        run_ours(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,595 @@
+// sc_api.cu -- the extern "C" entry points of libsaccade_ctarq.so.
+//
+// sc_layer_create mirrors SaccadeLinearOp::new (config.rs:76-150): it takes the
+// reference-format buffers, validates the dW CSR (the reference would panic on a column
+// >= in_features in build_csc, config.rs:176), and builds the device layout.  sc_forward
+// mirrors cpu_fwd (op.rs:10-185): router -> base product -> dW for routed tokens -> f16.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "sc_internal.h"
+
+namespace sc {
+
+static thread_local std::string g_last_error;
+static std::atomic<int> g_bypass{0};
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+sc_status cuda_fail(cudaError_t e, const char* what) {
+    set_error(std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+    return SC_ECUDA;
+}
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+static int64_t ceil_to(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+static int sm_count(int dev) {
+    int n = 148;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+WsLayout plan_workspace(const Layer& L, int64_t m) {
+    WsLayout w;
+    w.Mp = m <= 8 ? 8 : (m <= 16 ? 16 : ceil_to(m, 32));
+    w.chunk_tokens = 32;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = static_cast<size_t>(ceil_to(static_cast<int64_t>(off + bytes), 256));
+        return o;
+    };
+    w.xk = take(static_cast<size_t>(L.KB * 64 * w.Mp * 2));
+    w.mask = take(static_cast<size_t>(m > 0 ? m : 1));
+    w.scores = take(static_cast<size_t>(4 * (m > 0 ? m : 1)));
+    w.ridx = take(static_cast<size_t>(4 * (m > 0 ? m : 1)));
+    w.nrouted = take(16);
+    w.counter = take(16);
+    const int64_t RT = (L.Np + 127) / 128;
+    const int64_t first = std::min<int64_t>(m, 32);
+    const int occ = first <= 16 ? 2 : 1;
+    const int64_t target = static_cast<int64_t>(L.sms) * occ;
+    int64_t ks = (target + RT / 2) / RT;
+    ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(32, std::max<int64_t>(1, L.KB / 4))));
+    w.ksplit = static_cast<int>(ks);
+    w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
+    w.rtcount = take(static_cast<size_t>(RT * 4));
+    w.total = off;
+    return w;
+}
+
+// ------------------------------------------------------------------ default workspaces
+
+struct DefaultWs {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+static std::mutex g_ws_mu;
+static std::vector<DefaultWs> g_ws;
+
+static sc_status default_workspace(int dev, size_t need, void** out) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    if (static_cast<int>(g_ws.size()) <= dev) g_ws.resize(dev + 1);
+    DefaultWs& d = g_ws[dev];
+    if (d.bytes < need) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return cuda_fail(e, "default workspace: synchronize");
+        if (d.ptr) cudaFree(d.ptr);
+        d.ptr = nullptr;
+        d.bytes = 0;
+        size_t sz = std::max<size_t>(need, static_cast<size_t>(1) << 20);
+        e = cudaMalloc(&d.ptr, sz);
+        if (e != cudaSuccess) return cuda_fail(e, "default workspace: cudaMalloc");
+        e = cudaMemset(d.ptr, 0, sz);
+        if (e != cudaSuccess) return cuda_fail(e, "default workspace: memset");
+        d.bytes = sz;
+    }
+    *out = d.ptr;
+    return SC_OK;
+}
+
+// ------------------------------------------------------------------ forward
+
+static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
+                              const float* bias, uint8_t* mask_out, int32_t* ridx_out, int32_t* nrouted_out,
+                              void* ws, size_t ws_bytes, cudaStream_t stream, bool partial) {
+    if (m < 0) {
+        set_error("sc_forward: negative token count");
+        return SC_EINVAL;
+    }
+    if (m == 0) return SC_OK;
+    if (!x || !y) {
+        set_error("sc_forward: null x or y");
+        return SC_EINVAL;
+    }
+    if (x_dtype != SC_F16 && x_dtype != SC_BF16) {
+        set_error("sc_forward: x dtype must be F16 or BF16");
+        return SC_EINVAL;
+    }
+    if (!partial && y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32) {
+        set_error("sc_forward: y dtype must be F16, BF16 or F32");
+        return SC_EINVAL;
+    }
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
+        set_error("sc_forward: workspace must be 256-byte aligned");
+        return SC_ENONCONTIG;
+    }
+    const WsLayout w = plan_workspace(L, m);
+    if (ws_bytes < w.total) {
+        set_error("sc_forward: workspace of " + std::to_string(ws_bytes) + " bytes, need " +
+                  std::to_string(w.total));
+        return SC_ENOMEM;
+    }
+    unsigned char* base = static_cast<unsigned char*>(ws);
+    uint16_t* xk = reinterpret_cast<uint16_t*>(base + w.xk);
+    uint8_t* mask = mask_out ? mask_out : reinterpret_cast<uint8_t*>(base + w.mask);
+    int32_t* ridx = ridx_out ? ridx_out : reinterpret_cast<int32_t*>(base + w.ridx);
+    int32_t* nrouted = nrouted_out ? nrouted_out : reinterpret_cast<int32_t*>(base + w.nrouted);
+    const bool bypass = g_bypass.load() != 0;
+
+    RouterArgs r;
+    r.x = x;
+    r.x_dtype = x_dtype;
+    r.x_row_stride = L.shard_kind == SC_SHARD_ROWS ? L.fullK : L.K;
+    r.x_col0 = L.shard_kind == SC_SHARD_ROWS ? L.col_begin : 0;
+    r.M = m;
+    r.K = L.K;
+    r.Mp = w.Mp;
+    r.KB = L.KB;
+    r.t4 = L.t4;
+    r.t8 = L.t8;
+    r.route_all = bypass ? 1 : 0;
+    r.xk = xk;
+    r.mask = mask;
+    r.scores = reinterpret_cast<float*>(base + w.scores);
+    r.ridx = ridx;
+    r.nrouted = nrouted;
+    r.counter = reinterpret_cast<uint32_t*>(base + w.counter);
+    r.status = L.status;
+    cudaError_t e = launch_router(r, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "router launch");
+
+    DecodeArgs d;
+    d.L = &L;
+    d.xk = xk;
+    d.Mp = w.Mp;
+    d.mask = mask;
+    d.ridx = ridx;
+    d.nrouted = nrouted;
+    d.route_all = bypass ? 1 : 0;
+    d.dcol_begin = 0;
+    d.dcol_end = L.K;
+    d.y = y;
+    d.y_dtype = partial ? SC_F32 : y_dtype;
+    d.bias = partial ? nullptr : bias;
+    d.partial_out = partial ? 1 : 0;
+    d.ws_partial = reinterpret_cast<float*>(base + w.partial);
+    d.ws_rtcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
+    if (L.mode == SC_MODE_EXACT) {
+        d.tok0 = 0;
+        d.ntok = m;
+        d.ksplit = 1;
+        e = launch_decode_exact(d, bypass ? 1 : 0, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "exact kernel launch");
+        return SC_OK;
+    }
+    for (int64_t t0 = 0; t0 < m; t0 += w.chunk_tokens) {
+        d.tok0 = t0;
+        d.ntok = std::min<int64_t>(w.chunk_tokens, m - t0);
+        d.ksplit = w.ksplit;
+        e = launch_decode_tc(d, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "decode kernel launch");
+    }
+    return SC_OK;
+}
+
+}  // namespace sc
+
+using namespace sc;
+
+struct sc_layer {
+    Layer L;
+};
+
+extern "C" {
+
+int sc_abi_version(void) { return SC_ABI_VERSION; }
+
+const char* sc_op_name(void) { return "fused_c_tarq_saccade_linear"; }
+
+size_t sc_last_error(char* buf, size_t len) {
+    const std::string& s = g_last_error;
+    if (buf && len > 0) {
+        size_t n = std::min(len - 1, s.size());
+        std::memcpy(buf, s.data(), n);
+        buf[n] = '\0';
+    }
+    return s.size();
+}
+
+void sc_set_bypass_c_tarq(int on) { g_bypass.store(on ? 1 : 0); }
+int sc_is_c_tarq_bypassed(void) { return g_bypass.load(); }
+
+static void free_layer(Layer& L) {
+    cudaFree(L.wq);
+    cudaFree(L.scale);
+    cudaFree(L.rowptr);
+    cudaFree(L.col);
+    cudaFree(L.val);
+    cudaFree(L.status);
+    L.wq = nullptr;
+    L.scale = nullptr;
+    L.rowptr = nullptr;
+    L.col = nullptr;
+    L.val = nullptr;
+    L.status = nullptr;
+}
+
+sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
+    if (!desc || !out) {
+        set_error("sc_layer_create: null argument");
+        return SC_EINVAL;
+    }
+    *out = nullptr;
+    const int64_t N = desc->out_features, K = desc->in_features;
+    if (N <= 0 || K <= 0 || K % 8 != 0) {
+        set_error("sc_layer_create: need out_features > 0 and in_features a positive multiple of 8");
+        return SC_EINVAL;
+    }
+    if (!desc->packed_base || !desc->scale_base) {
+        set_error("sc_layer_create: packed_base and scale_base are required");
+        return SC_EINVAL;
+    }
+    const int64_t nnz_in = desc->delta_nnz;
+    if (nnz_in < 0 || (nnz_in > 0 && (!desc->delta_row_ptrs || !desc->delta_col_indices || !desc->delta_values))) {
+        set_error("sc_layer_create: delta_nnz > 0 needs row_ptrs, col_indices and values");
+        return SC_EINVAL;
+    }
+    if (desc->mode != SC_MODE_FAST && desc->mode != SC_MODE_EXACT) {
+        set_error("sc_layer_create: unknown mode");
+        return SC_EINVAL;
+    }
+    Layer L;
+    L.device = desc->device;
+    L.mode = desc->mode;
+    L.fullN = N;
+    L.fullK = K;
+    L.t4 = desc->t4;
+    L.t8 = desc->t8;
+    L.shard_kind = desc->shard_kind;
+    int64_t r0 = 0, r1 = N, c0 = 0, c1 = K;
+    if (desc->shard_kind != SC_SHARD_NONE) {
+        const int n = desc->shard_count, i = desc->shard_index;
+        if (n <= 0 || i < 0 || i >= n) {
+            set_error("sc_layer_create: bad shard index/count");
+            return SC_EINVAL;
+        }
+        if (desc->shard_kind == SC_SHARD_COLUMNS) {
+            r0 = std::min<int64_t>(N, ceil_to(N * i / n, 16));
+            r1 = std::min<int64_t>(N, ceil_to(N * (i + 1) / n, 16));
+            if (i == n - 1) r1 = N;
+        } else if (desc->shard_kind == SC_SHARD_ROWS) {
+            c0 = std::min<int64_t>(K, ceil_to(K * i / n, 64));
+            c1 = std::min<int64_t>(K, ceil_to(K * (i + 1) / n, 64));
+            if (i == n - 1) c1 = K;
+        } else {
+            set_error("sc_layer_create: unknown shard kind");
+            return SC_EINVAL;
+        }
+        if (r1 <= r0 || c1 <= c0) {
+            set_error("sc_layer_create: shard is empty");
+            return SC_EINVAL;
+        }
+    }
+    L.row_begin = r0;
+    L.col_begin = c0;
+    L.N = r1 - r0;
+    L.K = c1 - c0;
+    if (L.K > 65536) {
+        set_error("sc_layer_create: in_features per shard above 65536 (u16 dW columns)");
+        return SC_EUNSUPPORTED;
+    }
+    L.Np = ceil_to(L.N, 16);
+    L.Kp = ceil_to(L.K, 64);
+    L.KB = L.Kp / 64;
+
+    DeviceGuard guard(L.device);
+    if (!guard.ok) {
+        set_error("sc_layer_create: cannot select device " + std::to_string(L.device));
+        return SC_ECUDA;
+    }
+    L.sms = sm_count(L.device);
+    cudaError_t e;
+    const bool on_dev = desc->buffers_on_device != 0;
+    const int64_t kw_full = K / 8;
+
+    // ---- dW CSR: validate and slice on the host (load time only)
+    std::vector<uint32_t> rp(N + 1, 0);
+    std::vector<uint32_t> ci(static_cast<size_t>(nnz_in));
+    std::vector<uint8_t> cv(static_cast<size_t>(nnz_in));
+    if (nnz_in > 0) {
+        const cudaMemcpyKind kind = on_dev ? cudaMemcpyDeviceToHost : cudaMemcpyHostToHost;
+        if ((e = cudaMemcpy(rp.data(), desc->delta_row_ptrs, (N + 1) * 4, kind)) != cudaSuccess ||
+            (e = cudaMemcpy(ci.data(), desc->delta_col_indices, nnz_in * 4, kind)) != cudaSuccess ||
+            (e = cudaMemcpy(cv.data(), desc->delta_values, nnz_in, kind)) != cudaSuccess)
+            return cuda_fail(e, "sc_layer_create: reading dW");
+        if (rp[0] != 0 || static_cast<int64_t>(rp[N]) != nnz_in) {
+            set_error("sc_layer_create: delta_row_ptrs must start at 0 and end at delta_nnz");
+            return SC_EINVAL;
+        }
+        for (int64_t r = 0; r < N; ++r) {
+            if (rp[r + 1] < rp[r]) {
+                set_error("sc_layer_create: delta_row_ptrs not monotone");
+                return SC_EINVAL;
+            }
+            for (uint32_t q = rp[r]; q < rp[r + 1]; ++q) {
+                if (static_cast<int64_t>(ci[q]) >= K) {
+                    set_error("sc_layer_create: delta column index >= in_features");
+                    return SC_EINVAL;
+                }
+            }
+        }
+        // The reference adds a row's corrections in CSC order: ascending column, and for a
+        // repeated (row, column) in CSR order (config.rs:177-193, op.rs:156-167).  A stable
+        // per-row sort by column reproduces that order for any CSR the caller passes.
+        std::vector<uint32_t> perm;
+        for (int64_t r = 0; r < N; ++r) {
+            const uint32_t lo = rp[r], hi = rp[r + 1];
+            bool sorted = true;
+            for (uint32_t q = lo + 1; q < hi; ++q) sorted = sorted && ci[q - 1] <= ci[q];
+            if (sorted) continue;
+            perm.resize(hi - lo);
+            for (uint32_t q = lo; q < hi; ++q) perm[q - lo] = q;
+            std::stable_sort(perm.begin(), perm.end(), [&](uint32_t a, uint32_t b) { return ci[a] < ci[b]; });
+            std::vector<uint32_t> c2(hi - lo);
+            std::vector<uint8_t> v2(hi - lo);
+            for (uint32_t q = 0; q < hi - lo; ++q) {
+                c2[q] = ci[perm[q]];
+                v2[q] = cv[perm[q]];
+            }
+            std::copy(c2.begin(), c2.end(), ci.begin() + lo);
+            std::copy(v2.begin(), v2.end(), cv.begin() + lo);
+        }
+    }
+    std::vector<uint32_t> srp(L.N + 1, 0);
+    std::vector<uint16_t> scol;
+    std::vector<int8_t> sval;
+    for (int64_t r = 0; r < L.N; ++r) {
+        srp[r] = static_cast<uint32_t>(scol.size());
+        if (nnz_in > 0) {
+            for (uint32_t q = rp[r0 + r]; q < rp[r0 + r + 1]; ++q) {
+                const int64_t c = ci[q];
+                if (c >= c0 && c < c1) {
+                    scol.push_back(static_cast<uint16_t>(c - c0));
+                    sval.push_back(static_cast<int8_t>(cv[q]));
+                }
+            }
+        }
+    }
+    srp[L.N] = static_cast<uint32_t>(scol.size());
+    L.nnz = static_cast<int64_t>(scol.size());
+    {
+        const uint16_t dsb = desc->delta_scale;
+        // f16 -> f32 on the host (exact), matching config.rs:197 `s_cpu...[0].to_f32()`
+        const uint32_t sign = (dsb & 0x8000u) << 16, ex = (dsb >> 10) & 0x1Fu, man = dsb & 0x3FFu;
+        float f;
+        if (ex == 0) {
+            f = static_cast<float>(man) * 5.9604644775390625e-08f;
+            if (sign) f = -f;
+        } else {
+            uint32_t bits = (ex == 0x1F) ? (sign | 0x7F800000u | (man << 13)) : (sign | ((ex - 15u + 127u) << 23) | (man << 13));
+            std::memcpy(&f, &bits, 4);
+        }
+        L.ds = f;
+    }
+
+    // ---- allocations
+    const int64_t wq_words = (L.Np / 16) * L.KB * 128;
+    auto alloc = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes > 0 ? bytes : 16); };
+    if ((e = alloc(reinterpret_cast<void**>(&L.wq), wq_words * 4)) != cudaSuccess ||
+        (e = alloc(reinterpret_cast<void**>(&L.scale), L.Np * 4)) != cudaSuccess ||
+        (e = alloc(reinterpret_cast<void**>(&L.rowptr), (L.N + 1) * 4)) != cudaSuccess ||
+        (e = alloc(reinterpret_cast<void**>(&L.col), (L.nnz + 8) * 2)) != cudaSuccess ||
+        (e = alloc(reinterpret_cast<void**>(&L.val), L.nnz + 16)) != cudaSuccess ||
+        (e = alloc(reinterpret_cast<void**>(&L.status), 16)) != cudaSuccess) {
+        free_layer(L);
+        return cuda_fail(e, "sc_layer_create: cudaMalloc");
+    }
+    L.device_bytes = wq_words * 4 + L.Np * 4 + (L.N + 1) * 4 + (L.nnz + 8) * 2 + (L.nnz + 16);
+
+    // ---- base weights and scales: stage this shard's rows on the device, then repack
+    uint32_t* tmp_packed = nullptr;
+    uint16_t* tmp_scale = nullptr;
+    const uint32_t* src_packed = desc->packed_base + r0 * kw_full;
+    const uint16_t* src_scale = desc->scale_base + r0;
+    if (!on_dev) {
+        if ((e = cudaMalloc(&tmp_packed, L.N * kw_full * 4)) != cudaSuccess ||
+            (e = cudaMalloc(&tmp_scale, L.N * 2)) != cudaSuccess ||
+            (e = cudaMemcpy(tmp_packed, src_packed, L.N * kw_full * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+            (e = cudaMemcpy(tmp_scale, src_scale, L.N * 2, cudaMemcpyHostToDevice)) != cudaSuccess) {
+            cudaFree(tmp_packed);
+            cudaFree(tmp_scale);
+            free_layer(L);
+            return cuda_fail(e, "sc_layer_create: staging weights");
+        }
+        src_packed = tmp_packed;
+        src_scale = tmp_scale;
+    }
+    e = launch_repack(src_packed, kw_full, 0, c0 / 8, L, 0);
+    if (e == cudaSuccess) e = launch_scales(src_scale, 0, L, 0);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(L.rowptr, srp.data(), (L.N + 1) * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && L.nnz > 0) e = cudaMemcpy(L.col, scol.data(), L.nnz * 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && L.nnz > 0) e = cudaMemcpy(L.val, sval.data(), L.nnz, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(L.status, 0, 16);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(tmp_packed);
+    cudaFree(tmp_scale);
+    if (e != cudaSuccess) {
+        free_layer(L);
+        return cuda_fail(e, "sc_layer_create: device layout");
+    }
+    sc_layer* layer = new sc_layer;
+    layer->L = L;
+    *out = layer;
+    return SC_OK;
+}
+
+void sc_layer_destroy(sc_layer* layer) {
+    if (!layer) return;
+    DeviceGuard guard(layer->L.device);
+    free_layer(layer->L);
+    delete layer;
+}
+
+sc_status sc_layer_get_info(const sc_layer* layer, sc_layer_info* info) {
+    if (!layer || !info) {
+        set_error("sc_layer_get_info: null argument");
+        return SC_EINVAL;
+    }
+    const Layer& L = layer->L;
+    info->out_features = L.N;
+    info->in_features = L.K;
+    info->row_begin = L.row_begin;
+    info->col_begin = L.col_begin;
+    info->full_out_features = L.fullN;
+    info->full_in_features = L.fullK;
+    info->delta_nnz = L.nnz;
+    info->device_bytes = L.device_bytes;
+    info->t4 = L.t4;
+    info->t8 = L.t8;
+    info->mode = L.mode;
+    info->device = L.device;
+    return SC_OK;
+}
+
+sc_status sc_layer_set_thresholds(sc_layer* layer, float t4, float t8) {
+    if (!layer) {
+        set_error("sc_layer_set_thresholds: null layer");
+        return SC_EINVAL;
+    }
+    layer->L.t4 = t4;
+    layer->L.t8 = t8;
+    return SC_OK;
+}
+
+sc_status sc_layer_set_mode(sc_layer* layer, int mode) {
+    if (!layer || (mode != SC_MODE_FAST && mode != SC_MODE_EXACT)) {
+        set_error("sc_layer_set_mode: bad argument");
+        return SC_EINVAL;
+    }
+    layer->L.mode = mode;
+    return SC_OK;
+}
+
+sc_status sc_layer_check(sc_layer* layer, void* stream) {
+    if (!layer) {
+        set_error("sc_layer_check: null layer");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(layer->L.device);
+    uint32_t st = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&st, layer->L.status, 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "sc_layer_check");
+    if (st == DEV_OK) return SC_OK;
+    cudaMemsetAsync(layer->L.status, 0, 4, s);
+    cudaStreamSynchronize(s);
+    if (st == DEV_TIMEOUT) {
+        set_error("device wait timed out inside a C-TARQ kernel");
+        return SC_ETIMEOUT;
+    }
+    set_error("device recorded a bad index");
+    return SC_EDEVICE;
+}
+
+size_t sc_workspace_size(const sc_layer* layer, int64_t m) {
+    if (!layer || m < 0) return 0;
+    return plan_workspace(layer->L, m).total;
+}
+
+sc_status sc_forward_ws(const sc_layer* layer, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
+                        const float* bias, uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+    if (!layer) {
+        set_error("sc_forward: null layer");
+        return SC_EINVAL;
+    }
+    if (layer->L.shard_kind == SC_SHARD_ROWS) {
+        set_error("sc_forward: a ROWS shard produces partial sums; use sc_forward_partial");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(layer->L.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward: set device");
+    return forward_impl(layer->L, x, x_dtype, m, y, y_dtype, bias, mask_out, routed_idx_out, n_routed_out,
+                        workspace, workspace_bytes, static_cast<cudaStream_t>(stream), false);
+}
+
+sc_status sc_forward(const sc_layer* layer, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
+                     const float* bias, uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out,
+                     void* stream) {
+    if (!layer) {
+        set_error("sc_forward: null layer");
+        return SC_EINVAL;
+    }
+    if (m <= 0) return m == 0 ? SC_OK : (set_error("sc_forward: negative token count"), SC_EINVAL);
+    DeviceGuard guard(layer->L.device);
+    void* ws = nullptr;
+    const size_t need = plan_workspace(layer->L, m).total;
+    sc_status st = default_workspace(layer->L.device, need, &ws);
+    if (st != SC_OK) return st;
+    return sc_forward_ws(layer, x, x_dtype, m, y, y_dtype, bias, mask_out, routed_idx_out, n_routed_out, ws,
+                         need, stream);
+}
+
+sc_status sc_forward_partial(const sc_layer* layer, const void* x, int x_dtype, int64_t m, float* y_partial,
+                             uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (!layer) {
+        set_error("sc_forward_partial: null layer");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(layer->L.device);
+    void* ws = workspace;
+    size_t wsb = workspace_bytes;
+    if (!ws) {
+        wsb = plan_workspace(layer->L, m).total;
+        sc_status st = default_workspace(layer->L.device, wsb, &ws);
+        if (st != SC_OK) return st;
+    }
+    return forward_impl(layer->L, x, x_dtype, m, y_partial, SC_F32, nullptr, mask_out, routed_idx_out,
+                        n_routed_out, ws, wsb, static_cast<cudaStream_t>(stream), true);
+}
+
+sc_status sc_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
+                      void* stream) {
+    if (!acc || !y || m < 0 || n <= 0 || (y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32)) {
+        set_error("sc_finalize: bad argument");
+        return SC_EINVAL;
+    }
+    cudaError_t e = launch_finalize(acc, m, n, y, y_dtype, bias, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sc_finalize launch");
+    return SC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,109 @@
+// sc_internal.h -- host-side structures shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "saccade_ctarq.h"
+
+namespace sc {
+
+// Device status word codes (written with atomicCAS so the first error wins).
+enum : uint32_t { DEV_OK = 0, DEV_TIMEOUT = 1, DEV_BAD_INDEX = 2 };
+
+// Device layout of one C-TARQ layer (immutable after sc_layer_create).
+//
+//  wq      u32 [Np/16][KB][32][4]   fragment-tiled 4-bit base: for 16-row tile t and
+//                                   64-column block kb, lane L = 4g+c holds 4 words (ksteps
+//                                   s = 0..3); word s carries rows g, g+8 and columns
+//                                   64kb+16s+{2c,2c+1,2c+8,2c+9} (nibble map in sc_device.cuh).
+//                                   Padding rows/columns hold nibble 8 (q = 0).
+//  scale   f32 [Np]                 f16 row scale widened (config.rs:96-101); 0 on padding rows.
+//  rowptr  u32 [N+1], col u16 [nnz+8], val i8 [nnz+16]
+//                                   dW in CSR, columns ascending within a row (compress.rs:89-105).
+struct Layer {
+    int device = 0;
+    int sms = 148;               // multiprocessors of `device`
+    int mode = SC_MODE_FAST;
+    int64_t N = 0, K = 0;        // this shard's extent
+    int64_t Np = 0, Kp = 0;      // padded to 16 rows / 64 columns
+    int64_t KB = 0;              // Kp / 64
+    int64_t row_begin = 0, col_begin = 0, fullN = 0, fullK = 0;
+    int shard_kind = SC_SHARD_NONE;
+    int64_t nnz = 0;
+    float ds = 1.0f;             // dW scale widened from f16
+    float t4 = 0.0f, t8 = 0.0f;
+    uint32_t* wq = nullptr;
+    float* scale = nullptr;
+    uint32_t* rowptr = nullptr;
+    uint16_t* col = nullptr;
+    int8_t* val = nullptr;
+    uint32_t* status = nullptr;  // device status word
+    int64_t device_bytes = 0;
+};
+
+// Per-call workspace carve-up (offsets in bytes from the workspace base).
+struct WsLayout {
+    int64_t Mp = 0;              // tokens padded to 8
+    size_t xk = 0, mask = 0, scores = 0, ridx = 0, nrouted = 0, counter = 0;
+    size_t partial = 0, rtcount = 0;
+    size_t total = 0;
+    int ksplit = 1;
+    int chunk_tokens = 0;        // tokens per decode launch
+};
+
+WsLayout plan_workspace(const Layer& L, int64_t m);
+
+void set_error(const std::string& msg);
+sc_status cuda_fail(cudaError_t e, const char* what);
+
+// Kernel launchers (each returns the launch error, if any).
+cudaError_t launch_repack(const uint32_t* packed, int64_t ref_words_per_row, int64_t row0, int64_t word0,
+                          const Layer& L, cudaStream_t s);
+cudaError_t launch_scales(const uint16_t* scale_f16, int64_t row0, const Layer& L, cudaStream_t s);
+
+struct RouterArgs {
+    const void* x;
+    int x_dtype;
+    int64_t x_row_stride;   // elements between consecutive tokens of x
+    int64_t x_col0;         // first column of x used (0)
+    int64_t M, K, Mp, KB;
+    float t4, t8;
+    int route_all;          // bypass: every token takes dW
+    uint16_t* xk;           // [KB][Mp][64] f16 bits (swizzled)
+    uint8_t* mask;
+    float* scores;
+    int32_t* ridx;
+    int32_t* nrouted;
+    uint32_t* counter;
+    uint32_t* status;
+};
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t s);
+
+struct DecodeArgs {
+    const Layer* L;
+    const uint16_t* xk;
+    int64_t Mp;             // token stride of xk
+    int64_t tok0, ntok;     // token range of this launch
+    const uint8_t* mask;
+    const int32_t* ridx;
+    const int32_t* nrouted;
+    int route_all;
+    int64_t dcol_begin, dcol_end;   // dW columns applied (shard range, relative to L)
+    void* y;                // [M, N] rows tok0..tok0+ntok; or f32 partial when partial_out
+    int y_dtype;
+    const float* bias;
+    int partial_out;        // 1: write f32 accumulators (no f16 rounding)
+    float* ws_partial;
+    uint32_t* ws_rtcount;
+    int ksplit;
+};
+cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
+cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s);
+
+cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
+                            cudaStream_t s);
+
+}  // namespace sc

@@ -1,0 +1,244 @@
+// sc_router.cu -- per-token variance router (heuristics.rs:3-14, op.rs:64-73).
+//
+// One CTA per token.  The CTA widens the token to f16 (bf16 inputs are rounded to f16,
+// as the caller's to_dtype(F16) does at model.rs:58-61), stores it into the staged
+// activation layout xk used by the GEMV, and reduces sum(x), sum(x^2) and sum(|x|) in
+// f64 with warp shuffles.
+//
+// The reference decides on an f32 variance summed sequentially over k.  The f64 sums
+// are (to ~1e-16) the exact sums, and the standard bound on sequential f32 summation
+// (|fl(sum) - sum| <= gamma_{k-1} * sum|terms|, gamma_n = n*u/(1-n*u), u = 2^-24)
+// bounds how far the reference's f32 score can lie from the f64 one.  When both
+// thresholds are farther than that bound the decision is the reference's; otherwise
+// one thread replays the reference's exact sequential f32 chain for that token.  The
+// mask therefore equals the reference's mask for every token, at the cost of a serial
+// pass only for tokens sitting on a threshold.
+//
+// The last CTA to finish (completion counter in the workspace) compacts the mask into
+// the ascending routed-token list and resets the counter for the next call.
+#include "sc_device.cuh"
+#include "sc_internal.h"
+
+namespace sc {
+
+__device__ __forceinline__ bool route_rule_f32(float score, float t4, float t8) {
+    // op.rs:69-72: (score >= t4 && score < t8) || score >= t8; both flags select the dW.
+    return (score >= t4 && score < t8) || (score >= t8);
+}
+
+__device__ __forceinline__ bool route_rule_f64(double score, float t4, float t8) {
+    const double a = t4, b = t8;
+    return (score >= a && score < b) || (score >= b);
+}
+
+// Replays heuristics.rs:3-14 exactly: f16 -> f32, sequential f32 sums, f32 divide.
+__device__ float exact_variance(const void* x, int x_dtype, int64_t row_off, int64_t Kfull) {
+    float sum = 0.0f, sq = 0.0f;
+    for (int64_t i = 0; i < Kfull; ++i) {
+        float v;
+        if (x_dtype == SC_BF16) {
+            const __nv_bfloat16 b = reinterpret_cast<const __nv_bfloat16*>(x)[row_off + i];
+            v = __half2float(__float2half_rn(__bfloat162float(b)));
+        } else {
+            v = __half2float(reinterpret_cast<const __half*>(x)[row_off + i]);
+        }
+        sum = __fadd_rn(sum, v);
+        sq = __fadd_rn(sq, __fmul_rn(v, v));
+    }
+    const float hd = static_cast<float>(Kfull);
+    const float mean = __fdiv_rn(sum, hd);
+    return __fsub_rn(__fdiv_rn(sq, hd), __fmul_rn(mean, mean));
+}
+
+struct RouterKernelArgs {
+    const void* x;
+    int x_dtype;
+    int vec_ok;             // x rows 16-byte aligned: load 8 elements at a time
+    int64_t row_stride;
+    int64_t Kfull;          // elements per token used for the score
+    int64_t col0;           // first column staged into xk (multiple of 64)
+    int64_t K;              // columns staged into xk
+    int64_t M, Mp, KB;
+    float t4, t8;
+    int route_all;
+    uint16_t* xk;
+    uint8_t* mask;
+    float* scores;
+    int32_t* ridx;
+    int32_t* nrouted;
+    uint32_t* counter;
+    uint32_t* status;
+};
+
+template <int kThreads>
+__global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
+    constexpr int kWarps = kThreads / 32;
+    __shared__ double red[3][kWarps];
+    __shared__ int s_last;
+    __shared__ int s_wsum[kWarps];
+    const int64_t t = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5;
+
+    if (t >= a.M) {
+        // padding tokens of the last 8-token group: zero rows in xk
+        for (int64_t ch = tid; ch < a.KB * 8; ch += kThreads) {
+            const int64_t kb = ch >> 3;
+            *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + (ch & 7) * 8]) = make_uint4(0, 0, 0, 0);
+        }
+    } else {
+        double s1 = 0.0, s2 = 0.0, sa = 0.0;
+        const int64_t row_off = t * a.row_stride;
+        const int64_t nch = a.Kfull / 8;
+        const int64_t ch_lo = a.col0 / 8, ch_hi = (a.col0 + a.K) / 8;
+        for (int64_t ch = tid; ch < nch; ch += kThreads) {
+            uint16_t h[8];
+            if (a.x_dtype == SC_BF16) {
+                const __nv_bfloat16* xs = reinterpret_cast<const __nv_bfloat16*>(a.x) + row_off + ch * 8;
+                __nv_bfloat16 b[8];
+                if (a.vec_ok) {
+                    *reinterpret_cast<uint4*>(b) = __ldg(reinterpret_cast<const uint4*>(xs));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) b[j] = xs[j];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) h[j] = f32_to_f16_bits(__bfloat162float(b[j]));
+            } else {
+                const uint16_t* xs = reinterpret_cast<const uint16_t*>(a.x) + row_off + ch * 8;
+                if (a.vec_ok) {
+                    *reinterpret_cast<uint4*>(h) = __ldg(reinterpret_cast<const uint4*>(xs));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) h[j] = xs[j];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const double v = static_cast<double>(h2f(h[j]));
+                s1 += v;
+                s2 += v * v;
+                sa += fabs(v);
+            }
+            if (ch >= ch_lo && ch < ch_hi) {
+                const int64_t lc = ch - ch_lo;
+                const int64_t kb = lc >> 3;
+                const int chunk = static_cast<int>(lc & 7) ^ static_cast<int>(t & 7);
+                *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + chunk * 8]) =
+                    *reinterpret_cast<const uint4*>(h);
+            }
+        }
+        // zero the padding columns of the staged slice
+        for (int64_t lc = (a.K / 8) + tid; lc < a.KB * 8; lc += kThreads) {
+            const int64_t kb = lc >> 3;
+            const int chunk = static_cast<int>(lc & 7) ^ static_cast<int>(t & 7);
+            *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + chunk * 8]) = make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s1 += __shfl_down_sync(0xffffffffu, s1, o);
+            s2 += __shfl_down_sync(0xffffffffu, s2, o);
+            sa += __shfl_down_sync(0xffffffffu, sa, o);
+        }
+        if (lane == 0) {
+            red[0][warp] = s1;
+            red[1][warp] = s2;
+            red[2][warp] = sa;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            double S1 = 0.0, S2 = 0.0, SA = 0.0;
+            for (int w = 0; w < kWarps; ++w) {
+                S1 += red[0][w];
+                S2 += red[1][w];
+                SA += red[2][w];
+            }
+            const double n = static_cast<double>(a.Kfull);
+            const double u = 5.9604644775390625e-08;  // 2^-24
+            const double nu = (n - 1.0) * u;
+            const double gam = nu / (1.0 - nu);
+            const double E1 = gam * SA, E2 = gam * S2;
+            const double mean = S1 / n, A = S2 / n;
+            const double errMean = E1 / n + u * (fabs(S1) + E1) / n;
+            const double errA = E2 / n + u * (S2 + E2) / n;
+            const double errSq = errMean * (2.0 * fabs(mean) + errMean) + u * (fabs(mean) + errMean) * (fabs(mean) + errMean);
+            const double var = A - mean * mean;
+            double B = errA + errSq + u * (fabs(var) + errA + errSq);
+            B = 2.0 * B + 1e-37;
+            const double d4 = fabs(var - static_cast<double>(a.t4));
+            const double d8 = fabs(var - static_cast<double>(a.t8));
+            const bool finite = isfinite(var) && isfinite(B);
+            bool routed;
+            float score;
+            if (finite && !(d4 <= B) && !(d8 <= B)) {
+                routed = route_rule_f64(var, a.t4, a.t8);
+                score = static_cast<float>(var);
+            } else {
+                score = exact_variance(a.x, a.x_dtype, row_off, a.Kfull);
+                routed = route_rule_f32(score, a.t4, a.t8);
+            }
+            if (a.route_all) routed = true;
+            a.mask[t] = routed ? 1 : 0;
+            if (a.scores) a.scores[t] = score;
+        }
+    }
+
+    // completion count; the last CTA compacts the mask
+    if (tid == 0) {
+        __threadfence();
+        const unsigned ticket = atomicAdd(a.counter, 1u);
+        s_last = (ticket == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    int base = 0;
+    for (int64_t t0 = 0; t0 < a.M; t0 += kThreads) {
+        const int64_t tt = t0 + tid;
+        const int v = (tt < a.M) ? (reinterpret_cast<volatile uint8_t*>(a.mask)[tt] != 0) : 0;
+        const unsigned bal = __ballot_sync(0xffffffffu, v);
+        if (lane == 0) s_wsum[warp] = __popc(bal);
+        __syncthreads();
+        int pre = 0, tot = 0;
+        for (int w = 0; w < kWarps; ++w) {
+            if (w < warp) pre += s_wsum[w];
+            tot += s_wsum[w];
+        }
+        pre += __popc(bal & ((1u << lane) - 1u));
+        if (v) a.ridx[base + pre] = static_cast<int32_t>(tt);
+        base += tot;
+        __syncthreads();
+    }
+    if (tid == 0) {
+        *a.nrouted = base;
+        *a.counter = 0u;
+    }
+}
+
+cudaError_t launch_router(const RouterArgs& r, cudaStream_t s) {
+    RouterKernelArgs a;
+    a.x = r.x;
+    a.x_dtype = r.x_dtype;
+    a.row_stride = r.x_row_stride;
+    a.vec_ok = ((reinterpret_cast<uintptr_t>(r.x) & 15u) == 0 && (r.x_row_stride % 8) == 0) ? 1 : 0;
+    a.Kfull = r.x_row_stride;
+    a.col0 = r.x_col0;
+    a.K = r.K;
+    a.M = r.M;
+    a.Mp = r.Mp;
+    a.KB = r.KB;
+    a.t4 = r.t4;
+    a.t8 = r.t8;
+    a.route_all = r.route_all;
+    a.xk = r.xk;
+    a.mask = r.mask;
+    a.scores = r.scores;
+    a.ridx = r.ridx;
+    a.nrouted = r.nrouted;
+    a.counter = r.counter;
+    a.status = r.status;
+    k_router<256><<<static_cast<unsigned>(r.Mp), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace sc

@@ -1,0 +1,18 @@
+"""saccade_core: the C-TARQ linear on NVIDIA B200, with saccade-core's operator surface.
+
+Compute runs only in libsaccade_ctarq.so (hand-written sm_100a kernels, C ABI in
+include/saccade_ctarq.h); this package is the host-side mirror of the reference's
+names (saccade-core/src/lib.rs:9-12).
+"""
+from ._lib import CTarqError, LIB_PATH
+from .graph import CapturedStep
+from .compress import (ProfileRunner, compress_tensor_to_saccade, compute_percentile_threshold,
+                       saccade_op_from_compressed)
+from .op import (SaccadeConfig, SaccadeLinearOp, SparseDeltaMatrix, finalize, is_c_tarq_bypassed,
+                 set_bypass_c_tarq, variance_heuristic)
+
+__all__ = [
+    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearOp", "SparseDeltaMatrix",
+    "compress_tensor_to_saccade", "compute_percentile_threshold", "finalize", "is_c_tarq_bypassed",
+    "saccade_op_from_compressed", "set_bypass_c_tarq", "variance_heuristic",
+]

@@ -1,0 +1,279 @@
+"""SaccadeLinearOp: the C-TARQ linear on a B200, mirroring saccade-core's operator.
+
+    SaccadeConfig        config.rs:19-24
+    SparseDeltaMatrix    config.rs:28-33
+    SaccadeLinearOp      config.rs:60-150 (construction), op.rs:5-185 (name, forward)
+    set_bypass_c_tarq / is_c_tarq_bypassed   config.rs:4-12
+
+Construction copies the reference-format buffers to the device layout through
+sc_layer_create; forward() runs sc_forward_ws on the current CUDA stream with a
+per-(device, stream) workspace that is zero-filled once and reused.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import LIB, check
+
+_DT = {torch.float16: _lib.SC_F16, torch.bfloat16: _lib.SC_BF16, torch.float32: _lib.SC_F32}
+
+
+def set_bypass_c_tarq(val: bool) -> None:
+    """config.rs:6-8: global switch to the dense base+dW product for every token."""
+    LIB.sc_set_bypass_c_tarq(1 if val else 0)
+
+
+def is_c_tarq_bypassed() -> bool:
+    """config.rs:10-12."""
+    return bool(LIB.sc_is_c_tarq_bypassed())
+
+
+@dataclass
+class SaccadeConfig:
+    """config.rs:19-24.  `block_size` is carried for surface compatibility (unused by the
+    reference too); the heuristic is the variance heuristic (heuristics.rs:3-14)."""
+    t4: float
+    t8: float
+    block_size: int = 16
+    heuristic: str = "variance"
+
+
+@dataclass
+class SparseDeltaMatrix:
+    """config.rs:28-33: CSR dW (u32 row_ptrs [N+1], u32 col_indices [nnz], u8 values
+    holding i8 bits [nnz], f16 scale [1])."""
+    row_ptrs: torch.Tensor
+    col_indices: torch.Tensor
+    values: torch.Tensor
+    scale: torch.Tensor
+
+
+def _f16_bits(t: torch.Tensor) -> int:
+    return int(t.reshape(-1)[:1].to(torch.float16).view(torch.int16).item()) & 0xFFFF
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class _Workspaces:
+    """Zero-filled workspaces keyed by (device, stream); grown on demand."""
+
+    def __init__(self):
+        self._ws = {}
+
+    def get(self, device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
+        key = (device.index, stream.cuda_stream)
+        ws = self._ws.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+
+WORKSPACES = _Workspaces()
+
+
+def _u32(t: torch.Tensor) -> torch.Tensor:
+    """Reinterpret a u32/i32/i64 index tensor as contiguous 32-bit words."""
+    if t.dtype in (torch.int64, torch.long):
+        t = t.to(torch.int32)
+    if t.dtype == torch.uint32:
+        t = t.view(torch.int32)
+    return t.contiguous()
+
+
+class SaccadeLinearOp:
+    """One C-TARQ linear layer resident on a B200.
+
+    packed_base u32 [N, K/8] (8 nibbles of q+8 per word along K, compress.rs:54-83),
+    scale_base f16 [N], optional SparseDeltaMatrix, SaccadeConfig thresholds.
+    mode "fast" (tensor cores, default) or "exact" (op.rs's f32 order, bit-identical).
+    shard=("columns"|"rows", index, count) keeps a tensor-parallel slice.
+    """
+
+    NAME = "fused_c_tarq_saccade_linear"
+
+    def __init__(self, packed_base: torch.Tensor, scale_base: torch.Tensor,
+                 sparse_delta_q8: Optional[SparseDeltaMatrix], config: SaccadeConfig,
+                 out_features: int, in_features: int, *, device=None, mode: str = "fast",
+                 shard: Optional[tuple] = None):
+        if device is None:
+            device = packed_base.device if packed_base.is_cuda else torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("SaccadeLinearOp runs on a CUDA device only")
+        dev_index = device.index if device.index is not None else torch.cuda.current_device()
+        self.device = torch.device("cuda", dev_index)
+        self.config = config
+        self.full_out_features = int(out_features)
+        self.full_in_features = int(in_features)
+        on_dev = packed_base.is_cuda
+        keep = []  # keep temporaries alive across the create call
+
+        def prep(t, dtype=None):
+            if t is None:
+                return None
+            t = t.contiguous()
+            if on_dev and not t.is_cuda:
+                t = t.to(self.device)
+            if not on_dev and t.is_cuda:
+                t = t.cpu()
+            keep.append(t)
+            return t
+
+        pb = prep(_u32(packed_base))
+        sb = prep(scale_base.to(torch.float16) if scale_base.dtype != torch.float16 else scale_base)
+        d = _lib.ScLayerDesc()
+        d.out_features = int(out_features)
+        d.in_features = int(in_features)
+        if pb.numel() != out_features * (in_features // 8) or in_features % 8:
+            raise ValueError("packed_base must be [out_features, in_features/8] with in_features % 8 == 0")
+        d.packed_base = pb.data_ptr()
+        d.scale_base = sb.data_ptr()
+        if sparse_delta_q8 is not None and sparse_delta_q8.values.numel() > 0:
+            rp = prep(_u32(sparse_delta_q8.row_ptrs))
+            ci = prep(_u32(sparse_delta_q8.col_indices))
+            vals = sparse_delta_q8.values
+            if vals.dtype == torch.int8:
+                vals = vals.view(torch.uint8)
+            cv = prep(vals.to(torch.uint8) if vals.dtype != torch.uint8 else vals)
+            d.delta_row_ptrs = rp.data_ptr()
+            d.delta_col_indices = ci.data_ptr()
+            d.delta_values = cv.data_ptr()
+            d.delta_nnz = cv.numel()
+            d.delta_scale = _f16_bits(sparse_delta_q8.scale)
+        d.t4 = float(config.t4)
+        d.t8 = float(config.t8)
+        d.device = dev_index
+        d.buffers_on_device = 1 if on_dev else 0
+        d.mode = _lib.SC_MODE_EXACT if mode == "exact" else _lib.SC_MODE_FAST
+        if shard is not None:
+            kind, idx, cnt = shard
+            d.shard_kind = {"columns": _lib.SC_SHARD_COLUMNS, "rows": _lib.SC_SHARD_ROWS}[kind]
+            d.shard_index, d.shard_count = int(idx), int(cnt)
+        if on_dev:
+            torch.cuda.synchronize(self.device)
+        h = ctypes.c_void_p()
+        check(LIB.sc_layer_create(ctypes.byref(d), ctypes.byref(h)))
+        self._h = h
+        info = _lib.ScLayerInfo()
+        check(LIB.sc_layer_get_info(self._h, ctypes.byref(info)))
+        self.info = info
+        self.out_features = int(info.out_features)
+        self.in_features = int(info.in_features)
+        self.shard_kind = shard[0] if shard else None
+        self.mode = mode
+
+    # ------------------------------------------------------------------ surface of op.rs
+    def name(self) -> str:
+        return LIB.sc_op_name().decode()
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            LIB.sc_layer_destroy(h)
+            self._h = None
+
+    @property
+    def delta_nnz(self) -> int:
+        return int(self.info.delta_nnz)
+
+    def set_thresholds(self, t4: float, t8: float) -> None:
+        check(LIB.sc_layer_set_thresholds(self._h, float(t4), float(t8)))
+        self.config.t4, self.config.t8 = float(t4), float(t8)
+        LIB.sc_layer_get_info(self._h, ctypes.byref(self.info))
+
+    def set_mode(self, mode: str) -> None:
+        check(LIB.sc_layer_set_mode(self._h, _lib.SC_MODE_EXACT if mode == "exact" else _lib.SC_MODE_FAST))
+        self.mode = mode
+
+    def check_device(self) -> None:
+        """Raise if a kernel recorded a device-side error (bounded wait ran out, bad index)."""
+        check(LIB.sc_layer_check(self._h, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+
+    def workspace_size(self, m: int) -> int:
+        return int(LIB.sc_workspace_size(self._h, int(m)))
+
+    def _prep_x(self, x: torch.Tensor, k: int):
+        if not x.is_cuda or x.device != self.device:
+            raise ValueError(f"input must be on {self.device}")
+        if x.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("input dtype must be float16 or bfloat16 (op.rs:19 reads f16)")
+        if x.shape[-1] != k:
+            raise ValueError(f"last dimension {x.shape[-1]} != in_features {k}")
+        if not x.is_contiguous():
+            raise ValueError("input must be contiguous (op.rs:19-24 ignores strides)")
+        m = x.numel() // k if k else 0
+        return m
+
+    def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16,
+                bias: Optional[torch.Tensor] = None, return_routing: bool = False):
+        """op.rs:10-185.  x [..., K] f16/bf16 on this device -> y [..., N] (f16 by default).
+        bias (f32 [N]) is added after the f16 rounding; out_dtype f32/bf16 widens/rounds after."""
+        if self.shard_kind == "rows":
+            raise ValueError("a rows shard yields partial sums: use forward_partial + all-reduce + finalize")
+        m = self._prep_x(x, self.in_features)
+        y = torch.empty(x.shape[:-1] + (self.out_features,), dtype=out_dtype, device=self.device)
+        mask = torch.empty(m, dtype=torch.uint8, device=self.device) if return_routing else None
+        ridx = torch.empty(max(m, 1), dtype=torch.int32, device=self.device) if return_routing else None
+        nr = torch.zeros(1, dtype=torch.int32, device=self.device) if return_routing else None
+        if bias is not None:
+            bias = bias.to(device=self.device, dtype=torch.float32).contiguous()
+        if m > 0:
+            stream = torch.cuda.current_stream(self.device)
+            need = self.workspace_size(m)
+            ws = WORKSPACES.get(self.device, stream, need)
+            check(LIB.sc_forward_ws(self._h, x.data_ptr(), _DT[x.dtype], m, y.data_ptr(), _DT[out_dtype],
+                                    _ptr(bias), _ptr(mask), _ptr(ridx), _ptr(nr), ws.data_ptr(), ws.numel(),
+                                    ctypes.c_void_p(stream.cuda_stream)))
+        if return_routing:
+            return y, mask, ridx, nr
+        return y
+
+    __call__ = forward
+
+    def forward_partial(self, x_full: torch.Tensor, *, return_routing: bool = False):
+        """For tensor parallelism: f32 contribution [..., N] of this shard (rows shard: the input
+        is the whole [..., full_K] token), before the cross-shard sum and the f16 rounding."""
+        m = self._prep_x(x_full, self.full_in_features if self.shard_kind == "rows" else self.in_features)
+        y = torch.empty(x_full.shape[:-1] + (self.out_features,), dtype=torch.float32, device=self.device)
+        mask = torch.empty(m, dtype=torch.uint8, device=self.device) if return_routing else None
+        if m > 0:
+            stream = torch.cuda.current_stream(self.device)
+            need = self.workspace_size(m)
+            ws = WORKSPACES.get(self.device, stream, need)
+            check(LIB.sc_forward_partial(self._h, x_full.data_ptr(), _DT[x_full.dtype], m, y.data_ptr(),
+                                         _ptr(mask), None, None, ws.data_ptr(), ws.numel(),
+                                         ctypes.c_void_p(stream.cuda_stream)))
+        return (y, mask) if return_routing else y
+
+
+def finalize(acc: torch.Tensor, *, out_dtype=torch.float16, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """f32 accumulators [..., N] -> f16 rounding (op.rs:172-178), then bias/out dtype."""
+    acc = acc.contiguous()
+    n = acc.shape[-1]
+    m = acc.numel() // n
+    y = torch.empty(acc.shape, dtype=out_dtype, device=acc.device)
+    if bias is not None:
+        bias = bias.to(device=acc.device, dtype=torch.float32).contiguous()
+    check(LIB.sc_finalize(acc.data_ptr(), m, n, y.data_ptr(), _DT[out_dtype], _ptr(bias),
+                          ctypes.c_void_p(torch.cuda.current_stream(acc.device).cuda_stream)))
+    return y
+
+
+def variance_heuristic(x: torch.Tensor) -> torch.Tensor:
+    """heuristics.rs:3-14 per token of x [..., K] (f16/bf16/f32 on CUDA), in the reference's
+    exact sequential f32 order.  Returns f32 [...]."""
+    k = x.shape[-1]
+    x = x.contiguous()
+    m = x.numel() // k
+    out = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    check(LIB.sc_variance_heuristic(x.data_ptr(), _DT[x.dtype], m, k, out.data_ptr(),
+                                    ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)))
+    return out

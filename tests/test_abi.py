@@ -1,0 +1,68 @@
+"""CPU checks of the C-ABI library: it loads without a GPU, exports exactly the entry
+points include/saccade_ctarq.h declares, and its host-only calls behave."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "saccade_ctarq.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^SC_API\s+[\w\s\*]+?\b(sc_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for must in ("sc_layer_create", "sc_forward", "sc_forward_ws", "sc_op_name", "sc_compress", "sc_calibrate"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from saccade_core import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert set(declared_symbols()) == set(_lib.SIGNATURES), "ctypes signatures must cover the header exactly"
+
+
+def test_only_c_abi_is_exported():
+    from saccade_core import _lib
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True, check=True)
+    funcs = [ln.split()[-1] for ln in out.stdout.splitlines() if " T " in ln]
+    assert funcs and all(f.startswith("sc_") for f in funcs), [f for f in funcs if not f.startswith("sc_")][:10]
+
+
+def test_host_only_calls():
+    from saccade_core import _lib
+    L = _lib.LIB
+    assert L.sc_op_name() == b"fused_c_tarq_saccade_linear"
+    assert L.sc_abi_version() == 1
+    L.sc_set_bypass_c_tarq(1)
+    assert L.sc_is_c_tarq_bypassed() == 1
+    L.sc_set_bypass_c_tarq(0)
+    assert L.sc_is_c_tarq_bypassed() == 0
+
+
+def test_invalid_arguments_fail_before_touching_a_device():
+    from saccade_core import _lib
+    L = _lib.LIB
+    d = _lib.ScLayerDesc()
+    d.out_features, d.in_features = 4, 12  # K % 8 != 0
+    h = ctypes.c_void_p()
+    assert L.sc_layer_create(ctypes.byref(d), ctypes.byref(h)) == _lib.SC_EINVAL
+    assert "multiple of 8" in _lib.last_error()
+    assert L.sc_layer_create(None, ctypes.byref(h)) == _lib.SC_EINVAL
+    assert L.sc_forward(None, None, 0, 1, None, 0, None, None, None, None, None) == _lib.SC_EINVAL
+    assert L.sc_finalize(None, 1, 1, None, 0, None, None) == _lib.SC_EINVAL
+    assert L.sc_workspace_size(None, 4) == 0
+
+
+def test_error_type_is_raised():
+    from saccade_core import _lib
+    with pytest.raises(_lib.CTarqError):
+        _lib.check(_lib.SC_EINVAL)

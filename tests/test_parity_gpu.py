@@ -1,0 +1,322 @@
+"""GPU parity of the CUDA library against the oracle, through the C ABI (ctypes).
+
+Exact mode must be bit-identical to the oracle; the fast (tensor-core) mode must keep
+router masks identical and outputs within the tolerance of ctarq_cases.TOL_REL_RMS.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import oracle as O
+from ctarq_cases import assert_acc_close, assert_fast_close, make_case
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def sc():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import saccade_core
+    return saccade_core
+
+
+def to_op(sc, case, mode="fast", on_device=True, shard=None):
+    c = case.c
+    dev = torch.device("cuda", 0)
+
+    def t(a, dt):
+        x = torch.from_numpy(np.ascontiguousarray(a).view(dt))
+        return x.to(dev) if on_device else x
+
+    sp = None
+    if c.nnz:
+        sp = sc.SparseDeltaMatrix(t(c.delta_row_ptrs, np.int32), t(c.delta_col_indices, np.int32),
+                                  t(c.delta_values, np.uint8),
+                                  torch.tensor([c.delta_scale], dtype=torch.int16).view(torch.float16))
+    return sc.SaccadeLinearOp(t(c.packed_base, np.int32), t(c.scale_base, np.float16), sp,
+                              sc.SaccadeConfig(case.t4, case.t8), case.n, case.k, device=dev, mode=mode,
+                              shard=shard)
+
+
+def run_gpu(op, x_bits, dtype=torch.float16, **kw):
+    x = torch.from_numpy(x_bits.view(np.float16)).to("cuda:0")
+    if dtype == torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    y, mask, ridx, nr = op.forward(x, return_routing=True, **kw)
+    torch.cuda.synchronize()
+    op.check_device()
+    return y, mask.cpu().numpy(), ridx.cpu().numpy()[: int(nr.item())]
+
+
+def y_bits(y):
+    return y.cpu().numpy().view(np.uint16)
+
+
+SHAPES = [
+    # n, k, m, fill
+    (4864, 896, 16, 0.01),     # the single-layer configuration (4864x896, 16 tokens, 1 % dW)
+    (40, 64, 5, 0.05),
+    (33, 136, 9, 0.1),          # ragged rows and a K that is not a multiple of 64
+    (130, 200, 1, 0.02),
+    (256, 8, 3, 0.3),           # K = 8: one packed word per row
+    (512, 3584, 2, 0.01),       # k/v projection shape
+    (1000, 512, 17, 0.04),
+    (96, 256, 33, 0.01),
+    (300, 1024, 64, 0.01),
+    (64, 384, 100, 0.02),
+]
+
+
+@pytest.mark.parametrize("n,k,m,fill", SHAPES)
+def test_exact_mode_bit_identical(sc, n, k, m, fill):
+    case = make_case(n, k, m, fill, seed=n + k + m)
+    op = to_op(sc, case, mode="exact")
+    y, mask, ridx = run_gpu(op, case.x_bits)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    assert np.array_equal(mask, rr)
+    assert np.array_equal(ridx, np.nonzero(rr)[0])
+    assert np.array_equal(y_bits(y), yr), "exact mode must reproduce op.rs bit for bit"
+
+
+@pytest.mark.parametrize("n,k,m,fill", SHAPES)
+def test_fast_mode_within_tolerance(sc, n, k, m, fill):
+    case = make_case(n, k, m, fill, seed=n * 3 + k + m)
+    op = to_op(sc, case, mode="fast")
+    y, mask, ridx = run_gpu(op, case.x_bits)
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    assert np.array_equal(mask, rr), "router mask must equal the reference's"
+    assert np.array_equal(ridx, np.nonzero(rr)[0])
+    assert_fast_close(y_bits(y), yr, f"fast {n}x{k} m={m}")
+    acc = op.forward_partial(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")).cpu().numpy()
+    assert_acc_close(acc, acc_ref, f"fast acc {n}x{k} m={m}")
+
+
+def test_threshold_token_exactly_on_t4(sc):
+    # calibrate() puts t4 exactly on one token's score; the router must reproduce the
+    # reference's f32 decision for it (score >= t4 -> routed).
+    case = make_case(4864, 896, 16, 0.01, seed=42, boost=[1, 6, 9, 14])
+    scores = [O.variance(case.x_bits[t]) for t in range(16)]
+    assert case.t4 in scores
+    for mode in ("fast", "exact"):
+        op = to_op(sc, case, mode=mode)
+        _, mask, _ = run_gpu(op, case.x_bits)
+        _, rr, _ = case.oracle().forward(case.x_bits)
+        assert np.array_equal(mask, rr)
+        assert mask[scores.index(case.t4)] == 1
+
+
+def test_bf16_input(sc):
+    case = make_case(700, 448, 6, 0.02, seed=9)
+    xf = case.x_bits.view(np.float16).astype(np.float32)
+    xbf = torch.from_numpy(xf).to(torch.bfloat16)
+    bf_bits = xbf.view(torch.int16).numpy().view(np.uint16)
+    x16 = O.bf16_bits_to_f16_bits(bf_bits)
+    for mode in ("exact", "fast"):
+        op = to_op(sc, case, mode=mode)
+        y, mask, _ = op.forward(xbf.to("cuda:0"), return_routing=True)[:3]
+        yr, rr, _ = case.oracle().forward(x16)
+        assert np.array_equal(mask.cpu().numpy(), rr)
+        if mode == "exact":
+            assert np.array_equal(y_bits(y), yr)
+        else:
+            assert_fast_close(y_bits(y), yr, "bf16 fast")
+
+
+@pytest.mark.parametrize("out_dtype", ["f16", "f32", "bf16"])
+def test_bias_and_output_dtype(sc, out_dtype):
+    case = make_case(200, 320, 4, 0.02, seed=5)
+    rng = np.random.default_rng(1)
+    b = (rng.standard_normal(200) * 0.01).astype(np.float32)
+    op = to_op(sc, case, mode="exact")
+    dt = {"f16": torch.float16, "f32": torch.float32, "bf16": torch.bfloat16}[out_dtype]
+    x = torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")
+    y = op.forward(x, out_dtype=dt, bias=torch.from_numpy(b)).float().cpu().numpy()
+    yr, _, _ = case.oracle().forward(case.x_bits)
+    ref = torch.from_numpy((yr.view(np.float16).astype(np.float32) + b).astype(np.float32)).to(dt).float().numpy()
+    assert np.array_equal(y, ref)
+
+
+def test_no_delta_and_dense_delta(sc):
+    for fill, thr_case in ((None, "none"), (1.0, "dense")):
+        case = make_case(96, 128, 5, fill, seed=11)
+        if thr_case == "none":
+            assert case.c.nnz == 0
+        for mode in ("exact", "fast"):
+            op = to_op(sc, case, mode=mode)
+            y, mask, _ = run_gpu(op, case.x_bits)
+            yr, rr, _ = case.oracle().forward(case.x_bits)
+            assert np.array_equal(mask, rr)
+            if mode == "exact":
+                assert np.array_equal(y_bits(y), yr)
+            else:
+                assert_fast_close(y_bits(y), yr, f"{thr_case} fast")
+
+
+def test_forced_routes_and_t8_below_t4(sc):
+    base = make_case(160, 192, 8, 0.05, seed=21)
+    for t4, t8 in ((3.0e38, 3.0e38), (-1e30, -1e30), (2.0, 0.5), (0.5, 2.0)):
+        base.t4, base.t8 = t4, t8
+        op = to_op(sc, base, mode="exact")
+        y, mask, _ = run_gpu(op, base.x_bits)
+        yr, rr, _ = base.oracle().forward(base.x_bits)
+        assert np.array_equal(mask, rr), (t4, t8)
+        assert np.array_equal(y_bits(y), yr), (t4, t8)
+
+
+def test_bypass(sc):
+    case = make_case(128, 256, 4, 0.05, seed=3)
+    try:
+        sc.set_bypass_c_tarq(True)
+        for mode in ("exact", "fast"):
+            op = to_op(sc, case, mode=mode)
+            y, mask, _ = run_gpu(op, case.x_bits)
+            yr, _, _ = case.oracle().forward(case.x_bits, bypass=True)
+            assert mask.all()
+            if mode == "exact":
+                assert np.array_equal(y_bits(y), yr), "exact bypass must match op.rs:30-58"
+            else:
+                assert_fast_close(y_bits(y), yr, "bypass fast")
+    finally:
+        sc.set_bypass_c_tarq(False)
+
+
+def test_host_buffers_and_empty_batch(sc):
+    case = make_case(64, 64, 3, 0.05, seed=4)
+    op = to_op(sc, case, mode="exact", on_device=False)
+    y, mask, _ = run_gpu(op, case.x_bits)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    assert np.array_equal(y_bits(y), yr) and np.array_equal(mask, rr)
+    y0 = op.forward(torch.empty((0, 64), dtype=torch.float16, device="cuda:0"))
+    assert y0.shape == (0, 64)
+
+
+def test_rejects_bad_inputs(sc):
+    case = make_case(32, 64, 2, 0.05, seed=6)
+    op = to_op(sc, case)
+    with pytest.raises(ValueError):
+        op.forward(torch.zeros((2, 63), dtype=torch.float16, device="cuda:0"))
+    with pytest.raises(ValueError):
+        op.forward(torch.zeros((2, 64), dtype=torch.float32, device="cuda:0"))
+    with pytest.raises(ValueError):
+        op.forward(torch.zeros((64, 2), dtype=torch.float16, device="cuda:0").t())
+    bad = case.c.delta_col_indices.copy()
+    if bad.size:
+        bad[0] = 64
+        with pytest.raises(sc.CTarqError):
+            sc.SaccadeLinearOp(torch.from_numpy(case.c.packed_base.view(np.int32)),
+                               torch.from_numpy(case.c.scale_base.view(np.float16)),
+                               sc.SparseDeltaMatrix(torch.from_numpy(case.c.delta_row_ptrs.view(np.int32)),
+                                                    torch.from_numpy(bad.view(np.int32)),
+                                                    torch.from_numpy(case.c.delta_values),
+                                                    torch.tensor([case.c.delta_scale], dtype=torch.int16).view(
+                                                        torch.float16)),
+                               sc.SaccadeConfig(0.0, 1.0), 32, 64, device="cuda:0")
+
+
+def test_repeated_calls_reuse_workspace(sc):
+    case = make_case(384, 640, 12, 0.02, seed=8)
+    op = to_op(sc, case)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    first = None
+    for _ in range(3):
+        y, mask, _ = run_gpu(op, case.x_bits)
+        assert np.array_equal(mask, rr)
+        if first is None:
+            first = y_bits(y)
+        assert np.array_equal(y_bits(y), first), "the fast path is deterministic run to run"
+
+
+@pytest.mark.parametrize("n,k,m", [(3584, 3584, 1), (18944, 3584, 4), (3584, 18944, 16)])
+def test_qwen2_7b_shapes(sc, n, k, m):
+    case = make_case(n, k, m, 0.01, seed=n + m, boost=[0])
+    op = to_op(sc, case, mode="fast")
+    y, mask, _ = run_gpu(op, case.x_bits)
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    assert np.array_equal(mask, rr)
+    assert_fast_close(y_bits(y), yr, f"7B {n}x{k}")
+    acc = op.forward_partial(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")).cpu().numpy()
+    assert_acc_close(acc, acc_ref, f"7B acc {n}x{k}")
+
+
+# ------------------------------------------------------------------ tensor-parallel slices
+
+@pytest.mark.parametrize("count", [2, 3])
+def test_column_shards_concatenate(sc, count):
+    case = make_case(520, 256, 6, 0.02, seed=31)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    x = torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")
+    parts = []
+    for i in range(count):
+        op = to_op(sc, case, mode="exact", shard=("columns", i, count))
+        parts.append(y_bits(op.forward(x)))
+    assert np.array_equal(np.concatenate(parts, axis=1), yr)
+
+
+@pytest.mark.parametrize("count", [2, 4])
+def test_row_shards_sum_to_full(sc, count):
+    case = make_case(300, 1024, 5, 0.02, seed=41)
+    _, rr, acc_ref = case.oracle().forward(case.x_bits)
+    x = torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")
+    total = None
+    for i in range(count):
+        op = to_op(sc, case, mode="fast", shard=("rows", i, count))
+        part, mask = op.forward_partial(x, return_routing=True)
+        assert np.array_equal(mask.cpu().numpy(), rr), "every shard routes on the whole token"
+        total = part if total is None else total + part
+    assert_acc_close(total.cpu().numpy(), acc_ref, "rows shards")
+    y = sc.finalize(total)
+    yr, _, _ = case.oracle().forward(case.x_bits)
+    assert_fast_close(y_bits(y), yr, "rows shards f16")
+
+
+# ------------------------------------------------------------------ format producer on the GPU
+
+@pytest.mark.parametrize("n,k,fill", [(4864, 896, 0.01), (77, 200, 0.15), (256, 64, 1.0), (33, 8, 0.5)])
+def test_gpu_packer_bit_identical(sc, n, k, fill):
+    rng = np.random.default_rng(n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w[min(2, n - 1)] = 0.0
+    wt = torch.from_numpy(w).to("cuda:0")
+    thr = sc.compute_percentile_threshold(wt, fill)
+    assert np.float32(thr) == np.float32(O.percentile_threshold(w, fill))
+    blocks = sc.compress_tensor_to_saccade(wt, thr)
+    ref = O.compress(w, thr)
+    assert np.array_equal(blocks["packed_base"].view(torch.int32).cpu().numpy().view(np.uint32), ref.packed_base)
+    assert np.array_equal(blocks["scale_base"].cpu().numpy().view(np.uint16), ref.scale_base)
+    if ref.nnz:
+        assert np.array_equal(blocks["delta_row_ptrs"].view(torch.int32).cpu().numpy().view(np.uint32),
+                              ref.delta_row_ptrs)
+        assert np.array_equal(blocks["delta_col_indices"].view(torch.int32).cpu().numpy().view(np.uint32),
+                              ref.delta_col_indices)
+        assert np.array_equal(blocks["delta_values"].cpu().numpy(), ref.delta_values)
+        assert int(blocks["delta_scale"].view(torch.int16).item()) & 0xFFFF == ref.delta_scale
+    else:
+        assert "delta_row_ptrs" not in blocks
+
+
+def test_gpu_calibrate_and_variance(sc):
+    rng = np.random.default_rng(12)
+    acts = rng.standard_normal((300, 512)).astype(np.float32)
+    acts[::7] *= 8
+    a16 = acts.astype(np.float16)
+    for p4, p8 in ((0.75, 0.95), (0.0, 1.0), (0.5, 0.333)):
+        assert sc.ProfileRunner.calibrate(torch.from_numpy(acts), p4, p8) == O.calibrate(acts, p4, p8)
+        assert sc.ProfileRunner.calibrate(torch.from_numpy(a16), p4, p8) == O.calibrate(
+            a16.astype(np.float32), p4, p8)
+    v = sc.variance_heuristic(torch.from_numpy(a16).to("cuda:0")).cpu().numpy()
+    ref = np.array([O.variance(a16[t].view(np.uint16)) for t in range(300)], dtype=np.float32)
+    assert np.array_equal(v.view(np.uint32), ref.view(np.uint32))
+
+
+def test_end_to_end_from_dense_weights(sc):
+    # W on the GPU -> GPU packer -> layer -> forward, against the oracle run on the same W
+    case = make_case(1024, 896, 16, 0.01, seed=77)
+    wt = torch.from_numpy(case.w).to("cuda:0")
+    thr = sc.compute_percentile_threshold(wt, 0.01)
+    blocks = sc.compress_tensor_to_saccade(wt, thr)
+    op = sc.saccade_op_from_compressed(blocks, sc.SaccadeConfig(case.t4, case.t8), 1024, 896, mode="exact")
+    y, mask, _ = run_gpu(op, case.x_bits)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    assert np.array_equal(mask, rr) and np.array_equal(y_bits(y), yr)
