@@ -132,9 +132,11 @@ SC_API size_t sc_workspace_size(const sc_layer* layer, int64_t m);
  * n_routed_out (nullable, i32 [1]) are device outputs of the router.
  * sc_forward uses a per-device default workspace that it allocates on first use and grows
  * when a larger m arrives (both synchronise the device); it is meant for one stream at a time.
- * sc_forward_ws takes a caller workspace of sc_workspace_size() bytes (256-byte aligned) that is
- * zero-filled before its first use: it holds completion counters that every call returns to
- * zero.  Calls sharing a workspace must not overlap on the GPU. */
+ * sc_forward_ws takes a caller workspace of sc_workspace_size() bytes (256-byte aligned).  Its
+ * first 64 KiB hold completion counters at fixed offsets: zero-fill them before the first use;
+ * every call returns them to zero, so one workspace serves any sequence of layers and token
+ * counts.  Calls sharing a workspace must not overlap on the GPU.  After SC_ETIMEOUT, zero the
+ * counter region again before reusing the workspace. */
 SC_API sc_status sc_forward(const sc_layer* layer, const void* x, int x_dtype, int64_t m,
                      void* y, int y_dtype, const float* bias,
                      uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out, void* stream);

@@ -48,31 +48,46 @@ static int sm_count(int dev) {
     return n > 0 ? n : 148;
 }
 
+// Workspace layout.  The first kCounterBytes hold completion counters (the router's at
+// offset 0, the split-K row-tile counters after it) at offsets that do not depend on the
+// layer or the token count, so one workspace can serve every layer: each call returns the
+// counters it used to zero.  Everything after that region is scratch rewritten per call.
+// Column splits of the router-fused decode kernel: cover the SMs with 128-row tiles times
+// splits, with each CTA's column slice of x fitting its shared-memory copy.
+int fused_ksplit(const Layer& L) {
+    const int64_t RT = L.Np / 128;
+    int64_t ks = (static_cast<int64_t>(L.sms) + RT / 2) / RT;
+    ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(32, std::max<int64_t>(1, L.KB / 4))));
+    ks = std::max<int64_t>(ks, (L.KB + fused_max_kb() - 1) / fused_max_kb());
+    return static_cast<int>(ks);
+}
+
 WsLayout plan_workspace(const Layer& L, int64_t m) {
     WsLayout w;
-    w.Mp = m <= 8 ? 8 : (m <= 16 ? 16 : ceil_to(m, 32));
+    w.Mp = m <= 16 ? 16 : ceil_to(m, 32);
     w.chunk_tokens = 32;
-    size_t off = 0;
+    w.counter = 0;
+    w.rtcount = 256;
+    size_t off = kCounterBytes;
     auto take = [&](size_t bytes) {
         size_t o = off;
         off = static_cast<size_t>(ceil_to(static_cast<int64_t>(off + bytes), 256));
         return o;
     };
-    w.xk = take(static_cast<size_t>(L.KB * 64 * w.Mp * 2));
+    w.xk = take(static_cast<size_t>(L.KB * 64 * w.Mp * 2));  // [KB][Mp/8][8][8][8] f16
     w.mask = take(static_cast<size_t>(m > 0 ? m : 1));
     w.scores = take(static_cast<size_t>(4 * (m > 0 ? m : 1)));
     w.ridx = take(static_cast<size_t>(4 * (m > 0 ? m : 1)));
     w.nrouted = take(16);
-    w.counter = take(16);
-    const int64_t RT = (L.Np + 127) / 128;
-    const int64_t first = std::min<int64_t>(m, 32);
-    const int occ = first <= 16 ? 2 : 1;
-    const int64_t target = static_cast<int64_t>(L.sms) * occ;
+    // one CTA per SM (the ring takes ~200 KB of shared memory): split K so that the
+    // 128-row tiles times the splits cover the SMs, with at least one 4-block stage each
+    const int64_t RT = L.Np / 128;
+    const int64_t target = static_cast<int64_t>(L.sms);
     int64_t ks = (target + RT / 2) / RT;
     ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(32, std::max<int64_t>(1, L.KB / 4))));
+    if (m <= 8) ks = L.ks_fused;
     w.ksplit = static_cast<int>(ks);
     w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
-    w.rtcount = take(static_cast<size_t>(RT * 4));
     w.total = off;
     return w;
 }
@@ -140,6 +155,31 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         return SC_ENOMEM;
     }
     unsigned char* base = static_cast<unsigned char*>(ws);
+    const bool bypass_now = g_bypass.load() != 0;
+    if (L.mode == SC_MODE_FAST && m <= 8) {
+        // one launch: router, x staging, base product and dW in the same kernel
+        FusedArgs f;
+        f.L = &L;
+        f.x = x;
+        f.x_dtype = x_dtype;
+        f.x_stride = L.shard_kind == SC_SHARD_ROWS ? L.fullK : L.K;
+        f.x_col0 = L.shard_kind == SC_SHARD_ROWS ? L.col_begin : 0;
+        f.m = m;
+        f.route_all = bypass_now ? 1 : 0;
+        f.y = y;
+        f.y_dtype = partial ? SC_F32 : y_dtype;
+        f.bias = partial ? nullptr : bias;
+        f.partial_out = partial ? 1 : 0;
+        f.mask_out = mask_out;
+        f.ridx_out = ridx_out;
+        f.nrouted_out = nrouted_out;
+        f.ws_partial = reinterpret_cast<float*>(base + w.partial);
+        f.ws_rtcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
+        f.ksplit = w.ksplit;
+        cudaError_t e = launch_decode_fused(f, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "fused decode launch");
+        return SC_OK;
+    }
     uint16_t* xk = reinterpret_cast<uint16_t*>(base + w.xk);
     uint8_t* mask = mask_out ? mask_out : reinterpret_cast<uint8_t*>(base + w.mask);
     int32_t* ridx = ridx_out ? ridx_out : reinterpret_cast<int32_t*>(base + w.ridx);
@@ -236,6 +276,10 @@ static void free_layer(Layer& L) {
     cudaFree(L.col);
     cudaFree(L.val);
     cudaFree(L.status);
+    cudaFree(L.dwblk);
+    cudaFree(L.dwoff);
+    L.dwblk = nullptr;
+    L.dwoff = nullptr;
     L.wq = nullptr;
     L.scale = nullptr;
     L.rowptr = nullptr;
@@ -304,11 +348,15 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     L.col_begin = c0;
     L.N = r1 - r0;
     L.K = c1 - c0;
+    if (ceil_to(L.N, 128) / 128 > kMaxRowTiles) {
+        set_error("sc_layer_create: out_features per shard above " + std::to_string(kMaxRowTiles * 128));
+        return SC_EUNSUPPORTED;
+    }
     if (L.K > 65536) {
         set_error("sc_layer_create: in_features per shard above 65536 (u16 dW columns)");
         return SC_EUNSUPPORTED;
     }
-    L.Np = ceil_to(L.N, 16);
+    L.Np = ceil_to(L.N, 128);
     L.Kp = ceil_to(L.K, 64);
     L.KB = L.Kp / 64;
 
@@ -403,7 +451,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     }
 
     // ---- allocations
-    const int64_t wq_words = (L.Np / 16) * L.KB * 128;
+    const int64_t wq_words = L.Np * L.KB * 8;
     auto alloc = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes > 0 ? bytes : 16); };
     if ((e = alloc(reinterpret_cast<void**>(&L.wq), wq_words * 4)) != cudaSuccess ||
         (e = alloc(reinterpret_cast<void**>(&L.scale), L.Np * 4)) != cudaSuccess ||
@@ -441,6 +489,54 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     if (e == cudaSuccess && L.nnz > 0) e = cudaMemcpy(L.col, scol.data(), L.nnz * 2, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && L.nnz > 0) e = cudaMemcpy(L.val, sval.data(), L.nnz, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemset(L.status, 0, 16);
+    if (e == cudaSuccess) {
+        // dW blocks of the router-fused decode kernel
+        L.ks_fused = fused_ksplit(L);
+        const int64_t RT = L.Np / 128, ks = L.ks_fused;
+        std::vector<uint32_t> off(RT * ks + 1, 0);
+        std::vector<uint8_t> blob;
+        int64_t maxb = 0;
+        for (int64_t rt = 0; rt < RT; ++rt) {
+            for (int64_t sp = 0; sp < ks; ++sp) {
+                const int64_t bc0 = (L.KB * sp / ks) * 64, bc1 = (L.KB * (sp + 1) / ks) * 64;
+                std::vector<uint16_t> roff(129, 0), cols;
+                std::vector<int8_t> vals;
+                for (int r = 0; r < 128; ++r) {
+                    roff[r] = static_cast<uint16_t>(cols.size());
+                    const int64_t row = rt * 128 + r;
+                    if (row < L.N) {
+                        for (uint32_t q = srp[row]; q < srp[row + 1]; ++q) {
+                            if (scol[q] >= bc0 && scol[q] < bc1) {
+                                cols.push_back(static_cast<uint16_t>(scol[q] - bc0));
+                                vals.push_back(sval[q]);
+                            }
+                        }
+                    }
+                }
+                roff[128] = static_cast<uint16_t>(cols.size());
+                const size_t n = cols.size();
+                const size_t bytes = 272 + ((n * 2 + 15) / 16) * 16 + ((n + 15) / 16) * 16;
+                const size_t at = blob.size();
+                blob.resize(at + bytes, 0);
+                std::memcpy(&blob[at], roff.data(), 129 * 2);
+                if (n) {
+                    std::memcpy(&blob[at + 272], cols.data(), n * 2);
+                    std::memcpy(&blob[at + 272 + ((n * 2 + 15) / 16) * 16], vals.data(), n);
+                }
+                off[rt * ks + sp + 1] = static_cast<uint32_t>(blob.size());
+                maxb = std::max<int64_t>(maxb, static_cast<int64_t>(bytes));
+                if (n > 65535) maxb = INT64_MAX;  // u16 row offsets cannot describe the block
+            }
+        }
+        L.dw_max_block = maxb;
+        if (L.nnz > 0 && maxb <= kDwBlockMax) {
+            if ((e = cudaMalloc(&L.dwblk, blob.size())) == cudaSuccess &&
+                (e = cudaMalloc(&L.dwoff, off.size() * 4)) == cudaSuccess &&
+                (e = cudaMemcpy(L.dwblk, blob.data(), blob.size(), cudaMemcpyHostToDevice)) == cudaSuccess)
+                e = cudaMemcpy(L.dwoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
+            L.device_bytes += static_cast<int64_t>(blob.size() + off.size() * 4);
+        }
+    }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(tmp_packed);
     cudaFree(tmp_scale);

@@ -1,28 +1,31 @@
-// sc_decode.cu -- C-TARQ decode kernels (few tokens per call).
+// sc_decode.cu -- C-TARQ kernels for a few tokens per call (decode).
 //
-// k_decode_tc: the fast path.  One CTA owns 128 output rows (eight 16-row tiles) and a
-// contiguous range of 64-column blocks (split-K across CTAs when there are few rows).
-//   warp 8 (producer)   : one lane streams the weight tiles and the staged activations
-//                         into an 8-stage shared-memory ring with non-multicast bulk copies
-//                         (cp.async.bulk + mbarrier complete_tx); weights carry an L2
-//                         evict-first hint since each byte is read exactly once.
-//   warps 0-7 (MMA)     : one 16-row tile each; per 64-column block a lane reads 16 bytes
-//                         (four packed words), turns each word into an A fragment of exact
-//                         f16 integers q-8 (sc_device.cuh: dequant_word) and issues
-//                         m16n8k16 MMAs against the activations, f32 accumulation in registers.
-//                         The row scale is applied once at the end, as op.rs:148 does.
-//   warps 9-12 (dW)     : one output row per lane; while the MMA warps stream, they walk the
-//                         row's CSR dW entries inside this CTA's column range and accumulate
-//                         x * (i8 * scale) for the routed tokens (op.rs:152-170).
-// Epilogue: y = f16(acc * s + dW) (+ bias), or for split-K the last CTA of a row tile sums
-// the per-split partials in split order (deterministic) and stores.
+// Both fast kernels stream the 4-bit base through a shared-memory ring filled by one
+// producer lane with non-multicast bulk copies (cp.async.bulk + mbarrier complete_tx, L2
+// evict-first on weights).  A CTA owns one 128-row tile and a contiguous range of 64-column
+// blocks (split-K across CTAs when a layer has few rows).  Under programmatic dependent
+// launch the producer requests its first weight stages before griddepcontrol.wait, so they
+// overlap the previous kernel's tail; activations are read only after the wait.
 //
-// k_decode_exact: SC_MODE_EXACT.  One thread per row pair of a tile replays op.rs exactly:
-// four f32 accumulators fed in the reference's order with single-rounding
-// f16 x f16 -> f32 FMAs (the products are exact), ((a0+a1)+a2)+a3 then * scale, then the
-// dW entries in ascending column order with separate multiply and add.  Y is
-// bit-identical to the reference's cpu_fwd.  Each accumulator is a K/4-long dependent
-// chain, so this path is latency-bound; it exists for verification.
+//   k_ctarq_mma  (<= 8 tokens): eight MMA warps, one 16-row tile each.  Per 64 columns a lane
+//                reads 16 bytes of packed nibbles, converts each word into an mma.m16n8k16 A
+//                fragment of exact integers q-8 in registers (dequant_word) and multiplies it
+//                with the activations, f32 accumulation.  At decode sizes the kernel is
+//                bound by HBM and by this conversion, not by the tensor pipe.
+//   k_ctarq_tc   (9..32 tokens): the same words are stored to TMEM with tcgen05.st.16x256b and
+//                one thread issues tcgen05.mma.kind::f16 (A from TMEM, activations from shared
+//                memory as K-major core matrices, f32 accumulators in TMEM): the 5th-gen tensor
+//                core covers 16-32 tokens per instruction where mma.sync would need 2-4.
+//   dW warps (both kernels): one output row per lane; they walk the row's CSR dW entries in
+//                the CTA's column range for the routed tokens (op.rs:152-170) meanwhile.
+// Epilogue: y = f16(acc * s + dW) (+ bias after the rounding); with split-K the last CTA of a
+// row tile sums the partials in split order (deterministic).
+//
+// k_decode_exact: SC_MODE_EXACT.  One thread per row pair replays op.rs exactly: four f32
+// accumulators fed in the reference's order with single-rounding f16 x f16 -> f32 FMAs
+// (the products are exact), ((a0+a1)+a2)+a3 then * scale, then the dW entries in ascending
+// column order with separate multiply and add.  Y is bit-identical to cpu_fwd.  Each
+// accumulator is a K/4-long dependent chain: a verification path, not a fast one.
 #include <atomic>
 
 #include "sc_device.cuh"
@@ -30,11 +33,6 @@
 
 namespace sc {
 
-constexpr int kMmaWarps = 8;
-constexpr int kDeltaWarps = 4;
-constexpr int kProducerWarp = kMmaWarps;
-constexpr int kThreadsTC = (kMmaWarps + 1 + kDeltaWarps) * 32;  // 416
-constexpr int kSKB = 2;      // 64-column blocks per stage
 constexpr int kMaxChunkTokens = 32;
 
 struct TCParams {
@@ -51,7 +49,7 @@ struct TCParams {
     int ntok;
     const uint8_t* mask;
     int route_all;
-    int64_t N, K, KB, NT16;
+    int64_t N, K, KB;
     void* y;
     int y_dtype;
     const float* bias;
@@ -60,23 +58,6 @@ struct TCParams {
     uint32_t* ws_rtcount;
     int ksplit;
     uint32_t* status;
-};
-
-template <int NG>
-struct TCSmem {
-    // 8 stages (80 KB) for one token group and 6 (72 KB) for two keep two CTAs per SM;
-    // four groups take 8 stages (128 KB) and one CTA per SM.
-    static constexpr int kStages = NG == 2 ? 6 : 8;
-    static constexpr int kWBytes = kMmaWarps * kSKB * 512;    // weights per stage
-    static constexpr int kXBytes = kSKB * NG * 1024;          // activations per stage
-    static constexpr int kStageBytes = kWBytes + kXBytes;
-    static constexpr int kTok = NG * 8;
-    static constexpr int kLd = kTok + 1;                      // padded row of acc/corr tiles
-    static constexpr int kRingBytes = kStages * kStageBytes;
-    static constexpr int kAccOff = kRingBytes;
-    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
-    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
-    static constexpr int kTotal = kBarOff + 2 * kStages * 8 + 16;
 };
 
 __device__ __forceinline__ int64_t lower_bound_u16(const uint16_t* col, int64_t lo, int64_t hi, int64_t key) {
@@ -88,164 +69,106 @@ __device__ __forceinline__ int64_t lower_bound_u16(const uint16_t* col, int64_t 
     return lo;
 }
 
-template <int NG>
-__global__ void __launch_bounds__(kThreadsTC, NG <= 2 ? 2 : 1) k_decode_tc(TCParams p) {
-    using S = TCSmem<NG>;
-    constexpr int kStages = S::kStages;
-    extern __shared__ __align__(128) unsigned char smem[];
-    float* accbuf = reinterpret_cast<float*>(smem + S::kAccOff);
-    float* corrbuf = reinterpret_cast<float*>(smem + S::kCorrOff);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
-    uint64_t* empty = full + kStages;
-    __shared__ int s_last;
-    __shared__ int s_abort;
+// ---------------------------------------------------------------- shared pieces
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t rt = blockIdx.x / p.ksplit;
-    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
-    const int64_t kb_begin = (p.KB * split) / p.ksplit;
-    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
-    const int nst = static_cast<int>((kb_end - kb_begin + kSKB - 1) / kSKB);
-    const int64_t tile0 = rt * kMmaWarps;
-    const int ntiles = static_cast<int>(imin64(kMmaWarps, p.NT16 - tile0));
-
-    if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kMmaWarps);
-        }
-        fence_mbar_init();
-        s_abort = 0;
+// Producer lane: weights (4 KB per 64-column block, contiguous per row tile) and the real
+// token groups of the activations (1 KB per block and group) into ring stage `slot`.
+// Weights of the first `kStages` stages are requested before the dependency wait.
+template <int SKB, int S, int G, int WBYTES, int STAGEBYTES>
+__device__ __forceinline__ int producer_run(const TCParams& p, unsigned char* smem, uint64_t* full, uint64_t* empty,
+                                            int64_t rt, int64_t kb_begin, int64_t kb_end, int greal, int* abort) {
+    const int nst = static_cast<int>((kb_end - kb_begin + SKB - 1) / SKB);
+    const int Gp = static_cast<int>(p.Mp >> 3);
+    const uint64_t pol = policy_evict_first();
+    int issued = 0;
+    const int pre = nst < S ? nst : S;
+    for (int it = 0; it < pre; ++it, ++issued) {
+        const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
+        const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
+        mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
+        bulk_g2s_stream(smem + it * STAGEBYTES, p.wq + (rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096),
+                        &full[it], pol);
     }
-    for (int i = tid; i < 128 * S::kLd; i += kThreadsTC) corrbuf[i] = 0.0f;
-    __syncthreads();
-
-    int issued = 0;  // producer lane 0: stages whose copies were issued
-    if (warp == kProducerWarp) {
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            for (int it = 0; it < nst; ++it, ++issued) {
-                const int slot = it % kStages;
-                if (it >= kStages) {
-                    if (!mbar_wait(&empty[slot], ((it / kStages) - 1) & 1, p.status)) {
-                        s_abort = 1;
-                        break;
-                    }
-                }
-                const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * kSKB;
-                const int nkb = static_cast<int>(imin64(kSKB, kb_end - kb0));
-                unsigned char* st = smem + slot * S::kStageBytes;
-                const uint32_t bytes = static_cast<uint32_t>(ntiles * nkb * 512 + nkb * NG * 1024);
-                mbar_arrive_expect_tx(&full[slot], bytes);
-                for (int w = 0; w < ntiles; ++w) {
-                    const uint32_t* src = p.wq + ((tile0 + w) * p.KB + kb0) * 128;
-                    bulk_g2s_stream(st + w * kSKB * 512, src, static_cast<uint32_t>(nkb * 512), &full[slot], pol);
-                }
-                for (int j = 0; j < nkb; ++j) {
-                    const uint16_t* src = p.xk + ((kb0 + j) * p.Mp + p.tok0) * 64;
-                    bulk_g2s(st + S::kWBytes + j * NG * 1024, src, NG * 1024, &full[slot]);
-                }
-            }
-        }
-    } else if (warp < kMmaWarps) {
-        float acc[NG][4];
-#pragma unroll
-        for (int g = 0; g < NG; ++g)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[g][i] = 0.0f;
-        const bool valid = warp < ntiles;
-        const int tl = lane >> 2, c = lane & 3;
-        for (int it = 0; it < nst; ++it) {
-            const int slot = it % kStages;
-            if (!mbar_wait(&full[slot], (it / kStages) & 1, p.status)) {
-                s_abort = 1;
+    pdl_wait();
+    for (int it = 0; it < nst; ++it) {
+        const int slot = it % S;
+        const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
+        const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
+        unsigned char* st = smem + slot * STAGEBYTES;
+        if (it >= S) {
+            if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
+                *abort = 1;
                 break;
             }
-            const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * kSKB;
-            const int nkb = static_cast<int>(imin64(kSKB, kb_end - kb0));
-            const unsigned char* st = smem + slot * S::kStageBytes;
-            if (valid) {
-                for (int j = 0; j < nkb; ++j) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(st + warp * kSKB * 512 + j * 512 + lane * 16);
-                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-                    const uint32_t* xw = reinterpret_cast<const uint32_t*>(st + S::kWBytes + j * NG * 1024);
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        uint32_t a[4];
-                        dequant_word(words[s], a);
-#pragma unroll
-                        for (int g = 0; g < NG; ++g) {
-                            const uint32_t* xr = xw + g * 256 + tl * 32;
-                            const uint32_t b0 = xr[((2 * s) ^ tl) * 4 + c];
-                            const uint32_t b1 = xr[((2 * s + 1) ^ tl) * 4 + c];
-                            mma_16816(acc[g], a, b0, b1);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
+            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * 4096));
+            bulk_g2s_stream(st, p.wq + (rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096), &full[slot], pol);
+            ++issued;
         }
-        if (valid) {
-            const int r0 = warp * 16 + tl;
-#pragma unroll
-            for (int g = 0; g < NG; ++g) {
-                const int t0 = g * 8 + 2 * c;
-                accbuf[r0 * S::kLd + t0] = acc[g][0];
-                accbuf[r0 * S::kLd + t0 + 1] = acc[g][1];
-                accbuf[(r0 + 8) * S::kLd + t0] = acc[g][2];
-                accbuf[(r0 + 8) * S::kLd + t0 + 1] = acc[g][3];
-            }
-        }
-    } else {
-        // dW warps: one output row per lane, entries of this CTA's column range
-        const int rl = (warp - kMmaWarps - 1) * 32 + lane;
-        const int64_t row = rt * 128 + rl;
-        uint32_t routed = 0;
-        for (int tt = 0; tt < p.ntok; ++tt)
-            if (p.route_all || p.mask[p.tok0 + tt]) routed |= 1u << tt;
-        if (routed != 0 && row < p.N && p.nnz > 0) {
-            const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
-            const int64_t e0 = lower_bound_u16(p.col, lo, hi, kb_begin * 64);
-            const int64_t e1 = lower_bound_u16(p.col, e0, hi, kb_end * 64);
-            float corr[S::kTok];
-#pragma unroll
-            for (int tt = 0; tt < S::kTok; ++tt) corr[tt] = 0.0f;
-            for (int64_t e = e0; e < e1; ++e) {
-                const int64_t cc = p.col[e];
-                const float v = __fmul_rn(static_cast<float>(p.val[e]), p.ds);
-#pragma unroll
-                for (int tt = 0; tt < S::kTok; ++tt) {
-                    if (tt < p.ntok && ((routed >> tt) & 1u)) {
-                        const int t = static_cast<int>(p.tok0 + tt);
-                        const float xv = h2f(p.xk[xk_index(cc, t, static_cast<int>(p.Mp))]);
-                        corr[tt] = __fadd_rn(corr[tt], __fmul_rn(xv, v));
-                    }
-                }
-            }
-#pragma unroll
-            for (int tt = 0; tt < S::kTok; ++tt) corrbuf[rl * S::kLd + tt] = corr[tt];
-        }
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * greal * 1024));
+        for (int j = 0; j < n; ++j)
+            bulk_g2s(st + WBYTES + j * G * 1024, p.xk + ((kb0 + j) * Gp + (p.tok0 >> 3)) * 512,
+                     static_cast<uint32_t>(greal * 1024), &full[slot]);
     }
-    __syncthreads();
-    if (s_abort) {
-        // A wait ran out (already recorded).  Let this CTA's own bulk copies land before its
-        // shared memory is released: bounded waits on the last stages that were issued.
-        if (warp == kProducerWarp && lane == 0) {
-            for (int it = issued > kStages ? issued - kStages : 0; it < issued; ++it)
-                mbar_wait(&full[it % kStages], (it / kStages) & 1, nullptr, kDrainNs);
-        }
-        return;
-    }
+    return issued;
+}
 
-    // epilogue
+// dW warps: lane `rl` of a 128-row tile accumulates x * (i8 * scale) over the row's CSR entries
+// inside [kb_begin*64, kb_end*64) for every routed token of the chunk, in column order.
+template <int NT, int LD>
+__device__ __forceinline__ void delta_rows(const TCParams& p, float* corrbuf, int rl, int64_t rt, int64_t kb_begin,
+                                           int64_t kb_end) {
+    const int64_t row = rt * 128 + rl;
+    uint32_t routed = 0;
+    for (int tt = 0; tt < p.ntok; ++tt)
+        if (p.route_all || p.mask[p.tok0 + tt]) routed |= 1u << tt;
+    if (routed == 0 || row >= p.N || p.nnz == 0) return;
+    const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
+    const int64_t e0 = lower_bound_u16(p.col, lo, hi, kb_begin * 64);
+    const int64_t e1 = lower_bound_u16(p.col, e0, hi, kb_end * 64);
+    float corr[NT];
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) corr[tt] = 0.0f;
+    for (int64_t e = e0; e < e1; e += 8) {
+        const int cnt = static_cast<int>(imin64(8, e1 - e));
+        int64_t cc[8];
+        float vv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            cc[u] = u < cnt ? static_cast<int64_t>(p.col[e + u]) : 0;
+            vv[u] = u < cnt ? __fmul_rn(static_cast<float>(p.val[e + u]), p.ds) : 0.0f;
+        }
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) {
+            if ((routed >> tt) & 1u) {
+                const int t = static_cast<int>(p.tok0 + tt);
+                float xv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    xv[u] = u < cnt ? h2f(p.xk[xk_index(cc[u], t, static_cast<int>(p.Mp))]) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (u < cnt) corr[tt] = __fadd_rn(corr[tt], __fmul_rn(xv[u], vv[u]));
+            }
+        }
+    }
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) corrbuf[rl * LD + tt] = corr[tt];
+}
+
+// Epilogue over a [128 x NT] tile of f32 accumulators held in shared memory.  Single-split:
+// y = acc*s + dW.  Split-K: partials to the workspace, the last CTA of the row tile sums them
+// in split order.  Returns after the stores.
+template <int NT, int LD, int NTHREADS>
+__device__ __forceinline__ void epilogue_tile(const TCParams& p, const float* accbuf, const float* corrbuf, int64_t rt,
+                                              int split, int* s_last) {
+    const int tid = threadIdx.x;
     const int cnt = 128 * p.ntok;
     if (p.ksplit == 1) {
-        for (int i = tid; i < cnt; i += kThreadsTC) {
+        for (int i = tid; i < cnt; i += NTHREADS) {
             const int rl = i & 127, tt = i >> 7;
             const int64_t row = rt * 128 + rl;
             if (row >= p.N) continue;
-            const float v = __fadd_rn(__fmul_rn(accbuf[rl * S::kLd + tt], p.scale[row]), corrbuf[rl * S::kLd + tt]);
+            const float v = __fadd_rn(__fmul_rn(accbuf[rl * LD + tt], p.scale[row]), corrbuf[rl * LD + tt]);
             const int64_t oi = (p.tok0 + tt) * p.N + row;
             if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = v;
             else store_output(p.y, p.y_dtype, oi, v, p.bias, row);
@@ -253,11 +176,10 @@ __global__ void __launch_bounds__(kThreadsTC, NG <= 2 ? 2 : 1) k_decode_tc(TCPar
         return;
     }
     float* part = p.ws_partial + (rt * p.ksplit) * 128 * kMaxChunkTokens;
-    for (int i = tid; i < cnt; i += kThreadsTC) {
+    for (int i = tid; i < cnt; i += NTHREADS) {
         const int rl = i & 127, tt = i >> 7;
         const int64_t row = rt * 128 + rl;
-        const float v = row < p.N ? __fadd_rn(__fmul_rn(accbuf[rl * S::kLd + tt], p.scale[row]),
-                                              corrbuf[rl * S::kLd + tt])
+        const float v = row < p.N ? __fadd_rn(__fmul_rn(accbuf[rl * LD + tt], p.scale[row]), corrbuf[rl * LD + tt])
                                   : 0.0f;
         part[(split * 128 + rl) * kMaxChunkTokens + tt] = v;
     }
@@ -265,12 +187,12 @@ __global__ void __launch_bounds__(kThreadsTC, NG <= 2 ? 2 : 1) k_decode_tc(TCPar
     __syncthreads();
     if (tid == 0) {
         const unsigned ticket = atomicAdd(&p.ws_rtcount[rt], 1u);
-        s_last = (ticket == static_cast<unsigned>(p.ksplit - 1)) ? 1 : 0;
+        *s_last = (ticket == static_cast<unsigned>(p.ksplit - 1)) ? 1 : 0;
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!*s_last) return;
     __threadfence();
-    for (int i = tid; i < cnt; i += kThreadsTC) {
+    for (int i = tid; i < cnt; i += NTHREADS) {
         const int rl = i & 127, tt = i >> 7;
         const int64_t row = rt * 128 + rl;
         if (row >= p.N) continue;
@@ -283,21 +205,634 @@ __global__ void __launch_bounds__(kThreadsTC, NG <= 2 ? 2 : 1) k_decode_tc(TCPar
     if (tid == 0) p.ws_rtcount[rt] = 0u;
 }
 
-template <int NG>
-static cudaError_t launch_tc_ng(const TCParams& p, int64_t RT, cudaStream_t s) {
-    const int smem = TCSmem<NG>::kTotal;
-    // The shared-memory opt-in is per device; remember it per ordinal.
-    static std::atomic<uint64_t> attr_set{0};
+// ---------------------------------------------------------------- k_ctarq_mma (<= 8 tokens)
+
+struct MmaCfg {
+    static constexpr int kMmaWarps = 8;              // one 16-row tile each
+    static constexpr int kProducerWarp = 8;
+    static constexpr int kDeltaWarp0 = 9;
+    static constexpr int kThreads = 13 * 32;
+    static constexpr int NT = 8;
+    static constexpr int G = 1;
+    static constexpr int SKB = 8;                    // 64-column blocks per stage (32 KB of weights)
+    static constexpr int S = 4;
+    static constexpr int kWBytes = SKB * 4096;
+    static constexpr int kXBytes = SKB * G * 1024;
+    static constexpr int kStageBytes = kWBytes + kXBytes;
+    static constexpr int kLd = NT + 1;
+    static constexpr int kAccOff = S * kStageBytes;
+    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
+    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
+    static constexpr int kTotal = kBarOff + 2 * S * 8 + 16;
+    static_assert(kTotal <= 227 * 1024, "shared memory");
+};
+
+__global__ void __launch_bounds__(MmaCfg::kThreads, 1) k_ctarq_mma(TCParams p) {
+    using C = MmaCfg;
+    constexpr int SKB = C::SKB, S = C::S;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
+    float* corrbuf = reinterpret_cast<float*>(smem + C::kCorrOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* empty = full + S;
+    __shared__ int s_last;
+    __shared__ int s_abort;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t rt = blockIdx.x / p.ksplit;
+    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
+    const int64_t kb_begin = (p.KB * split) / p.ksplit;
+    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
+    const int nst = static_cast<int>((kb_end - kb_begin + SKB - 1) / SKB);
+
+    pdl_launch_dependents();
+    for (int i = tid; i < 2 * 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;  // acc and dW tiles
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 2);
+            mbar_init(&empty[i], C::kMmaWarps);
+        }
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+
+    int issued = 0;
+    if (warp == C::kProducerWarp) {
+        if (lane == 0)
+            issued = producer_run<SKB, S, C::G, C::kWBytes, C::kStageBytes>(p, smem, full, empty, rt, kb_begin, kb_end,
+                                                                           1, &s_abort);
+    } else if (warp < C::kMmaWarps) {
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int g = lane >> 2, c = lane & 3;
+        const bool has_tok = g < p.ntok;
+        // B fragment of step s: x[token g][k0 + 4c .. +3] (the permuted K of the A fragment)
+        const int xoff = g * 16 + (c & 1) * 8 + (c >> 1) * 128;
+        for (int it = 0; it < nst; ++it) {
+            const int slot = it % S;
+            if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
+                s_abort = 1;
+                break;
+            }
+            const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
+            const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
+            const unsigned char* st = smem + slot * C::kStageBytes;
+#pragma unroll
+            for (int j = 0; j < SKB; ++j) {
+                if (j < n) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(st + j * 4096 + warp * 512 + lane * 16);
+                    const unsigned char* xb = st + C::kWBytes + j * 1024 + xoff;
+                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        uint2 b = make_uint2(0u, 0u);
+                        if (has_tok) b = *reinterpret_cast<const uint2*>(xb + s * 256);
+                        uint32_t a[4];
+                        dequant_word(words[s], a);
+                        mma_16816(acc[s & 1], a, b.x, b.y);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        // fragment -> tile: rows g, g+8 of this warp's tile; tokens 2c, 2c+1
+        const int r0 = warp * 16 + g;
+        accbuf[r0 * C::kLd + 2 * c] = acc[0][0] + acc[1][0];
+        accbuf[r0 * C::kLd + 2 * c + 1] = acc[0][1] + acc[1][1];
+        accbuf[(r0 + 8) * C::kLd + 2 * c] = acc[0][2] + acc[1][2];
+        accbuf[(r0 + 8) * C::kLd + 2 * c + 1] = acc[0][3] + acc[1][3];
+    } else {
+        pdl_wait();
+        delta_rows<C::NT, C::kLd>(p, corrbuf, (warp - C::kDeltaWarp0) * 32 + lane, rt, kb_begin, kb_end);
+    }
+    __syncthreads();
+    if (s_abort) {
+        if (warp == C::kProducerWarp && lane == 0)
+            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+        return;
+    }
+    pdl_wait();
+    epilogue_tile<C::NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
+}
+
+// ---------------------------------------------------------------- k_ctarq_tc (9..32 tokens)
+
+template <int NT>
+struct TcCfg {
+    static constexpr int kDqWarps = 8;               // two per TMEM sub-partition, one 16-row tile each
+    static constexpr int kProducerWarp = 8;
+    static constexpr int kMmaWarp = 9;
+    static constexpr int kDeltaWarp0 = 10;
+    static constexpr int kThreads = 14 * 32;
+    static constexpr int G = NT / 8;
+    static constexpr int SKB = 4;
+    static constexpr int kWBytes = SKB * 4096;
+    static constexpr int kXBytes = SKB * G * 1024;
+    static constexpr int kStageBytes = kWBytes + kXBytes;
+    static constexpr int S = NT == 16 ? 7 : 5;
+    static constexpr int kAB = 4;                    // TMEM A buffers, one 64-column block (32 cols) each
+    static constexpr int kLd = NT + 1;
+    static constexpr int kAccOff = S * kStageBytes;
+    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
+    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
+    static constexpr int kNumBars = 2 * S + 2 * kAB + 1;
+    static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+    static constexpr int kTotal = kTmemSlotOff + 16;
+    static constexpr uint32_t kTmemCols = 256;       // D in [0, 32), A buffers in [32, 160)
+    static_assert(NT == 16 || NT == 32, "token tile");
+    static_assert(kTotal <= 227 * 1024, "shared memory");
+};
+
+template <int NT>
+__global__ void __launch_bounds__(TcCfg<NT>::kThreads, 1) k_ctarq_tc(TCParams p) {
+    using C = TcCfg<NT>;
+    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
+    float* corrbuf = reinterpret_cast<float*>(smem + C::kCorrOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* empty = full + S;
+    uint64_t* a_full = empty + S;
+    uint64_t* a_empty = a_full + AB;
+    uint64_t* done = a_empty + AB;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
+    __shared__ int s_last;
+    __shared__ int s_abort;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t rt = blockIdx.x / p.ksplit;
+    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
+    const int64_t kb_begin = (p.KB * split) / p.ksplit;
+    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
+    const int nkb = static_cast<int>(kb_end - kb_begin);
+    const int greal = (p.ntok + 7) >> 3;
+
+    pdl_launch_dependents();
+    // Padding token groups of the N tile must read as zero: clear the activation part of every
+    // stage once (bulk copies only write the real groups), plus the accumulator and dW tiles.
+    for (int i = tid; i < S * (C::kXBytes / 16); i += C::kThreads) {
+        const int st = i / (C::kXBytes / 16), off = i - st * (C::kXBytes / 16);
+        reinterpret_cast<uint4*>(smem + st * C::kStageBytes + C::kWBytes)[off] = make_uint4(0, 0, 0, 0);
+    }
+    for (int i = tid; i < 2 * 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
+    fence_proxy_async_smem();
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 2);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < AB; ++i) {
+            mbar_init(&a_full[i], C::kDqWarps);
+            mbar_init(&a_empty[i], 1);
+        }
+        mbar_init(done, 1);
+        fence_mbar_init();
+        s_abort = 0;
+    }
+    if (warp == C::kMmaWarp) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    int issued = 0;
+    if (warp == C::kProducerWarp) {
+        if (lane == 0)
+            issued = producer_run<SKB, S, C::G, C::kWBytes, C::kStageBytes>(p, smem, full, empty, rt, kb_begin, kb_end,
+                                                                           greal, &s_abort);
+    } else if (warp == C::kMmaWarp) {
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16_f32(128, NT);
+            for (int j = 0; j < nkb; ++j) {
+                const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
+                if (kbl == 0 && !mbar_wait(&full[slot], (s / S) & 1, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                if (!mbar_wait(&a_full[b], (j / AB) & 1, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const unsigned char* xs = smem + slot * C::kStageBytes + C::kWBytes + kbl * C::G * 1024;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    tc_mma_ts(tmem, tmem + 32 + b * 32 + i * 8, desc_kmajor(xs + 2 * i * 128, 128, 1024), idesc,
+                              (j | i) ? 1u : 0u);
+                tc_commit(&a_empty[b]);
+                if (kbl == SKB - 1 || j == nkb - 1) tc_commit(&empty[slot]);
+            }
+            tc_commit(done);  // also after an abort, so that the TMEM can be released
+        }
+    } else if (warp < C::kDqWarps) {
+        const int sp = warp & 3, q = warp >> 2;
+        const int tile = 2 * sp + q;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * sp + 16 * q) << 16;
+        for (int j = 0; j < nkb; ++j) {
+            const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
+            bool ok = true;
+            if (kbl == 0 && !mbar_wait(&full[slot], (s / S) & 1, p.status)) ok = false;
+            if (ok && j >= AB && !mbar_wait(&a_empty[b], ((j / AB) - 1) & 1, p.status)) ok = false;
+            if (!ok) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint4 wv =
+                *reinterpret_cast<const uint4*>(smem + slot * C::kStageBytes + kbl * 4096 + tile * 512 + lane * 16);
+            const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+                uint32_t h[4];
+                dequant_word(words[st], h);
+                tc_st_16x256b(tmem + lane_addr + 32 + b * 32 + st * 8, h[0], h[2], h[1], h[3]);
+            }
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[b]);
+        }
+        // accumulators -> shared tile: warp q of sub-partition sp reads token columns q*8.., q*8+16..
+        if (mbar_wait(done, 0, p.status)) {
+            tc_fence_after();
+            const uint32_t lane_rows = static_cast<uint32_t>(32 * sp) << 16;
+            const int rl = 32 * sp + lane;
+#pragma unroll
+            for (int cb = q; cb < NT / 8; cb += 2) {
+                uint32_t d[8];
+                tc_ld8(tmem + lane_rows + cb * 8, d);
+                tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) accbuf[rl * C::kLd + cb * 8 + i] = __uint_as_float(d[i]);
+            }
+        } else {
+            s_abort = 1;
+        }
+        tc_fence_before();
+    } else {
+        pdl_wait();
+        delta_rows<NT, C::kLd>(p, corrbuf, (warp - C::kDeltaWarp0) * 32 + lane, rt, kb_begin, kb_end);
+    }
+    __syncthreads();
+    if (warp == C::kMmaWarp) {
+        // every tcgen05 operation of this CTA has completed (done observed, loads waited)
+        if (s_abort) mbar_wait(done, 0, nullptr, kDrainNs);
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+    if (s_abort) {
+        if (warp == C::kProducerWarp && lane == 0)
+            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+        return;
+    }
+    pdl_wait();
+    epilogue_tile<NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
+}
+
+// ---------------------------------------------------------------- k_ctarq_fused (<= 8 tokens, router fused)
+
+// The decode kernel with the router folded in.  Four auxiliary warps stage this CTA's column
+// slice of every token into shared memory as K-major core matrices (bf16 rounded to f16) while
+// summing x, x^2 and |x| in f32, finish the sums over the rest of each row, and decide the
+// route of each token (route_token, with the band widened by the bound on their own f32
+// summation error, so the decision is still the reference's).  dW comes from a per-CTA block
+// prepared at load time and fetched with one bulk copy.  CTA 0 publishes the mask and the
+// routed-token list.  The ring carries weights only, so the producer never waits on the
+// previous kernel; one launch per call.
+struct FusedParams {
+    TCParams t;
+    const void* x;
+    int x_dtype;
+    int64_t x_stride;   // elements between tokens of x
+    int64_t x_col0;     // column of x where this layer's slice starts (rows shards)
+    int64_t Kfull;      // values per token used by the router
+    float t4, t8;
+    uint8_t* mask_out;
+    int32_t* ridx_out;
+    int32_t* nrouted_out;
+    const uint8_t* dwblk;   // blocked dW (null: read the CSR)
+    const uint32_t* dwoff;
+};
+
+struct FusedCfg {
+    static constexpr int kMmaWarps = 8;
+    static constexpr int kProducerWarp = 8;
+    static constexpr int kAuxWarp0 = 9;
+    static constexpr int kAuxThreads = 128;
+    static constexpr int kThreads = 13 * 32;
+    static constexpr int NT = 8;
+    static constexpr int SKB = 6;
+    static constexpr int S = 4;
+    static constexpr int kStageBytes = SKB * 4096;   // weights only
+    static constexpr int kMaxKb = 64;                // 64-column blocks of x held per CTA
+    static constexpr int kLd = NT + 1;
+    static constexpr int kXsOff = S * kStageBytes;
+    static constexpr int kDwOff = kXsOff + kMaxKb * 1024;
+    static constexpr int kAccOff = kDwOff + static_cast<int>(kDwBlockMax);
+    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
+    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
+    static constexpr int kTotal = kBarOff + (2 * S + 2) * 8 + 16;
+    static_assert(kTotal <= 227 * 1024, "shared memory");
+};
+
+__global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedParams fp) {
+    using C = FusedCfg;
+    constexpr int SKB = C::SKB, S = C::S;
+    const TCParams& p = fp.t;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    unsigned char* xs = smem + C::kXsOff;
+    unsigned char* dws = smem + C::kDwOff;
+    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
+    float* corrbuf = reinterpret_cast<float*>(smem + C::kCorrOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* empty = full + S;
+    uint64_t* x_ready = empty + S;
+    uint64_t* dw_ready = x_ready + 1;
+    __shared__ int s_last;
+    __shared__ int s_abort;
+    __shared__ unsigned s_mask;
+    __shared__ double s_red[3][C::NT][4];
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t rt = blockIdx.x / p.ksplit;
+    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
+    const int64_t kb_begin = (p.KB * split) / p.ksplit;
+    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
+    const int nkb = static_cast<int>(kb_end - kb_begin);
+    const int nst = (nkb + SKB - 1) / SKB;
+    const bool use_blk = fp.dwblk != nullptr && p.nnz > 0;
+
+    pdl_launch_dependents();
+    for (int i = tid; i < 2 * 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;  // acc and dW tiles
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], C::kMmaWarps);
+        }
+        mbar_init(x_ready, 4);
+        mbar_init(dw_ready, 1);
+        fence_mbar_init();
+        s_abort = 0;
+        s_mask = 0u;
+    }
+    __syncthreads();
+
+    int issued = 0;
+    if (warp == C::kProducerWarp) {
+        if (lane == 0) {
+            // weights and dW are read-only: no dependency on the previous kernel
+            const uint64_t pol = policy_evict_first();
+            const int pre = nst < S ? nst : S;
+            for (int it = 0; it < pre; ++it, ++issued) {
+                const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
+                const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
+                mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
+                bulk_g2s_stream(smem + it * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
+                                static_cast<uint32_t>(n * 4096), &full[it], pol);
+            }
+            if (use_blk) {
+                const uint32_t o0 = fp.dwoff[blockIdx.x], o1 = fp.dwoff[blockIdx.x + 1];
+                mbar_arrive_expect_tx(dw_ready, o1 - o0);
+                bulk_g2s(dws, fp.dwblk + o0, o1 - o0, dw_ready);
+            }
+            for (int it = pre; it < nst; ++it, ++issued) {
+                const int slot = it % S;
+                const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
+                const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
+                if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * 4096));
+                bulk_g2s_stream(smem + slot * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
+                                static_cast<uint32_t>(n * 4096), &full[slot], pol);
+            }
+        }
+    } else if (warp < C::kMmaWarps) {
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int g = lane >> 2, c = lane & 3;
+        const bool has_tok = g < p.ntok;
+        const int xoff = g * 16 + (c & 1) * 8 + (c >> 1) * 128;
+        if (!mbar_wait(x_ready, 0, p.status)) s_abort = 1;
+        for (int it = 0; it < nst && !s_abort; ++it) {
+            const int slot = it % S;
+            if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
+                s_abort = 1;
+                break;
+            }
+            const int n = static_cast<int>(imin64(SKB, kb_end - (kb_begin + static_cast<int64_t>(it) * SKB)));
+            const unsigned char* st = smem + slot * C::kStageBytes;
+            const unsigned char* xk0 = xs + (it * SKB) * 1024 + xoff;
+#pragma unroll
+            for (int j = 0; j < SKB; ++j) {
+                if (j < n) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(st + j * 4096 + warp * 512 + lane * 16);
+                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        uint2 b = make_uint2(0u, 0u);
+                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * 1024 + s * 256);
+                        uint32_t a[4];
+                        dequant_word(words[s], a);
+                        mma_16816(acc[s & 1], a, b.x, b.y);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        const int r0 = warp * 16 + g;
+        accbuf[r0 * C::kLd + 2 * c] = acc[0][0] + acc[1][0];
+        accbuf[r0 * C::kLd + 2 * c + 1] = acc[0][1] + acc[1][1];
+        accbuf[(r0 + 8) * C::kLd + 2 * c] = acc[0][2] + acc[1][2];
+        accbuf[(r0 + 8) * C::kLd + 2 * c + 1] = acc[0][3] + acc[1][3];
+    } else {
+        const int wi = warp - C::kAuxWarp0;      // 0..3
+        const int at = tid - C::kAuxWarp0 * 32;  // 0..127
+        pdl_wait();
+        const int64_t slice0 = fp.x_col0 + kb_begin * 64;             // first staged column of x
+        const int64_t slice1 = fp.x_col0 + imin64(kb_end * 64, p.K);  // end of its real columns
+        const bool vec = fp.x_dtype == SC_F16 && ((reinterpret_cast<uintptr_t>(fp.x) | (fp.x_stride * 2)) & 15) == 0 &&
+                         (fp.x_col0 & 7) == 0;
+        const int nin = nkb * 8;                                        // staged 8-column chunks
+        const int64_t nch = fp.Kfull / 8;                               // chunks of a routing row
+        const int64_t in0 = slice0 / 8, in1 = (slice1 + 7) / 8;
+        auto load8 = [&](int t, int64_t colx, uint16_t (&h)[8]) {
+            const int64_t base = (p.tok0 + t) * fp.x_stride + colx;
+            if (vec) {
+                *reinterpret_cast<uint4*>(h) = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(fp.x) + base));
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) h[e] = x_f16_bits(fp.x, fp.x_dtype, base + e);
+            }
+        };
+        auto reduce_store = [&](int t, float a1, float a2, float a3, bool add) {
+            double d1 = a1, d2 = a2, d3 = a3;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                d1 += __shfl_down_sync(0xffffffffu, d1, o);
+                d2 += __shfl_down_sync(0xffffffffu, d2, o);
+                d3 += __shfl_down_sync(0xffffffffu, d3, o);
+            }
+            if (lane == 0) {
+                if (add) {
+                    s_red[0][t][wi] += d1;
+                    s_red[1][t][wi] += d2;
+                    s_red[2][t][wi] += d3;
+                } else {
+                    s_red[0][t][wi] = d1;
+                    s_red[1][t][wi] = d2;
+                    s_red[2][t][wi] = d3;
+                }
+            }
+        };
+        // pass 1: stage the slice (all 8 token rows; rows >= ntok and columns >= K are zero)
+        for (int t = 0; t < C::NT; ++t) {
+            float a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+            for (int ci = at; ci < nin; ci += C::kAuxThreads) {
+                const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
+                uint16_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                if (t < p.ntok && colx < slice1) {
+                    load8(t, colx, h);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = h2f(h[e]);
+                        a1 += v;
+                        a2 = fmaf(v, v, a2);
+                        a3 += fabsf(v);
+                    }
+                }
+                *reinterpret_cast<uint4*>(xs + (ci >> 3) * 1024 + (ci & 7) * 128 + t * 16) =
+                    *reinterpret_cast<const uint4*>(h);
+            }
+            if (t < p.ntok) reduce_store(t, a1, a2, a3, false);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(x_ready);
+        // pass 2: the rest of each routing row, sums only
+        for (int t = 0; t < p.ntok; ++t) {
+            float a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+            for (int64_t ch = at; ch < nch; ch += C::kAuxThreads) {
+                if (ch >= in0 && ch < in1) continue;
+                uint16_t h[8];
+                load8(t, ch * 8, h);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float v = h2f(h[e]);
+                    a1 += v;
+                    a2 = fmaf(v, v, a2);
+                    a3 += fabsf(v);
+                }
+            }
+            reduce_store(t, a1, a2, a3, true);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (at == 0) {
+            // each thread summed at most T values sequentially in f32 per pass
+            const double T = 8.0 * static_cast<double>((nin + C::kAuxThreads - 1) / C::kAuxThreads +
+                                                       (nch + C::kAuxThreads - 1) / C::kAuxThreads);
+            const double u = 5.9604644775390625e-08;
+            const double gT = 2.0 * T * u / (1.0 - T * u);
+            unsigned m = 0u;
+            for (int t = 0; t < p.ntok; ++t) {
+                const double S1 = s_red[0][t][0] + s_red[0][t][1] + s_red[0][t][2] + s_red[0][t][3];
+                const double S2 = s_red[1][t][0] + s_red[1][t][1] + s_red[1][t][2] + s_red[1][t][3];
+                const double SA = s_red[2][t][0] + s_red[2][t][1] + s_red[2][t][2] + s_red[2][t][3];
+                const void* xrow = static_cast<const unsigned char*>(fp.x) + (p.tok0 + t) * fp.x_stride * 2;
+                const bool r = p.route_all ? true
+                                           : route_token(S1, S2, SA, fp.Kfull, fp.t4, fp.t8, xrow, fp.x_dtype, nullptr,
+                                                         gT * SA, gT * S2);
+                if (r) m |= 1u << t;
+            }
+            s_mask = m;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const unsigned mask = s_mask;
+        if (blockIdx.x == 0 && wi == 0) {
+            for (int t = lane; t < p.ntok; t += 32) {
+                const int r = (mask >> t) & 1u;
+                if (fp.mask_out) fp.mask_out[p.tok0 + t] = static_cast<uint8_t>(r);
+                if (fp.ridx_out && r) fp.ridx_out[__popc(mask & ((1u << t) - 1u))] = static_cast<int32_t>(p.tok0 + t);
+            }
+            if (lane == 0 && fp.nrouted_out) *fp.nrouted_out = __popc(mask);
+        }
+        // dW for the routed tokens, x from the staged copy, entries in column order
+        const int rl = at;
+        const int64_t row = rt * 128 + rl;
+        if (mask != 0u && row < p.N && p.nnz > 0) {
+            float corr[C::NT];
+#pragma unroll
+            for (int t = 0; t < C::NT; ++t) corr[t] = 0.0f;
+            auto add_entry = [&](int64_t cl, int8_t q) {
+                const float v = __fmul_rn(static_cast<float>(q), p.ds);
+                const unsigned char* xp = xs + (cl >> 6) * 1024 + ((cl & 63) >> 3) * 128 + (cl & 7) * 2;
+#pragma unroll
+                for (int t = 0; t < C::NT; ++t)
+                    if ((mask >> t) & 1u)
+                        corr[t] = __fadd_rn(corr[t], __fmul_rn(h2f(*reinterpret_cast<const uint16_t*>(xp + t * 16)), v));
+            };
+            if (use_blk) {
+                if (!mbar_wait(dw_ready, 0, p.status)) {
+                    s_abort = 1;
+                } else {
+                    const uint16_t* roff = reinterpret_cast<const uint16_t*>(dws);
+                    const int n = roff[128];
+                    const uint16_t* bcol = reinterpret_cast<const uint16_t*>(dws + 272);
+                    const int8_t* bval = reinterpret_cast<const int8_t*>(dws + 272 + ((n * 2 + 15) / 16) * 16);
+                    for (int e = roff[rl]; e < roff[rl + 1]; ++e) add_entry(bcol[e], bval[e]);
+                }
+            } else {
+                const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
+                const int64_t e0 = (p.ksplit == 1) ? lo : lower_bound_u16(p.col, lo, hi, kb_begin * 64);
+                const int64_t e1 = (p.ksplit == 1) ? hi : lower_bound_u16(p.col, e0, hi, kb_end * 64);
+                for (int64_t e = e0; e < e1; e += 8) {
+                    const int cnt = static_cast<int>(imin64(8, e1 - e));
+                    int64_t cc[8];
+                    int8_t vv[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        cc[u] = u < cnt ? static_cast<int64_t>(p.col[e + u]) - kb_begin * 64 : 0;
+                        vv[u] = u < cnt ? p.val[e + u] : 0;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (u < cnt) add_entry(cc[u], vv[u]);
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < C::NT; ++t) corrbuf[rl * C::kLd + t] = corr[t];
+        }
+    }
+    __syncthreads();
+    if (s_abort) {
+        if (warp == C::kProducerWarp && lane == 0) {
+            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+            if (use_blk) mbar_wait(dw_ready, 0, nullptr, kDrainNs);
+        }
+        return;
+    }
+    pdl_wait();
+    epilogue_tile<C::NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
+}
+
+// ---------------------------------------------------------------- launchers
+
+template <typename Kern>
+static cudaError_t set_smem_once(Kern kernel, int bytes, std::atomic<uint64_t>& flags) {
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    if (!(attr_set.load() & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode_tc<NG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        attr_set.fetch_or(bit);
-    }
-    k_decode_tc<NG><<<static_cast<unsigned>(RT * p.ksplit), kThreadsTC, smem, s>>>(p);
-    return cudaGetLastError();
+    if (flags.load() & bit) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) flags.fetch_or(bit);
+    return e;
 }
 
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s) {
@@ -319,7 +854,6 @@ cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s) {
     p.N = L.N;
     p.K = L.K;
     p.KB = L.KB;
-    p.NT16 = L.Np / 16;
     p.y = a.y;
     p.y_dtype = a.y_dtype;
     p.bias = a.bias;
@@ -328,22 +862,31 @@ cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s) {
     p.ws_rtcount = a.ws_rtcount;
     p.ksplit = a.ksplit;
     p.status = L.status;
-    const int64_t RT = (L.Np + 127) / 128;
-    const int ng = static_cast<int>((a.ntok + 7) / 8);
-    switch (ng) {
-        case 1: return launch_tc_ng<1>(p, RT, s);
-        case 2: return launch_tc_ng<2>(p, RT, s);
-        case 3:
-        case 4: return launch_tc_ng<4>(p, RT, s);
-        default: return cudaErrorInvalidValue;
+    const dim3 grid(static_cast<unsigned>((L.Np / 128) * p.ksplit));
+    if (a.ntok <= 8) {
+        static std::atomic<uint64_t> f{0};
+        cudaError_t e = set_smem_once(k_ctarq_mma, MmaCfg::kTotal, f);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(k_ctarq_mma, grid, dim3(MmaCfg::kThreads), MmaCfg::kTotal, s, p);
     }
+    if (a.ntok <= 16) {
+        static std::atomic<uint64_t> f{0};
+        cudaError_t e = set_smem_once(k_ctarq_tc<16>, TcCfg<16>::kTotal, f);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(k_ctarq_tc<16>, grid, dim3(TcCfg<16>::kThreads), TcCfg<16>::kTotal, s, p);
+    }
+    if (a.ntok <= 32) {
+        static std::atomic<uint64_t> f{0};
+        cudaError_t e = set_smem_once(k_ctarq_tc<32>, TcCfg<32>::kTotal, f);
+        if (e != cudaSuccess) return e;
+        return launch_pdl(k_ctarq_tc<32>, grid, dim3(TcCfg<32>::kThreads), TcCfg<32>::kTotal, s, p);
+    }
+    return cudaErrorInvalidValue;
 }
 
-// ---------------------------------------------------------------------------------------
-// Exact (reference-order) kernel
+// ---------------------------------------------------------------- exact (reference-order) kernel
 
-constexpr int kExactThreads = 128;  // 16 tiles of 16 rows (8 row pairs each) per CTA
-constexpr int kExactTok = 4;        // tokens per pass over the weights
+constexpr int kExactTok = 2;  // tokens per pass over the weights
 
 struct ExactParams {
     const uint32_t* wq;
@@ -360,7 +903,7 @@ struct ExactParams {
     const uint8_t* mask;
     int route_all;
     int bypass;
-    int64_t N, K, KB, NT16;
+    int64_t N, K, KB;
     void* y;
     int y_dtype;
     const float* bias;
@@ -369,27 +912,40 @@ struct ExactParams {
 
 __device__ __forceinline__ uint16_t half_sel(uint32_t h2, int e) { return e ? hi16(h2) : lo16(h2); }
 
-// Weight (q-8 as f16 bits) of row (g or g+8 by rh) at column offset i (0..15) of a kstep,
-// given the 4 lanes' dequantised registers hq[c][0..3].
-__device__ __forceinline__ uint16_t wq_at(const uint32_t (&hq)[4][4], int rh, int i) {
-    const int hi8 = i >> 3, ii = i & 7;
-    const int c = ii >> 1, e = ii & 1;
-    return half_sel(hq[c][(hi8 ? 2 : 0) + rh], e);
+// q-8 (f16 bits) of element e (0..7) of the reference word `grp` for row g (r = 0) or g+8
+// (r = 1), from the dequantised words of the four lanes c = 0..3 of the kstep holding it.
+__device__ __forceinline__ uint16_t wq_elem(const uint32_t (&hq)[4][4], int half, int e, int r) {
+    const int c = 2 * half + (e >> 2);
+    const int j4 = e & 3;
+    return half_sel(hq[c][(j4 < 2 ? 0 : 2) + r], j4 & 1);
 }
 
-__global__ void __launch_bounds__(kExactThreads) k_decode_exact(ExactParams p) {
-    const int64_t gtid = blockIdx.x * (int64_t)kExactThreads + threadIdx.x;
-    const int64_t tile = gtid >> 3;
-    const int gid = static_cast<int>(gtid & 7);
-    if (tile >= p.NT16) return;
-    const int64_t rowA = tile * 16 + gid, rowB = rowA + 8;
-    const int64_t kw = p.K / 8;  // valid 8-column groups
+__global__ void __launch_bounds__(128) k_decode_exact(ExactParams p) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t gtid = blockIdx.x * 128ll + threadIdx.x;
+    const int64_t rt = gtid >> 6;                  // 64 row pairs per 128-row tile
+    const int tile = static_cast<int>((gtid >> 3) & 7), g = static_cast<int>(gtid & 7);
+    const int64_t rows[2] = {rt * 128 + tile * 16 + g, rt * 128 + tile * 16 + g + 8};
+    if (rt >= p.N / 128 + ((p.N % 128) ? 1 : 0)) return;
+    const int64_t kw = p.K / 8;
     const int Mp = static_cast<int>(p.Mp);
-
+    float s_r[2], lo[2], hi[2];
+    int64_t lo_e[2], hi_e[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const bool in = rows[r] < p.N;
+        s_r[r] = in ? p.scale[rows[r]] : 0.0f;
+        lo_e[r] = (in && p.nnz > 0) ? p.rowptr[rows[r]] : 0;
+        hi_e[r] = (in && p.nnz > 0) ? p.rowptr[rows[r] + 1] : 0;
+        lo[r] = hi[r] = 0.0f;
+    }
+    (void)lo;
+    (void)hi;
     for (int tb = 0; tb < p.ntok; tb += kExactTok) {
         const int nt = min(kExactTok, p.ntok - tb);
         float a[2][4][kExactTok];
-        float accb[2][kExactTok];  // bypass: one accumulator per row (op.rs:39-48)
+        float accb[2][kExactTok];
 #pragma unroll
         for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -398,24 +954,10 @@ __global__ void __launch_bounds__(kExactThreads) k_decode_exact(ExactParams p) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) a[r][j][t] = 0.0f;
             }
-        // bypass merges the dW entries into the dense weight while walking the columns
-        int64_t bp[2] = {0, 0}, bpe[2] = {0, 0};
-        float sc[2] = {0.0f, 0.0f};
-        if (p.bypass) {
-            const int64_t rows[2] = {rowA, rowB};
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                if (rows[r] < p.N) {
-                    sc[r] = p.scale[rows[r]];
-                    if (p.nnz > 0) {
-                        bp[r] = p.rowptr[rows[r]];
-                        bpe[r] = p.rowptr[rows[r] + 1];
-                    }
-                }
-            }
-        }
+        int64_t bp[2] = {lo_e[0], lo_e[1]};
         for (int64_t kb = 0; kb < p.KB; ++kb) {
-            const uint4* src = reinterpret_cast<const uint4*>(p.wq + ((tile * p.KB + kb) * 32 + gid * 4) * 4);
+            // lanes 4g..4g+3 of this tile: 16 words, [c][s]
+            const uint4* src = reinterpret_cast<const uint4*>(p.wq + (rt * p.KB + kb) * 1024 + tile * 128 + g * 16);
             uint32_t w[4][4];
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -427,66 +969,58 @@ __global__ void __launch_bounds__(kExactThreads) k_decode_exact(ExactParams p) {
             }
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
-                const int64_t k0 = kb * 64 + 16 * s;
-                const int64_t grp0 = k0 >> 3;  // groups grp0 (cols k0..k0+7) and grp0+1
+                const int64_t grp0 = kb * 8 + 2 * s;  // reference words grp0 (cols 16s..16s+7) and grp0+1
                 if (grp0 >= kw) break;
-                const bool second = (grp0 + 1) < kw;
                 uint32_t hq[4][4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) dequant_word(w[c][s], hq[c]);
-                if (p.bypass) {
 #pragma unroll
-                    for (int r = 0; r < 2; ++r)
-                        while (bp[r] < bpe[r] && static_cast<int64_t>(p.col[bp[r]]) < k0) ++bp[r];
-                }
+                for (int half = 0; half < 2; ++half) {
+                    const int64_t grp = grp0 + half;
+                    if (grp >= kw) break;
 #pragma unroll
-                for (int t = 0; t < kExactTok; ++t) {
-                    if (t >= nt) break;
-                    const int tok = static_cast<int>(p.tok0 + tb + t);
-                    uint16_t xv[16];
-                    const uint16_t* xr = p.xk + (kb * Mp + tok) * 64;
-                    *reinterpret_cast<uint4*>(&xv[0]) = *reinterpret_cast<const uint4*>(xr + (((2 * s) ^ (tok & 7)) * 8));
-                    *reinterpret_cast<uint4*>(&xv[8]) =
-                        *reinterpret_cast<const uint4*>(xr + (((2 * s + 1) ^ (tok & 7)) * 8));
-                    if (!p.bypass) {
+                    for (int t = 0; t < kExactTok; ++t) {
+                        if (t >= nt) break;
+                        const int tok = static_cast<int>(p.tok0 + tb + t);
+                        uint16_t xv[8];
+                        *reinterpret_cast<uint4*>(xv) = *reinterpret_cast<const uint4*>(p.xk + xk_index(grp * 8, tok, Mp));
+                        if (!p.bypass) {
 #pragma unroll
-                        for (int r = 0; r < 2; ++r) {
+                            for (int r = 0; r < 2; ++r)
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                float v = a[r][j][t];
-                                v = fma_f16_f32(xv[j], wq_at(hq, r, j), v);
-                                v = fma_f16_f32(xv[j + 4], wq_at(hq, r, j + 4), v);
-                                if (second) {
-                                    v = fma_f16_f32(xv[j + 8], wq_at(hq, r, j + 8), v);
-                                    v = fma_f16_f32(xv[j + 12], wq_at(hq, r, j + 12), v);
+                                for (int j = 0; j < 4; ++j) {
+                                    float v = a[r][j][t];
+                                    v = fma_f16_f32(xv[j], wq_elem(hq, half, j, r), v);
+                                    v = fma_f16_f32(xv[j + 4], wq_elem(hq, half, j + 4, r), v);
+                                    a[r][j][t] = v;
                                 }
-                                a[r][j][t] = v;
-                            }
-                        }
-                    } else {
-                        const int lim = second ? 16 : 8;
+                        } else {
 #pragma unroll
-                        for (int r = 0; r < 2; ++r) {
-                            int64_t e = bp[r];  // first dW entry of this row at or after column k0
-                            for (int i = 0; i < lim; ++i) {
-                                const int64_t colg = k0 + i;
-                                float wv = __fmul_rn(h2f(wq_at(hq, r, i)), sc[r]);
-                                while (e < bpe[r] && static_cast<int64_t>(p.col[e]) < colg) ++e;
-                                if (e < bpe[r] && static_cast<int64_t>(p.col[e]) == colg)
-                                    wv = __fadd_rn(wv, __fmul_rn(static_cast<float>(p.val[e]), p.ds));
-                                accb[r][t] = __fadd_rn(accb[r][t], __fmul_rn(h2f(xv[i]), wv));
+                            for (int r = 0; r < 2; ++r) {
+                                int64_t e = bp[r];
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) {
+                                    const int64_t colg = grp * 8 + i;
+                                    float wv = __fmul_rn(h2f(wq_elem(hq, half, i, r)), s_r[r]);
+                                    while (e < hi_e[r] && static_cast<int64_t>(p.col[e]) < colg) ++e;
+                                    if (e < hi_e[r] && static_cast<int64_t>(p.col[e]) == colg)
+                                        wv = __fadd_rn(wv, __fmul_rn(static_cast<float>(p.val[e]), p.ds));
+                                    accb[r][t] = __fadd_rn(accb[r][t], __fmul_rn(h2f(xv[i]), wv));
+                                }
                             }
                         }
+                    }
+                    if (p.bypass) {
+#pragma unroll
+                        for (int r = 0; r < 2; ++r)
+                            while (bp[r] < hi_e[r] && static_cast<int64_t>(p.col[bp[r]]) < (grp + 1) * 8) ++bp[r];
                     }
                 }
             }
         }
-        const int64_t rows[2] = {rowA, rowB};
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             if (rows[r] >= p.N) continue;
-            const float s_r = p.scale[rows[r]];
-            const int64_t lo = p.nnz > 0 ? p.rowptr[rows[r]] : 0, hi = p.nnz > 0 ? p.rowptr[rows[r] + 1] : 0;
             for (int t = 0; t < nt; ++t) {
                 const int64_t tok = p.tok0 + tb + t;
                 float acc;
@@ -494,9 +1028,9 @@ __global__ void __launch_bounds__(kExactThreads) k_decode_exact(ExactParams p) {
                     acc = accb[r][t];
                 } else {
                     acc = __fmul_rn(__fadd_rn(__fadd_rn(__fadd_rn(a[r][0][t], a[r][1][t]), a[r][2][t]), a[r][3][t]),
-                                    s_r);
+                                    s_r[r]);
                     if (p.route_all || p.mask[tok]) {
-                        for (int64_t e = lo; e < hi; ++e) {
+                        for (int64_t e = lo_e[r]; e < hi_e[r]; ++e) {
                             const float dv = __fmul_rn(static_cast<float>(p.val[e]), p.ds);
                             const float xv = h2f(p.xk[xk_index(p.col[e], static_cast<int>(tok), Mp)]);
                             acc = __fadd_rn(acc, __fmul_rn(xv, dv));
@@ -510,6 +1044,55 @@ __global__ void __launch_bounds__(kExactThreads) k_decode_exact(ExactParams p) {
         }
     }
 }
+
+cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
+    const Layer& L = *f.L;
+    FusedParams fp;
+    TCParams& p = fp.t;
+    p.wq = L.wq;
+    p.scale = L.scale;
+    p.rowptr = L.rowptr;
+    p.col = L.col;
+    p.val = L.val;
+    p.ds = L.ds;
+    p.nnz = L.nnz;
+    p.xk = nullptr;
+    p.Mp = 0;
+    p.tok0 = 0;
+    p.ntok = static_cast<int>(f.m);
+    p.mask = nullptr;
+    p.route_all = f.route_all;
+    p.N = L.N;
+    p.K = L.K;
+    p.KB = L.KB;
+    p.y = f.y;
+    p.y_dtype = f.y_dtype;
+    p.bias = f.bias;
+    p.partial_out = f.partial_out;
+    p.ws_partial = f.ws_partial;
+    p.ws_rtcount = f.ws_rtcount;
+    p.ksplit = f.ksplit;
+    p.status = L.status;
+    fp.x = f.x;
+    fp.x_dtype = f.x_dtype;
+    fp.x_stride = f.x_stride;
+    fp.x_col0 = f.x_col0;
+    fp.Kfull = f.x_stride;
+    fp.t4 = L.t4;
+    fp.t8 = L.t8;
+    fp.mask_out = f.mask_out;
+    fp.ridx_out = f.ridx_out;
+    fp.nrouted_out = f.nrouted_out;
+    fp.dwblk = L.dwblk;
+    fp.dwoff = L.dwoff;
+    static std::atomic<uint64_t> flags{0};
+    cudaError_t e = set_smem_once(k_ctarq_fused, FusedCfg::kTotal, flags);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_ctarq_fused, dim3(static_cast<unsigned>((L.Np / 128) * p.ksplit)), dim3(FusedCfg::kThreads),
+                      FusedCfg::kTotal, s, fp);
+}
+
+int fused_max_kb() { return FusedCfg::kMaxKb; }
 
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s) {
     const Layer& L = *a.L;
@@ -531,21 +1114,20 @@ cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s)
     p.N = L.N;
     p.K = L.K;
     p.KB = L.KB;
-    p.NT16 = L.Np / 16;
     p.y = a.y;
     p.y_dtype = a.y_dtype;
     p.bias = a.bias;
     p.partial_out = a.partial_out;
-    const int64_t threads = p.NT16 * 8;
-    const int64_t blocks = (threads + kExactThreads - 1) / kExactThreads;
-    k_decode_exact<<<static_cast<unsigned>(blocks), kExactThreads, 0, s>>>(p);
-    return cudaGetLastError();
+    const int64_t threads = (L.Np / 128) * 64;  // one per row pair
+    return launch_pdl(k_decode_exact, dim3(static_cast<unsigned>((threads + 127) / 128)), dim3(128), 0, s, p);
 }
 
-// ---------------------------------------------------------------------------------------
+// ---------------------------------------------------------------- finalize
 
 __global__ void k_finalize(const float* __restrict__ acc, int64_t total, int64_t n, void* y, int y_dtype,
                            const float* bias) {
+    pdl_launch_dependents();
+    pdl_wait();
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
         store_output(y, y_dtype, i, acc[i], bias, i % n);
 }
@@ -556,8 +1138,8 @@ cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int
     if (total == 0) return cudaSuccess;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    k_finalize<<<static_cast<unsigned>(blocks), 256, 0, s>>>(acc, total, n, y, y_dtype, bias);
-    return cudaGetLastError();
+    return launch_pdl(k_finalize, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s, acc, total, n, y, y_dtype,
+                      bias);
 }
 
 }  // namespace sc

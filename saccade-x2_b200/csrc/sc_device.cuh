@@ -1,8 +1,8 @@
 // sc_device.cuh -- device-side helpers shared by the C-TARQ kernels (sm_100a).
 //
-// PTX wrappers for mbarriers, non-multicast bulk copies and the register-level
-// tensor-core MMA, the 4-bit -> f16 nibble conversion of the fragment-tiled
-// weight layout, and the bounded waits every spin in this library goes through.
+// PTX wrappers for mbarriers, non-multicast bulk copies and the tcgen05 tensor-core
+// instructions (TMEM alloc/st/ld, MMA with A in tensor memory), the 4-bit -> f16 nibble
+// conversion of the device weight layout, and the bounded waits every spin goes through.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -118,11 +118,14 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
     return d;
 }
 
-// One packed u32 of the fragment-tiled layout -> the four half2 registers of an
-// m16n8k16 A fragment, each element the exact integer q - 8.
-//   nibble p (bits 4p..4p+3) holds row (p&1 ? g+8 : g), column 2c + ((p>>1)&1)*8 + (p>>2)
-//   h[0] = {(g,2c),(g,2c+1)}  h[1] = {(g+8,2c),(g+8,2c+1)}
-//   h[2] = {(g,2c+8),(g,2c+9)}  h[3] = {(g+8,2c+8),(g+8,2c+9)}
+// One packed u32 of the device layout -> four half2 registers holding exact integers q - 8.
+// The word belongs to lane (g, c) of a 16-row tile and one 16-column step at k0:
+//   nibble p holds row g + (p & 1) * 8, column k0 + 4c + ((p >> 1) & 1) * 2 + (p >> 2), so
+//   h[0] = row g    {4c, 4c+1}     h[1] = row g+8  {4c, 4c+1}
+//   h[2] = row g    {4c+2, 4c+3}   h[3] = row g+8  {4c+2, 4c+3}
+// {h0,h1,h2,h3} is the A fragment of mma.m16n8k16 when the step's K order is permuted so
+// that fragment columns {2c, 2c+1 | 2c+8, 2c+9} mean K {4c, 4c+1 | 4c+2, 4c+3}; {h0,h2,h1,h3}
+// is the register set of tcgen05.st.16x256b (TMEM lanes g and g+8, columns 2c and 2c+1).
 // OR-ing a nibble into the mantissa of half 1024 gives 1024+n (low nibble of each half)
 // or 1024+16n (second nibble); one subtract / one fma maps both to n-8 exactly.
 __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t (&h)[4]) {
@@ -167,13 +170,91 @@ __device__ __forceinline__ uint16_t hi16(uint32_t v) { return static_cast<uint16
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 // Index (in halves) of element (token t, column col) of the staged activation layout
-// xk[KB][Mp][64]: within each 64-column block, 16-byte chunks are XOR-swizzled by t%8
-// so that the 8 tokens x 4 column pairs of an MMA B fragment hit 32 distinct banks.
+// xk[KB][Mp/8][8 chunks][8 tokens][8 halves]: for each 64-column block and group of 8
+// tokens, 8 "core matrices" of 8 tokens x 8 columns (128 B each), which is the canonical
+// K-major, unswizzled operand layout of tcgen05.mma (LBO 128 B between column chunks,
+// SBO 1 KB between token groups).
 __device__ __forceinline__ int64_t xk_index(int64_t col, int t, int Mp) {
     const int64_t kb = col >> 6;
-    const int within = static_cast<int>(col & 63);
-    const int chunk = (within >> 3) ^ (t & 7);
-    return (kb * Mp + t) * 64 + chunk * 8 + (within & 7);
+    const int chunk = static_cast<int>((col & 63) >> 3);
+    return ((kb * (Mp >> 3) + (t >> 3)) * 8 + chunk) * 64 + (t & 7) * 8 + (col & 7);
+}
+
+// ---------------------------------------------------------------- tcgen05 (5th-gen tensor core)
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive 32-bit columns, one row per thread of the warp.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+// 16 lanes x 256 bits: thread (g = lane/4, c = lane%4) writes TMEM lanes base+g (r0, r1 at
+// columns 2c, 2c+1) and base+g+8 (r2, r3 at columns 2c, 2c+1).
+__device__ __forceinline__ void tc_st_16x256b(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+
+// D[128 x N] (+)= A[128 x 16] (TMEM, f16) * B[16 x N] (shared memory, f16), f32 accumulation.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8 rows x 16 B,
+// `lbo` bytes between the two core matrices along K, `sbo` bytes between 8-row groups.
+__device__ __forceinline__ uint64_t desc_kmajor(const void* smem_ptr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = static_cast<uint64_t>((smem_u32(smem_ptr) >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
+    return d;
+}
+// Instruction descriptor of kind::f16: f16 A and B, f32 D, both K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint16_t f32_to_f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
@@ -201,6 +282,75 @@ __device__ __forceinline__ void store_output(void* y, int y_dtype, int64_t idx, 
     } else {
         reinterpret_cast<float*>(y)[idx] = v;
     }
+}
+
+
+// ---------------------------------------------------------------- router decision
+
+// op.rs:69-72: (score >= t4 && score < t8) || score >= t8; both flags select the dW.
+__device__ __forceinline__ bool route_rule_f32(float score, float t4, float t8) {
+    return (score >= t4 && score < t8) || (score >= t8);
+}
+__device__ __forceinline__ bool route_rule_f64(double score, float t4, float t8) {
+    const double a = t4, b = t8;
+    return (score >= a && score < b) || (score >= b);
+}
+
+// The token's value i as f16 bits (bf16 inputs are rounded to f16 first, as the caller's
+// to_dtype(F16) does at model.rs:58-61).
+__device__ __forceinline__ uint16_t x_f16_bits(const void* x, int x_dtype, int64_t i) {
+    if (x_dtype == SC_BF16)
+        return f32_to_f16_bits(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]));
+    return reinterpret_cast<const uint16_t*>(x)[i];
+}
+
+// Replays heuristics.rs:3-14 exactly on one token: f16 -> f32, sequential f32 sums, f32 divide.
+static __device__ __noinline__ float exact_variance(const void* xrow, int x_dtype, int64_t Kfull) {
+    float sum = 0.0f, sq = 0.0f;
+    for (int64_t i = 0; i < Kfull; ++i) {
+        const float v = h2f(x_f16_bits(xrow, x_dtype, i));
+        sum = __fadd_rn(sum, v);
+        sq = __fadd_rn(sq, __fmul_rn(v, v));
+    }
+    const float hd = static_cast<float>(Kfull);
+    const float mean = __fdiv_rn(sum, hd);
+    return __fsub_rn(__fdiv_rn(sq, hd), __fmul_rn(mean, mean));
+}
+
+// Routing decision of one token from (near-)exact f64 sums of x, x^2 and |x| over Kfull
+// values.  The reference decides on a sequentially summed f32 variance; the standard bound
+// |fl(sum) - sum| <= gamma_{k-1} * sum|terms| (gamma_n = n*u/(1-n*u), u = 2^-24), carried
+// through the mean, the square and the subtraction and doubled for safety, says how far that
+// f32 score can be from the f64 one.  If both thresholds lie farther away the f64 decision
+// is the reference's; otherwise the exact f32 chain is replayed for this token.
+//
+// S1, S2, SA may themselves carry a summation error: E1x, E2x bound |S1 - sum x| and
+// |S2 - sum x^2| (0 for exact sums); they widen the band accordingly.
+__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, float t4, float t8,
+                                            const void* xrow, int x_dtype, float* score_out, double E1x = 0.0,
+                                            double E2x = 0.0) {
+    const double n = static_cast<double>(Kfull);
+    const double u = 5.9604644775390625e-08;  // 2^-24
+    const double nu = (n - 1.0) * u;
+    const double gam = nu / (1.0 - nu);
+    const double E1 = gam * (SA + E1x) + E1x, E2 = gam * (S2 + E2x) + E2x;
+    const double mean = S1 / n, A = S2 / n;
+    const double errMean = E1 / n + u * (fabs(S1) + E1) / n;
+    const double errA = E2 / n + u * (S2 + E2) / n;
+    const double am = fabs(mean) + errMean;
+    const double errSq = errMean * (2.0 * fabs(mean) + errMean) + u * am * am;
+    const double var = A - mean * mean;
+    double B = errA + errSq + u * (fabs(var) + errA + errSq);
+    B = 2.0 * B + 1e-37;
+    const double d4 = fabs(var - static_cast<double>(t4));
+    const double d8 = fabs(var - static_cast<double>(t8));
+    if (isfinite(var) && isfinite(B) && !(d4 <= B) && !(d8 <= B)) {
+        if (score_out) *score_out = static_cast<float>(var);
+        return route_rule_f64(var, t4, t8);
+    }
+    const float score = exact_variance(xrow, x_dtype, Kfull);
+    if (score_out) *score_out = score;
+    return route_rule_f32(score, t4, t8);
 }
 
 }  // namespace sc

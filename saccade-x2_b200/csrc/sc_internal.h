@@ -15,20 +15,20 @@ enum : uint32_t { DEV_OK = 0, DEV_TIMEOUT = 1, DEV_BAD_INDEX = 2 };
 
 // Device layout of one C-TARQ layer (immutable after sc_layer_create).
 //
-//  wq      u32 [Np/16][KB][32][4]   fragment-tiled 4-bit base: for 16-row tile t and
-//                                   64-column block kb, lane L = 4g+c holds 4 words (ksteps
-//                                   s = 0..3); word s carries rows g, g+8 and columns
-//                                   64kb+16s+{2c,2c+1,2c+8,2c+9} (nibble map in sc_device.cuh).
-//                                   Padding rows/columns hold nibble 8 (q = 0).
-//  scale   f32 [Np]                 f16 row scale widened (config.rs:96-101); 0 on padding rows.
+//  wq      u32 [Np/128][KB][2][128][4]   4-bit base in 128-row x 64-column blocks (4 KB):
+//                                       chunk c of row r holds columns 64kb+32c .. +31 as
+//                                       four words of 8 columns; nibble p of a word holds
+//                                       column offset (p&3)*2 + (p>>2) (see dequant_word).
+//                                       Padding rows/columns hold nibble 8 (q = 0).
+//  scale   f32 [Np]                     f16 row scale widened (config.rs:96-101); 0 on padding.
 //  rowptr  u32 [N+1], col u16 [nnz+8], val i8 [nnz+16]
-//                                   dW in CSR, columns ascending within a row (compress.rs:89-105).
+//                                       dW in CSR, columns ascending within a row (compress.rs:89-105).
 struct Layer {
     int device = 0;
     int sms = 148;               // multiprocessors of `device`
     int mode = SC_MODE_FAST;
     int64_t N = 0, K = 0;        // this shard's extent
-    int64_t Np = 0, Kp = 0;      // padded to 16 rows / 64 columns
+    int64_t Np = 0, Kp = 0;      // padded to 128 rows / 64 columns
     int64_t KB = 0;              // Kp / 64
     int64_t row_begin = 0, col_begin = 0, fullN = 0, fullK = 0;
     int shard_kind = SC_SHARD_NONE;
@@ -42,7 +42,22 @@ struct Layer {
     int8_t* val = nullptr;
     uint32_t* status = nullptr;  // device status word
     int64_t device_bytes = 0;
+    // dW regrouped for the router-fused decode kernel: one block per (128-row tile, column
+    // split) holding u16 row offsets [129] (padded to 272 B), u16 local columns and i8 values
+    // (each padded to 16 B), so a CTA fetches exactly its entries with one bulk copy.
+    int ks_fused = 1;            // column splits of the fused kernel (fixed per layer)
+    uint8_t* dwblk = nullptr;
+    uint32_t* dwoff = nullptr;   // byte offset of block (rt * ks_fused + split); [RT*ks_fused + 1]
+    int64_t dw_max_block = 0;    // largest block in bytes
 };
+
+// Shared-memory budget of one dW block in the fused decode kernel.
+constexpr int64_t kDwBlockMax = 32 * 1024;
+int fused_ksplit(const Layer& L);
+
+// Completion-counter region at the start of every workspace (see plan_workspace).
+constexpr size_t kCounterBytes = 64 * 1024;
+constexpr int64_t kMaxRowTiles = (kCounterBytes - 256) / 4;   // 128-row tiles per layer
 
 // Per-call workspace carve-up (offsets in bytes from the workspace base).
 struct WsLayout {
@@ -58,6 +73,25 @@ WsLayout plan_workspace(const Layer& L, int64_t m);
 
 void set_error(const std::string& msg);
 sc_status cuda_fail(cudaError_t e, const char* what);
+
+// Launch with programmatic stream serialization (PDL): the kernel may start while the
+// previous kernel on the stream finishes; it must call griddepcontrol.wait before touching
+// anything that kernel writes or reads.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // Kernel launchers (each returns the launch error, if any).
 cudaError_t launch_repack(const uint32_t* packed, int64_t ref_words_per_row, int64_t row0, int64_t word0,
@@ -102,6 +136,29 @@ struct DecodeArgs {
 };
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s);
+
+// Decode with the router fused in (<= 8 tokens): one launch reads x directly.
+struct FusedArgs {
+    const Layer* L;
+    const void* x;
+    int x_dtype;
+    int64_t x_stride;       // elements per token row of x (the router's length)
+    int64_t x_col0;         // first column of this layer's slice within a row
+    int64_t m;
+    int route_all;
+    void* y;
+    int y_dtype;
+    const float* bias;
+    int partial_out;
+    uint8_t* mask_out;
+    int32_t* ridx_out;
+    int32_t* nrouted_out;
+    float* ws_partial;
+    uint32_t* ws_rtcount;
+    int ksplit;
+};
+cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s);
+int fused_max_kb();  // largest column range (in 64-column blocks) one CTA of the fused kernel holds
 
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                             cudaStream_t s);

@@ -2,9 +2,12 @@
 //
 // The reference keeps the 4-bit base as u32 [N, K/8] with element k at bits 4*(k%8) of
 // word k/8 (compress.rs:54-83, read back the same way at op.rs:120-131).  The device
-// layout regroups those nibbles so that one coalesced 16-byte load per lane yields four
-// ready-made tensor-core A fragments (layout described in sc_internal.h).  The numeric
-// content is unchanged: this is a permutation plus padding with q = 0.
+// layout regroups those nibbles into 128-row x 64-column blocks of 4 KB (eight 16-row
+// tiles x 32 lanes x 4 words) so that one 16-byte load per lane yields, per 16-column
+// step, a word holding rows g and g+8 of the lane's tile at columns 4c..4c+3 (g = lane/4,
+// c = lane%4).  That word is an mma.sync A fragment (with the K order permuted inside the
+// step, mirrored by the B fragment) and also a tcgen05.st.16x256b operand (natural K order
+// in TMEM).  The numeric content is unchanged: a permutation plus padding with q = 0.
 #include "sc_device.cuh"
 #include "sc_internal.h"
 
@@ -14,17 +17,19 @@ __global__ void k_repack(const uint32_t* __restrict__ packed, int64_t ref_wpr, i
                          int64_t N, int64_t K, int64_t KB, int64_t total_words, uint32_t* __restrict__ wq) {
     for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w < total_words;
          w += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t tile = w / (KB * 128);
-        const int64_t rem = w - tile * KB * 128;
-        const int64_t kb = rem >> 7;
-        const int r2 = static_cast<int>(rem & 127);
-        const int lane = r2 >> 2, s = r2 & 3;
+        const int64_t rt = w / (KB * 1024);
+        const int64_t rem = w - rt * KB * 1024;
+        const int64_t kb = rem >> 10;
+        const int r2 = static_cast<int>(rem & 1023);
+        const int tile = r2 >> 7, lane = (r2 >> 2) & 31, s = r2 & 3;
         const int g = lane >> 2, c = lane & 3;
+        const int64_t row_g = rt * 128 + tile * 16 + g;
+        const int64_t k0 = kb * 64 + 16 * s + 4 * c;
         uint32_t out = 0;
 #pragma unroll
         for (int p = 0; p < 8; ++p) {
-            const int64_t row = tile * 16 + g + ((p & 1) ? 8 : 0);
-            const int64_t col = kb * 64 + 16 * s + 2 * c + (((p >> 1) & 1) ? 8 : 0) + (p >> 2);
+            const int64_t row = row_g + (p & 1) * 8;
+            const int64_t col = k0 + ((p >> 1) & 1) * 2 + (p >> 2);
             uint32_t nib = 8u;
             if (row < N && col < K) {
                 const uint32_t word = packed[(row0 + row) * ref_wpr + word0 + (col >> 3)];
@@ -44,7 +49,7 @@ __global__ void k_scales(const uint16_t* __restrict__ scale_f16, int64_t row0, i
 
 cudaError_t launch_repack(const uint32_t* packed, int64_t ref_words_per_row, int64_t row0, int64_t word0,
                           const Layer& L, cudaStream_t s) {
-    const int64_t total = (L.Np / 16) * L.KB * 128;
+    const int64_t total = L.Np * L.KB * 8;
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads;
     k_repack<<<static_cast<unsigned>(blocks < 65535 * 16 ? blocks : 65535 * 16), threads, 0, s>>>(

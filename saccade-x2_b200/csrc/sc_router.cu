@@ -16,39 +16,13 @@
 //
 // The last CTA to finish (completion counter in the workspace) compacts the mask into
 // the ascending routed-token list and resets the counter for the next call.
+//
+// The staged layout xk is the tcgen05 K-major core-matrix layout of sc_device.cuh:
+// xk_index, with tokens padded to a multiple of 16 (the MMA N granularity).
 #include "sc_device.cuh"
 #include "sc_internal.h"
 
 namespace sc {
-
-__device__ __forceinline__ bool route_rule_f32(float score, float t4, float t8) {
-    // op.rs:69-72: (score >= t4 && score < t8) || score >= t8; both flags select the dW.
-    return (score >= t4 && score < t8) || (score >= t8);
-}
-
-__device__ __forceinline__ bool route_rule_f64(double score, float t4, float t8) {
-    const double a = t4, b = t8;
-    return (score >= a && score < b) || (score >= b);
-}
-
-// Replays heuristics.rs:3-14 exactly: f16 -> f32, sequential f32 sums, f32 divide.
-__device__ float exact_variance(const void* x, int x_dtype, int64_t row_off, int64_t Kfull) {
-    float sum = 0.0f, sq = 0.0f;
-    for (int64_t i = 0; i < Kfull; ++i) {
-        float v;
-        if (x_dtype == SC_BF16) {
-            const __nv_bfloat16 b = reinterpret_cast<const __nv_bfloat16*>(x)[row_off + i];
-            v = __half2float(__float2half_rn(__bfloat162float(b)));
-        } else {
-            v = __half2float(reinterpret_cast<const __half*>(x)[row_off + i]);
-        }
-        sum = __fadd_rn(sum, v);
-        sq = __fadd_rn(sq, __fmul_rn(v, v));
-    }
-    const float hd = static_cast<float>(Kfull);
-    const float mean = __fdiv_rn(sum, hd);
-    return __fsub_rn(__fdiv_rn(sq, hd), __fmul_rn(mean, mean));
-}
 
 struct RouterKernelArgs {
     const void* x;
@@ -79,13 +53,16 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
     const int64_t t = blockIdx.x;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
+    // Programmatic dependent launch: let the GEMV start streaming its weights now, but touch
+    // x, xk and the routing outputs only once the previous kernel on the stream is complete.
+    pdl_launch_dependents();
+    pdl_wait();
 
     if (t >= a.M) {
-        // padding tokens of the last 8-token group: zero rows in xk
-        for (int64_t ch = tid; ch < a.KB * 8; ch += kThreads) {
-            const int64_t kb = ch >> 3;
-            *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + (ch & 7) * 8]) = make_uint4(0, 0, 0, 0);
-        }
+        // padding tokens (up to a multiple of 16): zero rows in xk
+        for (int64_t ch = tid; ch < a.KB * 8; ch += kThreads)
+            *reinterpret_cast<uint4*>(&a.xk[xk_index(ch * 8, static_cast<int>(t), static_cast<int>(a.Mp))]) =
+                make_uint4(0, 0, 0, 0);
     } else {
         double s1 = 0.0, s2 = 0.0, sa = 0.0;
         const int64_t row_off = t * a.row_stride;
@@ -120,20 +97,14 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
                 s2 += v * v;
                 sa += fabs(v);
             }
-            if (ch >= ch_lo && ch < ch_hi) {
-                const int64_t lc = ch - ch_lo;
-                const int64_t kb = lc >> 3;
-                const int chunk = static_cast<int>(lc & 7) ^ static_cast<int>(t & 7);
-                *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + chunk * 8]) =
+            if (ch >= ch_lo && ch < ch_hi)
+                *reinterpret_cast<uint4*>(&a.xk[xk_index((ch - ch_lo) * 8, static_cast<int>(t), static_cast<int>(a.Mp))]) =
                     *reinterpret_cast<const uint4*>(h);
-            }
         }
         // zero the padding columns of the staged slice
-        for (int64_t lc = (a.K / 8) + tid; lc < a.KB * 8; lc += kThreads) {
-            const int64_t kb = lc >> 3;
-            const int chunk = static_cast<int>(lc & 7) ^ static_cast<int>(t & 7);
-            *reinterpret_cast<uint4*>(&a.xk[(kb * a.Mp + t) * 64 + chunk * 8]) = make_uint4(0, 0, 0, 0);
-        }
+        for (int64_t lc = (a.K / 8) + tid; lc < a.KB * 8; lc += kThreads)
+            *reinterpret_cast<uint4*>(&a.xk[xk_index(lc * 8, static_cast<int>(t), static_cast<int>(a.Mp))]) =
+                make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             s1 += __shfl_down_sync(0xffffffffu, s1, o);
@@ -153,30 +124,10 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
                 S2 += red[1][w];
                 SA += red[2][w];
             }
-            const double n = static_cast<double>(a.Kfull);
-            const double u = 5.9604644775390625e-08;  // 2^-24
-            const double nu = (n - 1.0) * u;
-            const double gam = nu / (1.0 - nu);
-            const double E1 = gam * SA, E2 = gam * S2;
-            const double mean = S1 / n, A = S2 / n;
-            const double errMean = E1 / n + u * (fabs(S1) + E1) / n;
-            const double errA = E2 / n + u * (S2 + E2) / n;
-            const double errSq = errMean * (2.0 * fabs(mean) + errMean) + u * (fabs(mean) + errMean) * (fabs(mean) + errMean);
-            const double var = A - mean * mean;
-            double B = errA + errSq + u * (fabs(var) + errA + errSq);
-            B = 2.0 * B + 1e-37;
-            const double d4 = fabs(var - static_cast<double>(a.t4));
-            const double d8 = fabs(var - static_cast<double>(a.t8));
-            const bool finite = isfinite(var) && isfinite(B);
-            bool routed;
-            float score;
-            if (finite && !(d4 <= B) && !(d8 <= B)) {
-                routed = route_rule_f64(var, a.t4, a.t8);
-                score = static_cast<float>(var);
-            } else {
-                score = exact_variance(a.x, a.x_dtype, row_off, a.Kfull);
-                routed = route_rule_f32(score, a.t4, a.t8);
-            }
+            float score = 0.0f;
+            bool routed = route_token(S1, S2, SA, a.Kfull, a.t4, a.t8,
+                                      static_cast<const unsigned char*>(a.x) + row_off * (a.x_dtype == SC_F32 ? 4 : 2),
+                                      a.x_dtype, &score);
             if (a.route_all) routed = true;
             a.mask[t] = routed ? 1 : 0;
             if (a.scores) a.scores[t] = score;
@@ -237,8 +188,7 @@ cudaError_t launch_router(const RouterArgs& r, cudaStream_t s) {
     a.nrouted = r.nrouted;
     a.counter = r.counter;
     a.status = r.status;
-    k_router<256><<<static_cast<unsigned>(r.Mp), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(k_router<256>, dim3(static_cast<unsigned>(r.Mp)), dim3(256), 0, s, a);
 }
 
 }  // namespace sc
