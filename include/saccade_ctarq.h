@@ -145,6 +145,26 @@ SC_API sc_status sc_forward_ws(const sc_layer* layer, const void* x, int x_dtype
                         uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* sc_forward_static has no counterpart in the reference.  It is sc_forward without any
+ * allocation: its scratch is a file-scope __device__ array of SC_STATIC_SCRATCH_BYTES inside
+ * this library, one per device, placed when the library's device code is loaded.  It serves
+ * callers that cannot allocate device memory or hand in a workspace on their hot path: a
+ * custom-op shim whose signature carries no workspace (candle's CustomOp1::cuda_fwd), or a
+ * process whose device memory a framework's caching allocator has already reserved, where an
+ * extra cudaMalloc fails or fragments the pool.  It calls no cudaMalloc/cudaFree.
+ *  - Limit: calls whose sc_workspace_size(layer, m) exceeds SC_STATIC_SCRATCH_BYTES (8 MiB;
+ *    enough for m <= 64 on 7B- and 70B-class decoder shapes) are rejected with SC_EINVAL;
+ *    use sc_forward_ws for those.  ROWS shards are rejected as by sc_forward.
+ *  - Each call first zero-fills the array's 64 KiB counter region on the stream.
+ *  - One array per device is shared by every call on that device: calls that overlap on the
+ *    GPU (several streams or host threads) race and corrupt each other's results.
+ *  - The first call on each device looks the array up (cudaGetSymbolAddress, which may load
+ *    the module); make that first call before any stream capture begins. */
+#define SC_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
+SC_API sc_status sc_forward_static(const sc_layer* layer, const void* x, int x_dtype, int64_t m,
+                            void* y, int y_dtype, const float* bias,
+                            uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out, void* stream);
+
 /* Tensor-parallel pieces.  For a ROWS-sharded layer, sc_forward_partial takes the full
  * [m, full_K] input, routes on it, and writes this shard's f32 contribution [m, N] (base times
  * row scale plus the shard's dW columns for routed tokens).  After an all-reduce (sum) of the

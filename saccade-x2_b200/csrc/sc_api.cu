@@ -242,6 +242,38 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
     return SC_OK;
 }
 
+// ------------------------------------------------------------------ static scratch
+
+// Scratch of sc_forward_static.  The module loader places one copy on every device that
+// loads this library's device code, so the call itself allocates nothing.
+static __device__ __align__(256) unsigned char g_static_scratch[SC_STATIC_SCRATCH_BYTES];
+
+constexpr int kStaticMaxDevices = 64;
+static std::mutex g_static_mu;
+static void* g_static_ptr[kStaticMaxDevices] = {};
+
+// Address of the current device's copy of g_static_scratch, looked up on the first call for
+// that device (the caller has made it current) and kept for the life of the process.
+static sc_status static_scratch(int dev, void** out) {
+    if (dev < 0 || dev >= kStaticMaxDevices) {
+        set_error("sc_forward_static: device ordinal " + std::to_string(dev) + " out of range");
+        return SC_EINVAL;
+    }
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "sc_forward_static: cudaGetSymbolAddress");
+        if (!p || (reinterpret_cast<uintptr_t>(p) & 255u) != 0) {
+            set_error("sc_forward_static: static scratch is not 256-byte aligned");
+            return SC_EDEVICE;
+        }
+        g_static_ptr[dev] = p;
+    }
+    *out = g_static_ptr[dev];
+    return SC_OK;
+}
+
 }  // namespace sc
 
 using namespace sc;
@@ -686,6 +718,38 @@ sc_status sc_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dty
     cudaError_t e = launch_finalize(acc, m, n, y, y_dtype, bias, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sc_finalize launch");
     return SC_OK;
+}
+
+sc_status sc_forward_static(const sc_layer* layer, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
+                            const float* bias, uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out,
+                            void* stream) {
+    if (!layer) {
+        set_error("sc_forward_static: null layer");
+        return SC_EINVAL;
+    }
+    if (m <= 0) return m == 0 ? SC_OK : (set_error("sc_forward_static: negative token count"), SC_EINVAL);
+    if (layer->L.shard_kind == SC_SHARD_ROWS) {
+        set_error("sc_forward_static: a ROWS shard produces partial sums; use sc_forward_partial");
+        return SC_EINVAL;
+    }
+    const size_t need = plan_workspace(layer->L, m).total;
+    if (need > static_cast<size_t>(SC_STATIC_SCRATCH_BYTES)) {
+        set_error("sc_forward_static: " + std::to_string(m) + " tokens on this layer need " + std::to_string(need) +
+                  " bytes of scratch, the static array holds " + std::to_string(SC_STATIC_SCRATCH_BYTES) +
+                  "; use sc_forward_ws");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(layer->L.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward_static: set device");
+    void* ws = nullptr;
+    sc_status st = static_scratch(layer->L.device, &ws);
+    if (st != SC_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // the completion counters must start at zero
+    const cudaError_t e = cudaMemsetAsync(ws, 0, kCounterBytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "sc_forward_static: clear counters");
+    return forward_impl(layer->L, x, x_dtype, m, y, y_dtype, bias, mask_out, routed_idx_out, n_routed_out, ws,
+                        static_cast<size_t>(SC_STATIC_SCRATCH_BYTES), s, false);
 }
 
 }  // extern "C"

@@ -90,6 +90,7 @@ SIGNATURES = {
     "sc_workspace_size": (ctypes.c_size_t, [_vp, _i64]),
     "sc_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "sc_forward_ws": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "sc_forward_static": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "sc_forward_partial": (_int, [_vp, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_finalize": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
     "sc_variance_heuristic": (_int, [_vp, _int, _i64, _i64, _vp, _vp]),
