@@ -52,14 +52,22 @@ static int sm_count(int dev) {
 // offset 0, the split-K row-tile counters after it) at offsets that do not depend on the
 // layer or the token count, so one workspace can serve every layer: each call returns the
 // counters it used to zero.  Everything after that region is scratch rewritten per call.
-// Column splits of the router-fused decode kernel: cover the SMs with 128-row tiles times
-// splits, with each CTA's column slice of x fitting its shared-memory copy.
+// Column splits of the router-fused decode kernel.  The splits of one 128-row tile form a
+// thread-block cluster (at most kMaxFusedCluster CTAs) that reduces through distributed
+// shared memory; aim at two CTAs per SM, with each CTA's column slice of x fitting its
+// shared-memory copy.  0 when the layer is too wide for one cluster.
 int fused_ksplit(const Layer& L) {
     const int64_t RT = L.Np / 128;
-    int64_t ks = (static_cast<int64_t>(L.sms) + RT / 2) / RT;
-    ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(32, std::max<int64_t>(1, L.KB / 4))));
-    ks = std::max<int64_t>(ks, (L.KB + fused_max_kb() - 1) / fused_max_kb());
-    return static_cast<int>(ks);
+    const int64_t target = kFusedCtasPerSm * static_cast<int64_t>(L.sms);
+    int64_t ks = (target + RT / 2) / RT;
+    ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(kMaxFusedCluster, std::max<int64_t>(1, L.KB / 2))));
+    ks = std::max<int64_t>(ks, (L.KB + fused_max_kb(1) - 1) / fused_max_kb(1));
+    return ks <= kMaxFusedCluster ? static_cast<int>(ks) : 0;
+}
+
+bool use_fused(const Layer& L, int64_t m) {
+    if (L.mode != SC_MODE_FAST || m > 8 || L.ks_fused <= 0) return false;
+    return (L.KB + L.ks_fused - 1) / L.ks_fused <= fused_max_kb(m);  // the x slice fits the CTA's copy
 }
 
 WsLayout plan_workspace(const Layer& L, int64_t m) {
@@ -85,9 +93,13 @@ WsLayout plan_workspace(const Layer& L, int64_t m) {
     const int64_t target = static_cast<int64_t>(L.sms);
     int64_t ks = (target + RT / 2) / RT;
     ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(32, std::max<int64_t>(1, L.KB / 4))));
-    if (m <= 8) ks = L.ks_fused;
-    w.ksplit = static_cast<int>(ks);
-    w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
+    if (use_fused(L, m)) {
+        w.ksplit = L.ks_fused;  // reduced inside the cluster: no partial buffer
+        w.partial = take(16);
+    } else {
+        w.ksplit = static_cast<int>(ks);
+        w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
+    }
     w.total = off;
     return w;
 }
@@ -156,7 +168,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
     }
     unsigned char* base = static_cast<unsigned char*>(ws);
     const bool bypass_now = g_bypass.load() != 0;
-    if (L.mode == SC_MODE_FAST && m <= 8) {
+    if (use_fused(L, m)) {
         // one launch: router, x staging, base product and dW in the same kernel
         FusedArgs f;
         f.L = &L;
@@ -524,7 +536,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     if (e == cudaSuccess) {
         // dW blocks of the router-fused decode kernel
         L.ks_fused = fused_ksplit(L);
-        const int64_t RT = L.Np / 128, ks = L.ks_fused;
+        const int64_t RT = L.Np / 128, ks = std::max(1, L.ks_fused);
         std::vector<uint32_t> off(RT * ks + 1, 0);
         std::vector<uint8_t> blob;
         int64_t maxb = 0;
@@ -561,7 +573,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
             }
         }
         L.dw_max_block = maxb;
-        if (L.nnz > 0 && maxb <= kDwBlockMax) {
+        if (L.nnz > 0 && L.ks_fused > 0 && maxb <= kDwBlockMax) {
             if ((e = cudaMalloc(&L.dwblk, blob.size())) == cudaSuccess &&
                 (e = cudaMalloc(&L.dwoff, off.size() * 4)) == cudaSuccess &&
                 (e = cudaMemcpy(L.dwblk, blob.data(), blob.size(), cudaMemcpyHostToDevice)) == cudaSuccess)

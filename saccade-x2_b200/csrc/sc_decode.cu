@@ -497,14 +497,19 @@ __global__ void __launch_bounds__(TcCfg<NT>::kThreads, 1) k_ctarq_tc(TCParams p)
 
 // ---------------------------------------------------------------- k_ctarq_fused (<= 8 tokens, router fused)
 
-// The decode kernel with the router folded in.  Four auxiliary warps stage this CTA's column
-// slice of every token into shared memory as K-major core matrices (bf16 rounded to f16) while
-// summing x, x^2 and |x| in f32, finish the sums over the rest of each row, and decide the
-// route of each token (route_token, with the band widened by the bound on their own f32
-// summation error, so the decision is still the reference's).  dW comes from a per-CTA block
-// prepared at load time and fetched with one bulk copy.  CTA 0 publishes the mask and the
-// routed-token list.  The ring carries weights only, so the producer never waits on the
-// previous kernel; one launch per call.
+// The decode kernel with the router folded in.  The ksplit CTAs that share a 128-row tile
+// form a thread-block cluster; each takes a column slice.  Four auxiliary warps stage the
+// slice of every token into shared memory (bf16 rounded to f16) while summing x, x^2 and |x|
+// in f32; each CTA pushes its sums to every CTA of the cluster (st.async into the receiver's
+// shared memory, completing on its mbarrier), so every CTA adds the whole-token sums in rank
+// order -- identical in every cluster -- and takes the reference's routing decision
+// (route_token, with the band widened by the bound on the f32 summation error).  dW comes
+// from a per-CTA block prepared at load time and fetched with one bulk copy; auxiliary thread
+// r owns row r of the tile: it adds that row's dW, scales, and pushes the row to the cluster
+// CTA that owns it, which adds the splits in rank order and writes y.  CTA 0 publishes the
+// mask and the routed-token list.  The ring carries weights only, so the producer never waits
+// on the previous kernel; about 108 KB of shared memory lets two CTAs (of this call and the
+// next) share an SM.  x is staged for NTp = ntok rounded up to a power of two tokens.
 struct FusedParams {
     TCParams t;
     const void* x;
@@ -518,6 +523,7 @@ struct FusedParams {
     int32_t* nrouted_out;
     const uint8_t* dwblk;   // blocked dW (null: read the CSR)
     const uint32_t* dwoff;
+    int ntp;                // staged token rows: 1, 2, 4 or 8
 };
 
 struct FusedCfg {
@@ -527,49 +533,80 @@ struct FusedCfg {
     static constexpr int kAuxThreads = 128;
     static constexpr int kThreads = 13 * 32;
     static constexpr int NT = 8;
-    static constexpr int SKB = 6;
-    static constexpr int S = 4;
+    static constexpr int SKB = 4;
+    static constexpr int S = 3;
     static constexpr int kStageBytes = SKB * 4096;   // weights only
-    static constexpr int kMaxKb = 64;                // 64-column blocks of x held per CTA
+    static constexpr int kXsBytes = 32 * 1024;       // staged x: 32768 / (128 * ntp) column blocks
     static constexpr int kLd = NT + 1;
     static constexpr int kXsOff = S * kStageBytes;
-    static constexpr int kDwOff = kXsOff + kMaxKb * 1024;
+    static constexpr int kDwOff = kXsOff + kXsBytes;
     static constexpr int kAccOff = kDwOff + static_cast<int>(kDwBlockMax);
-    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
-    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
-    static constexpr int kTotal = kBarOff + (2 * S + 2) * 8 + 16;
-    static_assert(kTotal <= 227 * 1024, "shared memory");
+    static constexpr int kStatsOff = kAccOff + 128 * kLd * 4;              // [16 ranks][8 tokens][3] f64
+    static constexpr int kRedOff = kStatsOff + kMaxFusedCluster * NT * 3 * 8;  // [ks][rows of rank][8] f32
+    static constexpr int kRedBytes = (128 + kMaxFusedCluster) * NT * 4;
+    static constexpr int kBarOff = kRedOff + kRedBytes;
+    static constexpr int kTotal = kBarOff + (2 * S + 4) * 8;
+    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
 };
 
-__global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedParams fp) {
+__device__ __forceinline__ uint4 load_x8(const void* x, int x_dtype, bool vec, int64_t base) {
+    if (vec) return __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + base));
+    uint16_t h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = x_f16_bits(x, x_dtype, base + e);
+    return *reinterpret_cast<const uint4*>(h);
+}
+
+__device__ __forceinline__ void sum_x8(uint4 v, float& a1, float& a2, float& a3) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float lo = h2f(lo16(w[q])), hi = h2f(hi16(w[q]));
+        a1 += lo;
+        a2 = fmaf(lo, lo, a2);
+        a3 += fabsf(lo);
+        a1 += hi;
+        a2 = fmaf(hi, hi, a2);
+        a3 += fabsf(hi);
+    }
+}
+
+__global__ void __launch_bounds__(FusedCfg::kThreads, 2) k_ctarq_fused(FusedParams fp) {
     using C = FusedCfg;
-    constexpr int SKB = C::SKB, S = C::S;
+    constexpr int SKB = C::SKB, S = C::S, NT = C::NT;
     const TCParams& p = fp.t;
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* xs = smem + C::kXsOff;
     unsigned char* dws = smem + C::kDwOff;
     float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
-    float* corrbuf = reinterpret_cast<float*>(smem + C::kCorrOff);
+    double* rstats = reinterpret_cast<double*>(smem + C::kStatsOff);
+    float* rbuf = reinterpret_cast<float*>(smem + C::kRedOff);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
     uint64_t* empty = full + S;
     uint64_t* x_ready = empty + S;
     uint64_t* dw_ready = x_ready + 1;
-    __shared__ int s_last;
+    uint64_t* stats_bar = dw_ready + 1;
+    uint64_t* red_bar = stats_bar + 1;
     __shared__ int s_abort;
     __shared__ unsigned s_mask;
-    __shared__ double s_red[3][C::NT][4];
+    __shared__ double s_red[3][NT][4];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t rt = blockIdx.x / p.ksplit;
-    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
-    const int64_t kb_begin = (p.KB * split) / p.ksplit;
-    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
+    const int ks = p.ksplit;
+    const int ntok = p.ntok;
+    const int64_t rt = blockIdx.x / ks;
+    const int split = static_cast<int>(blockIdx.x - rt * ks);   // = cluster rank
+    const int64_t kb_begin = (p.KB * split) / ks;
+    const int64_t kb_end = (p.KB * (split + 1)) / ks;
     const int nkb = static_cast<int>(kb_end - kb_begin);
     const int nst = (nkb + SKB - 1) / SKB;
     const bool use_blk = fp.dwblk != nullptr && p.nnz > 0;
+    const int cs = fp.ntp * 16;       // bytes per staged 8-column chunk (all token rows)
+    const int bs = 8 * cs;            // bytes per staged 64-column block
+    const int rb = (128 * split) / ks, nr = (128 * (split + 1)) / ks - rb;   // rows this CTA writes
 
     pdl_launch_dependents();
-    for (int i = tid; i < 2 * 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;  // acc and dW tiles
+    for (int i = tid; i < 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
@@ -577,11 +614,18 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
         }
         mbar_init(x_ready, 4);
         mbar_init(dw_ready, 1);
+        mbar_init(stats_bar, 1);
+        mbar_init(red_bar, 1);
         fence_mbar_init();
+        if (ks > 1) {
+            mbar_arrive_expect_tx(stats_bar, static_cast<uint32_t>(ks * ntok * 24));
+            mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>(ks * nr * NT * 4));
+        }
         s_abort = 0;
         s_mask = 0u;
     }
     __syncthreads();
+    if (ks > 1) cluster_arrive();  // this CTA's mbarriers are initialised
 
     int issued = 0;
     if (warp == C::kProducerWarp) {
@@ -617,8 +661,8 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
     } else if (warp < C::kMmaWarps) {
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         const int g = lane >> 2, c = lane & 3;
-        const bool has_tok = g < p.ntok;
-        const int xoff = g * 16 + (c & 1) * 8 + (c >> 1) * 128;
+        const bool has_tok = g < ntok;
+        const int xoff = (c >> 1) * cs + g * 16 + (c & 1) * 8;
         if (!mbar_wait(x_ready, 0, p.status)) s_abort = 1;
         for (int it = 0; it < nst && !s_abort; ++it) {
             const int slot = it % S;
@@ -628,7 +672,7 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
             }
             const int n = static_cast<int>(imin64(SKB, kb_end - (kb_begin + static_cast<int64_t>(it) * SKB)));
             const unsigned char* st = smem + slot * C::kStageBytes;
-            const unsigned char* xk0 = xs + (it * SKB) * 1024 + xoff;
+            const unsigned char* xk0 = xs + (it * SKB) * bs + xoff;
 #pragma unroll
             for (int j = 0; j < SKB; ++j) {
                 if (j < n) {
@@ -637,7 +681,7 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         uint2 b = make_uint2(0u, 0u);
-                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * 1024 + s * 256);
+                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * bs + 2 * s * cs);
                         uint32_t a[4];
                         dequant_word(words[s], a);
                         mma_16816(acc[s & 1], a, b.x, b.y);
@@ -652,128 +696,149 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
         accbuf[r0 * C::kLd + 2 * c + 1] = acc[0][1] + acc[1][1];
         accbuf[(r0 + 8) * C::kLd + 2 * c] = acc[0][2] + acc[1][2];
         accbuf[(r0 + 8) * C::kLd + 2 * c + 1] = acc[0][3] + acc[1][3];
-    } else {
-        const int wi = warp - C::kAuxWarp0;      // 0..3
-        const int at = tid - C::kAuxWarp0 * 32;  // 0..127
+    }
+    // auxiliary warps: staging, routing, dW; thread `at` owns row `at` of the tile
+    float corr[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) corr[t] = 0.0f;
+    const int at = tid - C::kAuxWarp0 * 32;
+    if (warp >= C::kAuxWarp0) {
+        const int wi = warp - C::kAuxWarp0;
         pdl_wait();
         const int64_t slice0 = fp.x_col0 + kb_begin * 64;             // first staged column of x
         const int64_t slice1 = fp.x_col0 + imin64(kb_end * 64, p.K);  // end of its real columns
         const bool vec = fp.x_dtype == SC_F16 && ((reinterpret_cast<uintptr_t>(fp.x) | (fp.x_stride * 2)) & 15) == 0 &&
                          (fp.x_col0 & 7) == 0;
         const int nin = nkb * 8;                                        // staged 8-column chunks
-        const int64_t nch = fp.Kfull / 8;                               // chunks of a routing row
-        const int64_t in0 = slice0 / 8, in1 = (slice1 + 7) / 8;
-        auto load8 = [&](int t, int64_t colx, uint16_t (&h)[8]) {
-            const int64_t base = (p.tok0 + t) * fp.x_stride + colx;
-            if (vec) {
-                *reinterpret_cast<uint4*>(h) = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(fp.x) + base));
-            } else {
+        float a1[NT], a2[NT], a3[NT];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) h[e] = x_f16_bits(fp.x, fp.x_dtype, base + e);
-            }
-        };
-        auto reduce_store = [&](int t, float a1, float a2, float a3, bool add) {
-            double d1 = a1, d2 = a2, d3 = a3;
+        for (int t = 0; t < NT; ++t) a1[t] = a2[t] = a3[t] = 0.0f;
+        // pass 1: stage the slice (ntp token rows; rows >= ntok and columns >= K are zero)
+        for (int ci = at; ci < nin; ci += C::kAuxThreads) {
+            const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
+            const bool inb = colx < slice1;
+            unsigned char* dst = xs + ci * cs;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                d1 += __shfl_down_sync(0xffffffffu, d1, o);
-                d2 += __shfl_down_sync(0xffffffffu, d2, o);
-                d3 += __shfl_down_sync(0xffffffffu, d3, o);
+            for (int g4 = 0; g4 < NT; g4 += 4) {
+                if (g4 < fp.ntp) {
+                    uint4 v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        v[u] = make_uint4(0u, 0u, 0u, 0u);
+                        if (g4 + u < ntok && inb)
+                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                        if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                    }
+                }
             }
-            if (lane == 0) {
-                if (add) {
-                    s_red[0][t][wi] += d1;
-                    s_red[1][t][wi] += d2;
-                    s_red[2][t][wi] += d3;
-                } else {
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(x_ready);
+        // pass 2 (rows shards): this CTA's share of the columns outside the layer's slice
+        const int64_t nch = fp.Kfull / 8;
+        const int64_t in0 = fp.x_col0 / 8, in1 = (fp.x_col0 + p.K) / 8;
+        const int64_t nout = nch - (in1 - in0);
+        const int64_t o0 = (nout * split) / ks, o1 = (nout * (split + 1)) / ks;
+        for (int64_t j = o0 + at; j < o1; j += C::kAuxThreads) {
+            const int64_t ch = j < in0 ? j : j + (in1 - in0);
+#pragma unroll
+            for (int g4 = 0; g4 < NT; g4 += 4) {
+                if (g4 < ntok) {
+                    uint4 v[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        v[u] = make_uint4(0u, 0u, 0u, 0u);
+                        if (g4 + u < ntok)
+                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                }
+            }
+        }
+        // block sums of this CTA (f64 from here on)
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            if (t < ntok) {
+                double d1 = a1[t], d2 = a2[t], d3 = a3[t];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    d1 += __shfl_down_sync(0xffffffffu, d1, o);
+                    d2 += __shfl_down_sync(0xffffffffu, d2, o);
+                    d3 += __shfl_down_sync(0xffffffffu, d3, o);
+                }
+                if (lane == 0) {
                     s_red[0][t][wi] = d1;
                     s_red[1][t][wi] = d2;
                     s_red[2][t][wi] = d3;
                 }
             }
-        };
-        // pass 1: stage the slice (all 8 token rows; rows >= ntok and columns >= K are zero)
-        for (int t = 0; t < C::NT; ++t) {
-            float a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-            for (int ci = at; ci < nin; ci += C::kAuxThreads) {
-                const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
-                uint16_t h[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                if (t < p.ntok && colx < slice1) {
-                    load8(t, colx, h);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float v = h2f(h[e]);
-                        a1 += v;
-                        a2 = fmaf(v, v, a2);
-                        a3 += fabsf(v);
-                    }
-                }
-                *reinterpret_cast<uint4*>(xs + (ci >> 3) * 1024 + (ci & 7) * 128 + t * 16) =
-                    *reinterpret_cast<const uint4*>(h);
-            }
-            if (t < p.ntok) reduce_store(t, a1, a2, a3, false);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(x_ready);
-        // pass 2: the rest of each routing row, sums only
-        for (int t = 0; t < p.ntok; ++t) {
-            float a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-            for (int64_t ch = at; ch < nch; ch += C::kAuxThreads) {
-                if (ch >= in0 && ch < in1) continue;
-                uint16_t h[8];
-                load8(t, ch * 8, h);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float v = h2f(h[e]);
-                    a1 += v;
-                    a2 = fmaf(v, v, a2);
-                    a3 += fabsf(v);
-                }
-            }
-            reduce_store(t, a1, a2, a3, true);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (ks > 1) {
+            cluster_wait();  // every mbarrier of the cluster is initialised
+            if (wi == 0 && lane < ks) {
+                // lane r sends this CTA's sums to rank r, into slot [split]
+                const uint32_t dst = dsmem_addr(rstats + split * NT * 3, static_cast<uint32_t>(lane));
+                const uint32_t bar = dsmem_addr(stats_bar, static_cast<uint32_t>(lane));
+                for (int t = 0; t < ntok; ++t)
+                    for (int q = 0; q < 3; ++q)
+                        st_async_f64(dst + (t * 3 + q) * 8,
+                                     ((s_red[q][t][0] + s_red[q][t][1]) + s_red[q][t][2]) + s_red[q][t][3], bar);
+            }
+        } else if (at == 0) {
+            for (int t = 0; t < ntok; ++t)
+                for (int q = 0; q < 3; ++q)
+                    rstats[t * 3 + q] = ((s_red[q][t][0] + s_red[q][t][1]) + s_red[q][t][2]) + s_red[q][t][3];
+        }
         if (at == 0) {
-            // each thread summed at most T values sequentially in f32 per pass
-            const double T = 8.0 * static_cast<double>((nin + C::kAuxThreads - 1) / C::kAuxThreads +
-                                                       (nch + C::kAuxThreads - 1) / C::kAuxThreads);
+            bool ok = ks == 1 || mbar_wait(stats_bar, 0, p.status);
+            // each thread summed at most T values sequentially in f32 (both passes)
+            const int64_t kbmax = (p.KB + ks - 1) / ks;
+            const int64_t omax = (nout + ks - 1) / ks;
+            const double T = 8.0 * static_cast<double>((kbmax * 8 + C::kAuxThreads - 1) / C::kAuxThreads +
+                                                       (omax + C::kAuxThreads - 1) / C::kAuxThreads);
             const double u = 5.9604644775390625e-08;
             const double gT = 2.0 * T * u / (1.0 - T * u);
             unsigned m = 0u;
-            for (int t = 0; t < p.ntok; ++t) {
-                const double S1 = s_red[0][t][0] + s_red[0][t][1] + s_red[0][t][2] + s_red[0][t][3];
-                const double S2 = s_red[1][t][0] + s_red[1][t][1] + s_red[1][t][2] + s_red[1][t][3];
-                const double SA = s_red[2][t][0] + s_red[2][t][1] + s_red[2][t][2] + s_red[2][t][3];
+            for (int t = 0; t < ntok && ok; ++t) {
+                double S1 = 0.0, S2 = 0.0, SA = 0.0;
+                for (int r = 0; r < ks; ++r) {
+                    S1 += rstats[(r * NT + t) * 3 + 0];
+                    S2 += rstats[(r * NT + t) * 3 + 1];
+                    SA += rstats[(r * NT + t) * 3 + 2];
+                }
                 const void* xrow = static_cast<const unsigned char*>(fp.x) + (p.tok0 + t) * fp.x_stride * 2;
                 const bool r = p.route_all ? true
                                            : route_token(S1, S2, SA, fp.Kfull, fp.t4, fp.t8, xrow, fp.x_dtype, nullptr,
                                                          gT * SA, gT * S2);
                 if (r) m |= 1u << t;
             }
+            if (!ok) s_abort = 1;
             s_mask = m;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
         const unsigned mask = s_mask;
         if (blockIdx.x == 0 && wi == 0) {
-            for (int t = lane; t < p.ntok; t += 32) {
+            for (int t = lane; t < ntok; t += 32) {
                 const int r = (mask >> t) & 1u;
                 if (fp.mask_out) fp.mask_out[p.tok0 + t] = static_cast<uint8_t>(r);
                 if (fp.ridx_out && r) fp.ridx_out[__popc(mask & ((1u << t) - 1u))] = static_cast<int32_t>(p.tok0 + t);
             }
             if (lane == 0 && fp.nrouted_out) *fp.nrouted_out = __popc(mask);
         }
-        // dW for the routed tokens, x from the staged copy, entries in column order
-        const int rl = at;
-        const int64_t row = rt * 128 + rl;
+        // dW of this thread's row for the routed tokens, x from the staged copy, column order
+        const int64_t row = rt * 128 + at;
         if (mask != 0u && row < p.N && p.nnz > 0) {
-            float corr[C::NT];
-#pragma unroll
-            for (int t = 0; t < C::NT; ++t) corr[t] = 0.0f;
             auto add_entry = [&](int64_t cl, int8_t q) {
                 const float v = __fmul_rn(static_cast<float>(q), p.ds);
-                const unsigned char* xp = xs + (cl >> 6) * 1024 + ((cl & 63) >> 3) * 128 + (cl & 7) * 2;
+                const unsigned char* xp = xs + ((cl >> 3) * fp.ntp) * 16 + (cl & 7) * 2;
 #pragma unroll
-                for (int t = 0; t < C::NT; ++t)
+                for (int t = 0; t < NT; ++t)
                     if ((mask >> t) & 1u)
                         corr[t] = __fadd_rn(corr[t], __fmul_rn(h2f(*reinterpret_cast<const uint16_t*>(xp + t * 16)), v));
             };
@@ -785,12 +850,12 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
                     const int n = roff[128];
                     const uint16_t* bcol = reinterpret_cast<const uint16_t*>(dws + 272);
                     const int8_t* bval = reinterpret_cast<const int8_t*>(dws + 272 + ((n * 2 + 15) / 16) * 16);
-                    for (int e = roff[rl]; e < roff[rl + 1]; ++e) add_entry(bcol[e], bval[e]);
+                    for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
                 }
             } else {
                 const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
-                const int64_t e0 = (p.ksplit == 1) ? lo : lower_bound_u16(p.col, lo, hi, kb_begin * 64);
-                const int64_t e1 = (p.ksplit == 1) ? hi : lower_bound_u16(p.col, e0, hi, kb_end * 64);
+                const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, kb_begin * 64);
+                const int64_t e1 = (ks == 1) ? hi : lower_bound_u16(p.col, e0, hi, kb_end * 64);
                 for (int64_t e = e0; e < e1; e += 8) {
                     const int cnt = static_cast<int>(imin64(8, e1 - e));
                     int64_t cc[8];
@@ -805,21 +870,60 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 1) k_ctarq_fused(FusedPara
                         if (u < cnt) add_entry(cc[u], vv[u]);
                 }
             }
-#pragma unroll
-            for (int t = 0; t < C::NT; ++t) corrbuf[rl * C::kLd + t] = corr[t];
         }
+    } else if (ks > 1) {
+        __syncwarp();
+        cluster_wait();
     }
     __syncthreads();
-    if (s_abort) {
-        if (warp == C::kProducerWarp && lane == 0) {
-            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
-                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
-            if (use_blk) mbar_wait(dw_ready, 0, nullptr, kDrainNs);
+    if (s_abort && warp == C::kProducerWarp && lane == 0) {
+        for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+            mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+        if (use_blk) mbar_wait(dw_ready, 0, nullptr, kDrainNs);
+    }
+    if (warp < C::kAuxWarp0) return;
+    pdl_wait();
+    // thread `at`: this split's contribution to row `at` (acc * row scale + dW; 0 past N)
+    const int64_t row = rt * 128 + at;
+    const float sc = row < p.N ? p.scale[row] : 0.0f;
+    float v[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;
+    auto store_row = [&](int64_t r, const float* w) {
+        for (int t = 0; t < ntok; ++t) {
+            const int64_t oi = (p.tok0 + t) * p.N + r;
+            if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = w[t];
+            else store_output(p.y, p.y_dtype, oi, w[t], p.bias, r);
         }
+    };
+    if (ks == 1) {
+        if (!s_abort && row < p.N) store_row(row, v);
         return;
     }
-    pdl_wait();
-    epilogue_tile<C::NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
+    {
+        // push the row to its owner: rank o owns rows [128 o / ks, 128 (o+1) / ks)
+        const int o = (at * ks + ks - 1) / 128;
+        const int orb = (128 * o) / ks, onr = (128 * (o + 1)) / ks - orb;
+        const uint32_t dst = dsmem_addr(rbuf + (split * onr + (at - orb)) * NT, static_cast<uint32_t>(o));
+        const uint32_t bar = dsmem_addr(red_bar, static_cast<uint32_t>(o));
+        st_async_v4_f32(dst, v[0], v[1], v[2], v[3], bar);
+        st_async_v4_f32(dst + 16, v[4], v[5], v[6], v[7], bar);
+    }
+    if (at < nr) {
+        // owner: rows rb + at, the splits added in rank order
+        const bool ok = mbar_wait(red_bar, 0, p.status);
+        const int64_t r = rt * 128 + rb + at;
+        if (ok && !s_abort && r < p.N) {
+            float w[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) w[t] = 0.0f;
+            for (int sp = 0; sp < ks; ++sp) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) w[t] = __fadd_rn(w[t], rbuf[(sp * nr + at) * NT + t]);
+            }
+            store_row(r, w);
+        }
+    }
 }
 
 // ---------------------------------------------------------------- launchers
@@ -1085,14 +1189,40 @@ cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
     fp.nrouted_out = f.nrouted_out;
     fp.dwblk = L.dwblk;
     fp.dwoff = L.dwoff;
+    fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
     static std::atomic<uint64_t> flags{0};
-    cudaError_t e = set_smem_once(k_ctarq_fused, FusedCfg::kTotal, flags);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(k_ctarq_fused, dim3(static_cast<unsigned>((L.Np / 128) * p.ksplit)), dim3(FusedCfg::kThreads),
-                      FusedCfg::kTotal, s, fp);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(flags.load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, FusedCfg::kTotal);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e == cudaSuccess)  // two CTAs per SM need the largest shared-memory carveout
+            e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
+        flags.fetch_or(bit);
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((L.Np / 128) * p.ksplit));
+    cfg.blockDim = dim3(FusedCfg::kThreads);
+    cfg.dynamicSmemBytes = FusedCfg::kTotal;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(p.ksplit);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.ksplit > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, k_ctarq_fused, fp);
 }
 
-int fused_max_kb() { return FusedCfg::kMaxKb; }
+int fused_max_kb(int64_t m) {
+    const int ntp = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
+    return FusedCfg::kXsBytes / (128 * ntp);
+}
 
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s) {
     const Layer& L = *a.L;

@@ -78,6 +78,80 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// ---------------------------------------------------------------- thread-block clusters
+// All threads of every CTA of the cluster execute cluster_sync() the same number of times,
+// so it needs no bound: it is a barrier, not a spin.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Shared-memory address of the same object in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ double ld_dsmem_f64(uint32_t addr) {
+    double v;
+    asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(addr) : "memory");
+    return v;
+}
+// Split cluster barrier: every thread of the cluster arrives once and waits once.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Stores into the shared memory of a cluster CTA (addresses from dsmem_addr) that complete
+// their bytes on that CTA's mbarrier `rbar`; the receiver waits on its own mbarrier.
+__device__ __forceinline__ void st_async_f64(uint32_t raddr, double v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f64 [%0], %1, [%2];" ::"r"(raddr), "d"(v),
+                 "r"(rbar)
+                 : "memory");
+}
+__device__ __forceinline__ void st_async_v4_f32(uint32_t raddr, float a, float b, float c, float d, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     raddr),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(rbar)
+                 : "memory");
+}
+// Arrive on an mbarrier of cluster CTA `rank`, releasing this thread's prior writes at
+// cluster scope.
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* local_bar, uint32_t rank) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(dsmem_addr(local_bar, rank))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (for arrivals from other CTAs of the cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                                  uint64_t limit_ns = kWaitNs) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > limit_ns) break;
+    }
+    record_error(status, DEV_TIMEOUT);
+    return false;
+}
+
 // Non-multicast bulk copy global -> this CTA's shared memory, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
@@ -330,13 +404,14 @@ __device__ __forceinline__ bool route_token(double S1, double S2, double SA, int
                                             const void* xrow, int x_dtype, float* score_out, double E1x = 0.0,
                                             double E2x = 0.0) {
     const double n = static_cast<double>(Kfull);
+    const double inv_n = 1.0 / n;  // products with 1/n differ from quotients by f64 ulps, far inside B
     const double u = 5.9604644775390625e-08;  // 2^-24
     const double nu = (n - 1.0) * u;
     const double gam = nu / (1.0 - nu);
     const double E1 = gam * (SA + E1x) + E1x, E2 = gam * (S2 + E2x) + E2x;
-    const double mean = S1 / n, A = S2 / n;
-    const double errMean = E1 / n + u * (fabs(S1) + E1) / n;
-    const double errA = E2 / n + u * (S2 + E2) / n;
+    const double mean = S1 * inv_n, A = S2 * inv_n;
+    const double errMean = (E1 + u * (fabs(S1) + E1)) * inv_n;
+    const double errA = (E2 + u * (S2 + E2)) * inv_n;
     const double am = fabs(mean) + errMean;
     const double errSq = errMean * (2.0 * fabs(mean) + errMean) + u * am * am;
     const double var = A - mean * mean;

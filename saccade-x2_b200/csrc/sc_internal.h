@@ -45,15 +45,24 @@ struct Layer {
     // dW regrouped for the router-fused decode kernel: one block per (128-row tile, column
     // split) holding u16 row offsets [129] (padded to 272 B), u16 local columns and i8 values
     // (each padded to 16 B), so a CTA fetches exactly its entries with one bulk copy.
-    int ks_fused = 1;            // column splits of the fused kernel (fixed per layer)
+    int ks_fused = 0;            // column splits (= cluster size) of the fused kernel; 0: not usable
     uint8_t* dwblk = nullptr;
     uint32_t* dwoff = nullptr;   // byte offset of block (rt * ks_fused + split); [RT*ks_fused + 1]
     int64_t dw_max_block = 0;    // largest block in bytes
 };
 
 // Shared-memory budget of one dW block in the fused decode kernel.
-constexpr int64_t kDwBlockMax = 32 * 1024;
+constexpr int64_t kDwBlockMax = 16 * 1024;
+#ifndef SC_FUSED_MAX_CLUSTER
+#define SC_FUSED_MAX_CLUSTER 8
+#endif
+#ifndef SC_FUSED_CTAS_PER_SM
+#define SC_FUSED_CTAS_PER_SM 2
+#endif
+constexpr int kMaxFusedCluster = SC_FUSED_MAX_CLUSTER;  // CTAs of one row tile (cluster size)
+constexpr int kFusedCtasPerSm = SC_FUSED_CTAS_PER_SM;   // grid target of the fused kernel
 int fused_ksplit(const Layer& L);
+bool use_fused(const Layer& L, int64_t m);  // the router-fused decode kernel serves this call
 
 // Completion-counter region at the start of every workspace (see plan_workspace).
 constexpr size_t kCounterBytes = 64 * 1024;
@@ -158,7 +167,7 @@ struct FusedArgs {
     int ksplit;
 };
 cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s);
-int fused_max_kb();  // largest column range (in 64-column blocks) one CTA of the fused kernel holds
+int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
 
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                             cudaStream_t s);
