@@ -51,10 +51,25 @@ def parse():
     ap.add_argument("--fill", type=float, default=0.01)
     ap.add_argument("--route-frac", type=float, default=0.25)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="fast", choices=["fast", "exact"])
+    ap.add_argument("--mode", default="fast", choices=["fast", "fast_tc", "exact"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
+
+
+def launches_per_call(args):
+    """Kernels one forward call launches: the router-fused decode kernel for <= 8 tokens in the
+    fast modes; the router kernel plus one decode launch per 32-token chunk otherwise."""
+    if args.mode != "exact" and args.tokens <= 8:
+        return 1
+    return 1 + (1 if args.mode == "exact" else -(-args.tokens // 32))
+
+
+def launch_kind(args):
+    if args.mode != "exact" and args.tokens <= 8:
+        return "k_ctarq_fused_tc (router-fused decode, tcgen05)" if args.mode == "fast_tc" else \
+            "k_ctarq_fused_mma (router-fused decode, mma.sync)"
+    return "k_decode_exact (+ k_router)" if args.mode == "exact" else "k_ctarq_tc / k_ctarq_mma (+ k_router)"
 
 
 def call_bytes(n, k, m, nnz, routed):
@@ -96,54 +111,63 @@ def make_x(m, k, boosted, rng):
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of this GPU, polled through NVML from a host thread every
+    ~2 ms while the timed region runs (the host only waits on the GPU there)."""
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = None
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.thread = None
+        self.stop_flag = False
+        self.err = None
+
+    def _handle(self, nv):
+        import torch
+        try:
+            p = torch.cuda.get_device_properties(self.device)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:  # noqa: BLE001 - fall back to the CUDA ordinal
+            return nv.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def start(self):
+        import threading
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception as e:  # noqa: BLE001
+            self.err = f"nvml unavailable: {type(e).__name__}"
+            return
+
+        def run():
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self.stop_flag:
+                try:
+                    self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(get_reasons(h)),
+                                         nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                except Exception:  # noqa: BLE001
+                    pass
+                time.sleep(0.002)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        rows = []
-        for ln in open(self.path).read().splitlines():
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) >= 9:
-                rows.append(f)
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-
-        def num(s):
-            try:
-                return float(s)
-            except ValueError:
-                return None
-
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
-        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no sampler"]}
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+        reasons = sorted({n for _, r, _ in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(c for c, _, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples),
+                "power_w_median": round(statistics.median(p for _, _, p in self.samples), 1),
+                "source": "nvml, 2 ms polling during the timed region"}
 
 
 def measured_peak():
@@ -297,19 +321,27 @@ def run_ours(args, rank, world):
     g_step = sc.CapturedStep(step, dev)
     g_big = sc.CapturedStep(big_step, dev)
 
-    # end to end through the public API: pinned host inputs -> device -> C-TARQ -> host outputs
-    xs_host = [x.cpu().pin_memory() for x in xs]
-    ys_host = [torch.empty((args.tokens, op.out_features), dtype=torch.float16).pin_memory() for op in ops]
-    xs_dev = [torch.empty_like(x) for x in xs]
+    # end to end through the public API: every call's input from one pinned host buffer (one
+    # host->device copy), every output into one device buffer read back by one device->host copy
+    xsz = [x.numel() for x in xs]
+    ysz = [args.tokens * op.out_features for op in ops]
+    x_host = torch.cat([x.reshape(-1) for x in xs]).cpu().pin_memory()
+    y_host = torch.empty(sum(ysz), dtype=torch.float16).pin_memory()
+    x_dev = torch.empty_like(x_host, device=dev)
+    y_dev = torch.empty(sum(ysz), dtype=torch.float16, device=dev)
+    x_views = list(torch.split(x_dev, xsz))
+    y_views = list(torch.split(y_dev, ysz))
 
     def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
         for i, op in enumerate(ops):
-            xs_dev[i].copy_(xs_host[i], non_blocking=True)
-            ys_host[i].copy_(op.forward(xs_dev[i]), non_blocking=True)
+            op.forward(x_views[i].view(args.tokens, op.in_features),
+                       out=y_views[i].view(args.tokens, op.out_features))
+        y_host.copy_(y_dev, non_blocking=True)
 
     g_e2e = sc.CapturedStep(e2e_step, dev)
-    h2d = sum(x.numel() * 2 for x in xs)
-    d2h = sum(y.numel() * 2 for y in ys_host)
+    h2d = x_host.numel() * 2
+    d2h = y_host.numel() * 2
 
     def barrier():
         if world > 1:
@@ -339,7 +371,7 @@ def run_ours(args, rank, world):
             ms = float(t.item())
         return ms
 
-    clocks = ClockSampler(dev.index)
+    clocks = ClockSampler(dev)
     clocks.start()
     ms = timed(g_step, args.steps)
     clk = clocks.stop()
@@ -372,13 +404,14 @@ def run_ours(args, rank, world):
                    "parallelism": f"replicas{world}", "graph": "one CUDA graph per step"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "k_decode_tc (+ its router) on the gate/up/down calls",
+                     "kernel": launch_kind(args) + " on the gate/up/down calls (84 launches per step)",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
         "e2e": {"value": round(step_bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": "pinned host x -> device, forward, y -> pinned host, captured step, host sync each step"},
-        "gpu_launches": 2 * len(ops) * args.steps,
+                "how": "one pinned host->device copy of all inputs, the 196 calls, one device->host copy of "
+                       "all outputs; captured step, host sync each step"},
+        "gpu_launches": launches_per_call(args) * len(ops) * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args)

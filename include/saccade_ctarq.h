@@ -62,7 +62,9 @@ typedef enum sc_dtype { SC_F16 = 0, SC_BF16 = 1, SC_F32 = 2 } sc_dtype;
 /* Arithmetic of Phase 1 (the 4-bit base product). */
 typedef enum sc_mode {
     SC_MODE_FAST = 0,   /* tensor cores, f32 accumulation in hardware order (default) */
-    SC_MODE_EXACT = 1   /* CUDA cores in op.rs's exact 4-accumulator f32 order: bit-identical Y */
+    SC_MODE_EXACT = 1,  /* CUDA cores in op.rs's exact 4-accumulator f32 order: bit-identical Y */
+    SC_MODE_FAST_TC = 2 /* as SC_MODE_FAST (same tolerance); decode of <= 8 tokens dequantises the
+                         * weights into tensor memory and runs tcgen05 MMAs instead of mma.sync */
 } sc_mode;
 
 typedef enum sc_shard { SC_SHARD_NONE = 0, SC_SHARD_COLUMNS = 1, SC_SHARD_ROWS = 2 } sc_shard;

@@ -66,7 +66,7 @@ int fused_ksplit(const Layer& L) {
 }
 
 bool use_fused(const Layer& L, int64_t m) {
-    if (L.mode != SC_MODE_FAST || m > 8 || L.ks_fused <= 0) return false;
+    if (L.mode == SC_MODE_EXACT || m > 8 || L.ks_fused <= 0) return false;
     return (L.KB + L.ks_fused - 1) / L.ks_fused <= fused_max_kb(m);  // the x slice fits the CTA's copy
 }
 
@@ -352,7 +352,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
         set_error("sc_layer_create: delta_nnz > 0 needs row_ptrs, col_indices and values");
         return SC_EINVAL;
     }
-    if (desc->mode != SC_MODE_FAST && desc->mode != SC_MODE_EXACT) {
+    if (desc->mode != SC_MODE_FAST && desc->mode != SC_MODE_EXACT && desc->mode != SC_MODE_FAST_TC) {
         set_error("sc_layer_create: unknown mode");
         return SC_EINVAL;
     }
@@ -633,7 +633,7 @@ sc_status sc_layer_set_thresholds(sc_layer* layer, float t4, float t8) {
 }
 
 sc_status sc_layer_set_mode(sc_layer* layer, int mode) {
-    if (!layer || (mode != SC_MODE_FAST && mode != SC_MODE_EXACT)) {
+    if (!layer || (mode != SC_MODE_FAST && mode != SC_MODE_EXACT && mode != SC_MODE_FAST_TC)) {
         set_error("sc_layer_set_mode: bad argument");
         return SC_EINVAL;
     }

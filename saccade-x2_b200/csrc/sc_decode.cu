@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(MmaCfg::kThreads, 1) k_ctarq_mma(TCParams p) {
         pdl_wait();
         delta_rows<C::NT, C::kLd>(p, corrbuf, (warp - C::kDeltaWarp0) * 32 + lane, rt, kb_begin, kb_end);
     }
+    __syncwarp();
     __syncthreads();
     if (s_abort) {
         if (warp == C::kProducerWarp && lane == 0)
@@ -478,6 +479,7 @@ __global__ void __launch_bounds__(TcCfg<NT>::kThreads, 1) k_ctarq_tc(TCParams p)
         pdl_wait();
         delta_rows<NT, C::kLd>(p, corrbuf, (warp - C::kDeltaWarp0) * 32 + lane, rt, kb_begin, kb_end);
     }
+    __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
     __syncthreads();
     if (warp == C::kMmaWarp) {
         // every tcgen05 operation of this CTA has completed (done observed, loads waited)
@@ -495,21 +497,25 @@ __global__ void __launch_bounds__(TcCfg<NT>::kThreads, 1) k_ctarq_tc(TCParams p)
     epilogue_tile<NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
 }
 
-// ---------------------------------------------------------------- k_ctarq_fused (<= 8 tokens, router fused)
+// ---------------------------------------------------------------- router-fused decode (<= 8 tokens)
 
-// The decode kernel with the router folded in.  The ksplit CTAs that share a 128-row tile
-// form a thread-block cluster; each takes a column slice.  Four auxiliary warps stage the
-// slice of every token into shared memory (bf16 rounded to f16) while summing x, x^2 and |x|
-// in f32; each CTA pushes its sums to every CTA of the cluster (st.async into the receiver's
-// shared memory, completing on its mbarrier), so every CTA adds the whole-token sums in rank
-// order -- identical in every cluster -- and takes the reference's routing decision
-// (route_token, with the band widened by the bound on the f32 summation error).  dW comes
-// from a per-CTA block prepared at load time and fetched with one bulk copy; auxiliary thread
-// r owns row r of the tile: it adds that row's dW, scales, and pushes the row to the cluster
-// CTA that owns it, which adds the splits in rank order and writes y.  CTA 0 publishes the
-// mask and the routed-token list.  The ring carries weights only, so the producer never waits
-// on the previous kernel; about 108 KB of shared memory lets two CTAs (of this call and the
-// next) share an SM.  x is staged for NTp = ntok rounded up to a power of two tokens.
+// Decode kernels with the router folded in.  The ksplit CTAs that share a 128-row tile form a
+// thread-block cluster; each takes a column slice.  Four auxiliary warps stage the slice of
+// every token into shared memory (bf16 rounded to f16) while summing x, x^2 and |x| in f32;
+// each CTA pushes its sums to every CTA of the cluster (st.async into the receiver's shared
+// memory, completing on its mbarrier), so every CTA adds the whole-token sums in rank order --
+// identical in every cluster -- and takes the reference's routing decision (route_token, with
+// the band widened by the bound on the f32 summation error).  dW comes from a per-CTA block
+// prepared at load time and fetched with one bulk copy; auxiliary thread r owns row r of the
+// tile: it adds that row's dW, scales, and pushes the row to the cluster CTA that owns it, which
+// adds the splits in rank order and writes y.  CTA 0 publishes the mask and the routed-token
+// list.  The ring carries weights only, so the producer never waits on the previous kernel;
+// about 108 KB of shared memory lets two CTAs (of this call and the next) share an SM.  x is
+// staged for ntp = ntok rounded up to a power of two tokens, as [8-column chunk][ntp][8 f16].
+//
+// Two base-product engines share that frame: k_ctarq_fused_tc dequantises the weights into
+// tensor memory and runs tcgen05 MMAs (M=128, N=16, K=16) on the staged x; k_ctarq_fused_mma
+// runs mma.sync on the same data.
 struct FusedParams {
     TCParams t;
     const void* x;
@@ -524,30 +530,122 @@ struct FusedParams {
     const uint8_t* dwblk;   // blocked dW (null: read the CSR)
     const uint32_t* dwoff;
     int ntp;                // staged token rows: 1, 2, 4 or 8
+    RouteConsts rc;         // of Kfull
+    double gT;              // bound factor of this kernel's own f32 sums (gamma of their depth, doubled)
 };
 
-struct FusedCfg {
-    static constexpr int kMmaWarps = 8;
-    static constexpr int kProducerWarp = 8;
-    static constexpr int kAuxWarp0 = 9;
-    static constexpr int kAuxThreads = 128;
-    static constexpr int kThreads = 13 * 32;
+// Shared-memory regions after the weight ring, common to both engines.
+struct FusedRegions {
     static constexpr int NT = 8;
-    static constexpr int SKB = 4;
-    static constexpr int S = 3;
-    static constexpr int kStageBytes = SKB * 4096;   // weights only
-    static constexpr int kXsBytes = 32 * 1024;       // staged x: 32768 / (128 * ntp) column blocks
-    static constexpr int kLd = NT + 1;
-    static constexpr int kXsOff = S * kStageBytes;
-    static constexpr int kDwOff = kXsOff + kXsBytes;
-    static constexpr int kAccOff = kDwOff + static_cast<int>(kDwBlockMax);
-    static constexpr int kStatsOff = kAccOff + 128 * kLd * 4;              // [16 ranks][8 tokens][3] f64
-    static constexpr int kRedOff = kStatsOff + kMaxFusedCluster * NT * 3 * 8;  // [ks][rows of rank][8] f32
-    static constexpr int kRedBytes = (128 + kMaxFusedCluster) * NT * 4;
-    static constexpr int kBarOff = kRedOff + kRedBytes;
-    static constexpr int kTotal = kBarOff + (2 * S + 4) * 8;
-    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+    static constexpr int kAuxThreads = 128;
+    static constexpr int kXsBytes = 32 * 1024;   // staged x: 32768 / (128 * ntp) column blocks
+    static constexpr int kPad = 128;             // MMA operand rows past the last staged chunk read here
+    static constexpr int kXs = 0;
+    static constexpr int kDw = kXsBytes + kPad;
+    static constexpr int kStats = kDw + static_cast<int>(kDwBlockMax);             // [ranks][8 tokens][3] f64
+    static constexpr int kRed = kStats + kMaxFusedCluster * NT * 3 * 8;            // [ks][rows of rank][8] f32
+    static constexpr int kBytes = kRed + (128 + kMaxFusedCluster) * NT * 4;
+    static constexpr int kBars = 4;                                                // x_ready dw_ready stats red
 };
+
+struct FusedCtx {
+    const FusedParams* fp;
+    unsigned char* xs;
+    const unsigned char* dws;
+    double* rstats;
+    float* rbuf;
+    uint64_t* x_ready;   // 4 arrivals (auxiliary warps): x staged
+    uint64_t* dw_ready;  // bulk copy of the dW block
+    uint64_t* stats_bar; // cluster sums received
+    uint64_t* red_bar;   // split partials of owned rows received
+    int* s_abort;
+    unsigned* s_mask;
+    double (*s_red)[FusedRegions::NT][4];
+    int64_t rt, kb_begin, kb_end;
+    int split, ks, nkb, ntok, cs, rb, nr;
+    bool use_blk;
+};
+
+__device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, unsigned char* regions, uint64_t* bars, int* s_abort,
+                                              unsigned* s_mask, double (*s_red)[FusedRegions::NT][4]) {
+    using R = FusedRegions;
+    const TCParams& p = fp.t;
+    FusedCtx c;
+    c.fp = &fp;
+    c.xs = regions + R::kXs;
+    c.dws = regions + R::kDw;
+    c.rstats = reinterpret_cast<double*>(regions + R::kStats);
+    c.rbuf = reinterpret_cast<float*>(regions + R::kRed);
+    c.x_ready = bars;
+    c.dw_ready = bars + 1;
+    c.stats_bar = bars + 2;
+    c.red_bar = bars + 3;
+    c.s_abort = s_abort;
+    c.s_mask = s_mask;
+    c.s_red = s_red;
+    c.ks = p.ksplit;
+    c.ntok = p.ntok;
+    c.rt = blockIdx.x / c.ks;
+    c.split = static_cast<int>(blockIdx.x - c.rt * c.ks);   // = cluster rank
+    c.kb_begin = (p.KB * c.split) / c.ks;
+    c.kb_end = (p.KB * (c.split + 1)) / c.ks;
+    c.nkb = static_cast<int>(c.kb_end - c.kb_begin);
+    c.cs = fp.ntp * 16;
+    c.rb = (128 * c.split) / c.ks;
+    c.nr = (128 * (c.split + 1)) / c.ks - c.rb;
+    c.use_blk = fp.dwblk != nullptr && p.nnz > 0;
+    return c;
+}
+
+// One thread: the common mbarriers and the byte counts expected from the cluster.
+__device__ __forceinline__ void fused_init_bars(const FusedCtx& c) {
+    mbar_init(c.x_ready, 4);
+    mbar_init(c.dw_ready, 1);
+    mbar_init(c.stats_bar, 1);
+    mbar_init(c.red_bar, 1);
+    fence_mbar_init();
+    if (c.ks > 1) {
+        mbar_arrive_expect_tx(c.stats_bar, static_cast<uint32_t>(c.ks * c.ntok * 24));
+        mbar_arrive_expect_tx(c.red_bar, static_cast<uint32_t>(c.ks * c.nr * FusedRegions::NT * 4));
+    }
+}
+
+// Producer lane: weights through the ring (stages of SKB 4 KB blocks), dW block up front.
+// Returns the number of stages issued.
+template <int SKB, int S>
+__device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* ring, uint64_t* full, uint64_t* empty) {
+    const TCParams& p = c.fp->t;
+    constexpr int kStage = SKB * 4096;
+    const int nst = (c.nkb + SKB - 1) / SKB;
+    const uint64_t pol = policy_evict_first();
+    const int pre = nst < S ? nst : S;
+    int issued = 0;
+    for (int it = 0; it < pre; ++it, ++issued) {
+        const int64_t kb0 = c.kb_begin + static_cast<int64_t>(it) * SKB;
+        const int n = static_cast<int>(imin64(SKB, c.kb_end - kb0));
+        mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
+        bulk_g2s_stream(ring + it * kStage, p.wq + (c.rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096),
+                        &full[it], pol);
+    }
+    if (c.use_blk) {
+        const uint32_t o0 = c.fp->dwoff[blockIdx.x], o1 = c.fp->dwoff[blockIdx.x + 1];
+        mbar_arrive_expect_tx(c.dw_ready, o1 - o0);
+        bulk_g2s(const_cast<unsigned char*>(c.dws), c.fp->dwblk + o0, o1 - o0, c.dw_ready);
+    }
+    for (int it = pre; it < nst; ++it, ++issued) {
+        const int slot = it % S;
+        const int64_t kb0 = c.kb_begin + static_cast<int64_t>(it) * SKB;
+        const int n = static_cast<int>(imin64(SKB, c.kb_end - kb0));
+        if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
+            *c.s_abort = 1;
+            break;
+        }
+        mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * 4096));
+        bulk_g2s_stream(ring + slot * kStage, p.wq + (c.rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096),
+                        &full[slot], pol);
+    }
+    return issued;
+}
 
 __device__ __forceinline__ uint4 load_x8(const void* x, int x_dtype, bool vec, int64_t base) {
     if (vec) return __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + base));
@@ -571,108 +669,467 @@ __device__ __forceinline__ void sum_x8(uint4 v, float& a1, float& a2, float& a3)
     }
 }
 
-__global__ void __launch_bounds__(FusedCfg::kThreads, 2) k_ctarq_fused(FusedParams fp) {
-    using C = FusedCfg;
-    constexpr int SKB = C::SKB, S = C::S, NT = C::NT;
+// Auxiliary warps (four consecutive warps; thread `at` = 32 * (warp % 4) + lane owns row `at`
+// of the tile): stage x, route, publish the mask, and accumulate this row's dW into corr.
+__device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float (&corr)[FusedRegions::NT]) {
+    using R = FusedRegions;
+    constexpr int NT = R::NT;
+    const FusedParams& fp = *c.fp;
+    const TCParams& p = fp.t;
+    const int wi = at >> 5, lane = at & 31;
+    const int ntok = c.ntok, ks = c.ks;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) corr[t] = 0.0f;
+    pdl_wait();
+    const int64_t slice0 = fp.x_col0 + c.kb_begin * 64;             // first staged column of x
+    const int64_t slice1 = fp.x_col0 + imin64(c.kb_end * 64, p.K);  // end of its real columns
+    const bool vec = fp.x_dtype == SC_F16 && ((reinterpret_cast<uintptr_t>(fp.x) | (fp.x_stride * 2)) & 15) == 0 &&
+                     (fp.x_col0 & 7) == 0;
+    const int nin = c.nkb * 8;  // staged 8-column chunks
+    float a1[NT], a2[NT], a3[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) a1[t] = a2[t] = a3[t] = 0.0f;
+    // pass 1: stage the slice (ntp token rows; rows >= ntok and columns >= K are zero)
+    for (int ci = at; ci < nin; ci += R::kAuxThreads) {
+        const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
+        const bool inb = colx < slice1;
+        unsigned char* dst = c.xs + ci * c.cs;
+#pragma unroll
+        for (int g4 = 0; g4 < NT; g4 += 4) {
+            if (g4 < fp.ntp) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    v[u] = make_uint4(0u, 0u, 0u, 0u);
+                    if (g4 + u < ntok && inb) v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                    if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                }
+            }
+        }
+    }
+    fence_proxy_async_smem();  // the tensor cores read the staged x through the async proxy
+    __syncwarp();
+    if (lane == 0) mbar_arrive(c.x_ready);
+    // pass 2 (rows shards): this CTA's share of the columns outside the layer's slice
+    const int64_t nch = fp.Kfull / 8;
+    const int64_t in0 = fp.x_col0 / 8, in1 = (fp.x_col0 + p.K) / 8;
+    const int64_t nout = nch - (in1 - in0);
+    const int64_t o0 = (nout * c.split) / ks, o1 = (nout * (c.split + 1)) / ks;
+    for (int64_t j = o0 + at; j < o1; j += R::kAuxThreads) {
+        const int64_t ch = j < in0 ? j : j + (in1 - in0);
+#pragma unroll
+        for (int g4 = 0; g4 < NT; g4 += 4) {
+            if (g4 < ntok) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    v[u] = make_uint4(0u, 0u, 0u, 0u);
+                    if (g4 + u < ntok) v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+            }
+        }
+    }
+    // warp sums in f32 (five more levels of the summation tree, inside gT), then f64
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (t < ntok) {
+            float d1 = a1[t], d2 = a2[t], d3 = a3[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                d1 += __shfl_down_sync(0xffffffffu, d1, o);
+                d2 += __shfl_down_sync(0xffffffffu, d2, o);
+                d3 += __shfl_down_sync(0xffffffffu, d3, o);
+            }
+            if (lane == 0) {
+                c.s_red[0][t][wi] = d1;
+                c.s_red[1][t][wi] = d2;
+                c.s_red[2][t][wi] = d3;
+            }
+        }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (ks > 1) {
+        cluster_wait();  // every mbarrier of the cluster is initialised
+        if (wi == 0 && lane < ks) {
+            // lane r sends this CTA's sums to rank r, into slot [split]
+            const uint32_t dst = dsmem_addr(c.rstats + c.split * NT * 3, static_cast<uint32_t>(lane));
+            const uint32_t bar = dsmem_addr(c.stats_bar, static_cast<uint32_t>(lane));
+            for (int t = 0; t < ntok; ++t)
+                for (int q = 0; q < 3; ++q)
+                    st_async_f64(dst + (t * 3 + q) * 8,
+                                 ((c.s_red[q][t][0] + c.s_red[q][t][1]) + c.s_red[q][t][2]) + c.s_red[q][t][3], bar);
+        }
+    } else if (at == 0) {
+        for (int t = 0; t < ntok; ++t)
+            for (int q = 0; q < 3; ++q)
+                c.rstats[t * 3 + q] = ((c.s_red[q][t][0] + c.s_red[q][t][1]) + c.s_red[q][t][2]) + c.s_red[q][t][3];
+    }
+    if (at == 0) {
+        const bool ok = ks == 1 || mbar_wait(c.stats_bar, 0, p.status);
+        unsigned m = 0u;
+        for (int t = 0; t < ntok && ok; ++t) {
+            double S1 = 0.0, S2 = 0.0, SA = 0.0;
+            for (int r = 0; r < ks; ++r) {
+                S1 += c.rstats[(r * NT + t) * 3 + 0];
+                S2 += c.rstats[(r * NT + t) * 3 + 1];
+                SA += c.rstats[(r * NT + t) * 3 + 2];
+            }
+            const void* xrow = static_cast<const unsigned char*>(fp.x) + (p.tok0 + t) * fp.x_stride * 2;
+            const bool r = p.route_all ? true
+                                       : route_token(S1, S2, SA, fp.Kfull, fp.rc, fp.t4, fp.t8, xrow, fp.x_dtype, nullptr,
+                                                     fp.gT * SA, fp.gT * S2);
+            if (r) m |= 1u << t;
+        }
+        if (!ok) *c.s_abort = 1;
+        *c.s_mask = m;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const unsigned mask = *c.s_mask;
+    if (blockIdx.x == 0 && wi == 0) {
+        for (int t = lane; t < ntok; t += 32) {
+            const int r = (mask >> t) & 1u;
+            if (fp.mask_out) fp.mask_out[p.tok0 + t] = static_cast<uint8_t>(r);
+            if (fp.ridx_out && r) fp.ridx_out[__popc(mask & ((1u << t) - 1u))] = static_cast<int32_t>(p.tok0 + t);
+        }
+        if (lane == 0 && fp.nrouted_out) *fp.nrouted_out = __popc(mask);
+    }
+    // dW of this thread's row for the routed tokens, x from the staged copy, column order
+    const int64_t row = c.rt * 128 + at;
+    if (mask == 0u || row >= p.N || p.nnz == 0) return;
+    auto add_entry = [&](int64_t cl, int8_t q) {
+        const float v = __fmul_rn(static_cast<float>(q), p.ds);
+        const unsigned char* xp = c.xs + ((cl >> 3) * fp.ntp) * 16 + (cl & 7) * 2;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            if ((mask >> t) & 1u)
+                corr[t] = __fadd_rn(corr[t], __fmul_rn(h2f(*reinterpret_cast<const uint16_t*>(xp + t * 16)), v));
+    };
+    if (c.use_blk) {
+        if (!mbar_wait(c.dw_ready, 0, p.status)) {
+            *c.s_abort = 1;
+            return;
+        }
+        const uint16_t* roff = reinterpret_cast<const uint16_t*>(c.dws);
+        const int n = roff[128];
+        const uint16_t* bcol = reinterpret_cast<const uint16_t*>(c.dws + 272);
+        const int8_t* bval = reinterpret_cast<const int8_t*>(c.dws + 272 + ((n * 2 + 15) / 16) * 16);
+        for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
+    } else {
+        const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
+        const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, c.kb_begin * 64);
+        const int64_t e1 = (ks == 1) ? hi : lower_bound_u16(p.col, e0, hi, c.kb_end * 64);
+        for (int64_t e = e0; e < e1; e += 8) {
+            const int cnt = static_cast<int>(imin64(8, e1 - e));
+            int64_t cc[8];
+            int8_t vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                cc[u] = u < cnt ? static_cast<int64_t>(p.col[e + u]) - c.kb_begin * 64 : 0;
+                vv[u] = u < cnt ? p.val[e + u] : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (u < cnt) add_entry(cc[u], vv[u]);
+        }
+    }
+}
+
+// Auxiliary thread `at` with this split's row contribution v: with one split, write y; else
+// push the row to the cluster CTA that owns it and, for owned rows, add the splits in rank
+// order and write y.
+__device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, const float (&v)[FusedRegions::NT]) {
+    constexpr int NT = FusedRegions::NT;
+    const TCParams& p = c.fp->t;
+    const int ks = c.ks;
+    pdl_wait();
+    auto store_row = [&](int64_t r, const float* w) {
+        for (int t = 0; t < c.ntok; ++t) {
+            const int64_t oi = (p.tok0 + t) * p.N + r;
+            if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = w[t];
+            else store_output(p.y, p.y_dtype, oi, w[t], p.bias, r);
+        }
+    };
+    const int64_t row = c.rt * 128 + at;
+    if (ks == 1) {
+        if (!*c.s_abort && row < p.N) store_row(row, v);
+        return;
+    }
+    {
+        // rank o owns rows [128 o / ks, 128 (o+1) / ks)
+        const int o = (at * ks + ks - 1) / 128;
+        const int orb = (128 * o) / ks, onr = (128 * (o + 1)) / ks - orb;
+        const uint32_t dst = dsmem_addr(c.rbuf + (c.split * onr + (at - orb)) * NT, static_cast<uint32_t>(o));
+        const uint32_t bar = dsmem_addr(c.red_bar, static_cast<uint32_t>(o));
+        st_async_v4_f32(dst, v[0], v[1], v[2], v[3], bar);
+        st_async_v4_f32(dst + 16, v[4], v[5], v[6], v[7], bar);
+    }
+    if (at < c.nr) {
+        const bool ok = mbar_wait(c.red_bar, 0, p.status);
+        const int64_t r = c.rt * 128 + c.rb + at;
+        if (ok && !*c.s_abort && r < p.N) {
+            float w[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) w[t] = 0.0f;
+            for (int sp = 0; sp < ks; ++sp) {
+#pragma unroll
+                for (int t = 0; t < NT; ++t) w[t] = __fadd_rn(w[t], c.rbuf[(sp * c.nr + at) * NT + t]);
+            }
+            store_row(r, w);
+        }
+    }
+}
+
+// ---- engine 1: tcgen05 (weights dequantised into tensor memory)
+struct FusedTcCfg {
+    static constexpr int kDqWarps = 8;               // two per TMEM sub-partition, one 16-row tile each
+    static constexpr int kProducerWarp = 8;
+    static constexpr int kMmaWarp = 9;
+    static constexpr int kAuxWarp0 = 10;
+    static constexpr int kThreads = 14 * 32;
+    // One ring stage is one hand-off between the dequantising warps and the MMA thread: every
+    // hand-off costs a few hundred cycles of latency, so it carries 3 blocks (12 MMAs).
+    static constexpr int SKB = 3;
+    static constexpr int S = 4;
+    static constexpr int kStageBytes = SKB * 4096;
+    static constexpr int kAB = 2;                    // TMEM A buffers, one stage (SKB * 32 columns) each
+    static constexpr uint32_t kTmemCols = 256;       // D in [0, 16), A buffers in [32, 32 + 2 * 96)
+    static constexpr int kRegions = S * kStageBytes;
+    static constexpr int kBarOff = kRegions + FusedRegions::kBytes;
+    static constexpr int kNumBars = 2 * S + 2 * kAB + 1 + FusedRegions::kBars;
+    static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
+    static constexpr int kTotal = kTmemSlotOff + 16;
+    static_assert(32 + kAB * SKB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
+    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+};
+
+__global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(FusedParams fp) {
+    using C = FusedTcCfg;
+    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = FusedRegions::NT;
     const TCParams& p = fp.t;
     extern __shared__ __align__(1024) unsigned char smem[];
-    unsigned char* xs = smem + C::kXsOff;
-    unsigned char* dws = smem + C::kDwOff;
-    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
-    double* rstats = reinterpret_cast<double*>(smem + C::kStatsOff);
-    float* rbuf = reinterpret_cast<float*>(smem + C::kRedOff);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
     uint64_t* empty = full + S;
-    uint64_t* x_ready = empty + S;
-    uint64_t* dw_ready = x_ready + 1;
-    uint64_t* stats_bar = dw_ready + 1;
-    uint64_t* red_bar = stats_bar + 1;
+    uint64_t* a_full = empty + S;
+    uint64_t* a_empty = a_full + AB;
+    uint64_t* done = a_empty + AB;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
     __shared__ int s_abort;
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
-
+    const FusedCtx c = fused_ctx(fp, smem + C::kRegions, done + 1, &s_abort, &s_mask, s_red);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ks = p.ksplit;
-    const int ntok = p.ntok;
-    const int64_t rt = blockIdx.x / ks;
-    const int split = static_cast<int>(blockIdx.x - rt * ks);   // = cluster rank
-    const int64_t kb_begin = (p.KB * split) / ks;
-    const int64_t kb_end = (p.KB * (split + 1)) / ks;
-    const int nkb = static_cast<int>(kb_end - kb_begin);
-    const int nst = (nkb + SKB - 1) / SKB;
-    const bool use_blk = fp.dwblk != nullptr && p.nnz > 0;
-    const int cs = fp.ntp * 16;       // bytes per staged 8-column chunk (all token rows)
-    const int bs = 8 * cs;            // bytes per staged 64-column block
-    const int rb = (128 * split) / ks, nr = (128 * (split + 1)) / ks - rb;   // rows this CTA writes
 
     pdl_launch_dependents();
-    for (int i = tid; i < 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
+    if (tid == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], C::kDqWarps);
+        }
+        for (int i = 0; i < AB; ++i) {
+            mbar_init(&a_full[i], C::kDqWarps);
+            mbar_init(&a_empty[i], 1);
+        }
+        mbar_init(done, 1);
+        fused_init_bars(c);
+        s_abort = 0;
+        s_mask = 0u;
+    }
+    if (warp == C::kMmaWarp) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (c.ks > 1) cluster_arrive_relaxed();  // this CTA's mbarriers are initialised (released above)
+
+    int issued = 0;
+    float corr[NT];
+    const int at = 32 * (warp & 3) + lane;  // auxiliary threads: tile row, in this warp's TMEM lanes
+    if (warp == C::kProducerWarp) {
+        if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
+    } else if (warp == C::kMmaWarp) {
+        // the whole warp runs the loop (uniform); one elected lane issues
+        constexpr uint32_t idesc = idesc_f16_f32(128, 16);
+        bool ok = __all_sync(0xffffffffu, mbar_wait(c.x_ready, 0, p.status));
+        const int nst = (c.nkb + SKB - 1) / SKB;
+        // B descriptor of staged chunk `ch`: base + ch * ntp (start address in 16-byte units)
+        const uint64_t bd0 = desc_kmajor(c.xs, c.cs, 0);
+        const uint64_t ntp = static_cast<uint64_t>(fp.ntp);
+        for (int u = 0; u < nst && ok; ++u) {
+            const int b = u % AB;
+            ok = __all_sync(0xffffffffu, mbar_wait(&a_full[b], (u / AB) & 1, p.status));
+            if (!ok) break;
+            tc_fence_after();
+            const int n = c.nkb - u * SKB < SKB ? c.nkb - u * SKB : SKB;
+            const uint32_t a0 = tmem + 32 + b * SKB * 32;
+            const uint64_t bu = bd0 + static_cast<uint64_t>(u * SKB * 8) * ntp;
+            if (elect_one()) {
+                for (int k = 0; k < n; ++k) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)  // B: [chunk][ntp][16 B]; rows past ntok are not read back
+                        tc_mma_ts(tmem, a0 + k * 32 + i * 8, bu + static_cast<uint64_t>(k * 8 + 2 * i) * ntp, idesc,
+                                  (u | k | i) ? 1u : 0u);
+                }
+                tc_commit(&a_empty[b]);
+            }
+            __syncwarp();
+        }
+        if (!ok && lane == 0) s_abort = 1;
+        if (elect_one()) tc_commit(done);  // also after an abort, so that the TMEM can be released
+        __syncwarp();
+    } else if (warp < C::kDqWarps) {
+        const int sp = warp & 3, q = warp >> 2;
+        const int tile = 2 * sp + q;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * sp + 16 * q) << 16;
+        const int nst = (c.nkb + SKB - 1) / SKB;
+        for (int u = 0; u < nst; ++u) {
+            const int slot = u % S, b = u % AB;
+            if (!mbar_wait(&full[slot], (u / S) & 1, p.status)) {
+                s_abort = 1;
+                break;
+            }
+            // the stage goes to registers and its ring slot back to the producer at once, so
+            // the ring keeps every stage in flight while this unit waits for a TMEM buffer
+            const int n = c.nkb - u * SKB < SKB ? c.nkb - u * SKB : SKB;
+            uint4 wv[SKB];
+#pragma unroll
+            for (int k = 0; k < SKB; ++k)
+                if (k < n)
+                    wv[k] = *reinterpret_cast<const uint4*>(smem + slot * C::kStageBytes + k * 4096 + tile * 512 + lane * 16);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (u >= AB && !mbar_wait(&a_empty[b], ((u / AB) - 1) & 1, p.status)) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < SKB; ++k) {
+                if (k < n) {
+                    const uint32_t words[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
+#pragma unroll
+                    for (int st = 0; st < 4; ++st) {
+                        uint32_t h[4];
+                        dequant_word(words[st], h);
+                        tc_st_16x256b(tmem + lane_addr + 32 + (b * SKB + k) * 32 + st * 8, h[0], h[2], h[1], h[3]);
+                    }
+                }
+            }
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[b]);
+        }
+    } else {
+        fused_aux_front(c, at, corr);
+    }
+    __syncwarp();
+    if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
+    // auxiliary threads: this split's contribution to row `at` (acc * row scale + dW; 0 past N)
+    float v[NT];
+    if (warp >= C::kAuxWarp0) {
+        const int64_t row = c.rt * 128 + at;
+        const float sc = row < p.N ? __ldg(p.scale + row) : 0.0f;
+        uint32_t d[8];
+        const bool ok = mbar_wait(done, 0, p.status);
+        tc_fence_after();
+        tc_ld8(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16), d);
+        tc_wait_ld();
+        if (!ok) s_abort = 1;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            v[t] = row < p.N ? __fadd_rn(__fmul_rn(__uint_as_float(d[t]), sc), corr[t]) : 0.0f;
+    }
+    __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
+    tc_fence_before();
+    __syncthreads();
+    if (warp == C::kMmaWarp) {
+        if (s_abort) mbar_wait(done, 0, nullptr, kDrainNs);
+        tc_fence_after();
+        tmem_dealloc(tmem, C::kTmemCols);
+    }
+    if (s_abort && warp == C::kProducerWarp && lane == 0) {
+        for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+            mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+        if (c.use_blk) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
+    }
+    if (warp >= C::kAuxWarp0) fused_aux_finish(c, at, v);
+}
+
+// ---- engine 2: mma.sync on the same frame
+struct FusedMmaCfg {
+    static constexpr int kMmaWarps = 8;
+    static constexpr int kProducerWarp = 8;
+    static constexpr int kAuxWarp0 = 9;
+    static constexpr int kThreads = 13 * 32;
+    static constexpr int SKB = 4;
+    static constexpr int S = 3;
+    static constexpr int kStageBytes = SKB * 4096;
+    static constexpr int kLd = FusedRegions::NT + 1;
+    static constexpr int kAccOff = S * kStageBytes;
+    static constexpr int kRegions = kAccOff + 128 * kLd * 4;
+    static constexpr int kBarOff = kRegions + FusedRegions::kBytes;
+    static constexpr int kTotal = kBarOff + (2 * S + FusedRegions::kBars) * 8;
+    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+};
+
+__global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(FusedParams fp) {
+    using C = FusedMmaCfg;
+    constexpr int SKB = C::SKB, S = C::S, NT = FusedRegions::NT;
+    const TCParams& p = fp.t;
+    extern __shared__ __align__(1024) unsigned char smem[];
+    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+    uint64_t* empty = full + S;
+    __shared__ int s_abort;
+    __shared__ unsigned s_mask;
+    __shared__ double s_red[3][NT][4];
+    const FusedCtx c = fused_ctx(fp, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nst = (c.nkb + SKB - 1) / SKB;
+
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], C::kMmaWarps);
         }
-        mbar_init(x_ready, 4);
-        mbar_init(dw_ready, 1);
-        mbar_init(stats_bar, 1);
-        mbar_init(red_bar, 1);
-        fence_mbar_init();
-        if (ks > 1) {
-            mbar_arrive_expect_tx(stats_bar, static_cast<uint32_t>(ks * ntok * 24));
-            mbar_arrive_expect_tx(red_bar, static_cast<uint32_t>(ks * nr * NT * 4));
-        }
+        fused_init_bars(c);
         s_abort = 0;
         s_mask = 0u;
     }
+    for (int i = tid; i < 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
     __syncthreads();
-    if (ks > 1) cluster_arrive();  // this CTA's mbarriers are initialised
+    if (c.ks > 1) cluster_arrive_relaxed();
 
     int issued = 0;
+    float corr[NT];
+    const int at = 32 * (warp & 3) + lane;
     if (warp == C::kProducerWarp) {
-        if (lane == 0) {
-            // weights and dW are read-only: no dependency on the previous kernel
-            const uint64_t pol = policy_evict_first();
-            const int pre = nst < S ? nst : S;
-            for (int it = 0; it < pre; ++it, ++issued) {
-                const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
-                const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
-                mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
-                bulk_g2s_stream(smem + it * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
-                                static_cast<uint32_t>(n * 4096), &full[it], pol);
-            }
-            if (use_blk) {
-                const uint32_t o0 = fp.dwoff[blockIdx.x], o1 = fp.dwoff[blockIdx.x + 1];
-                mbar_arrive_expect_tx(dw_ready, o1 - o0);
-                bulk_g2s(dws, fp.dwblk + o0, o1 - o0, dw_ready);
-            }
-            for (int it = pre; it < nst; ++it, ++issued) {
-                const int slot = it % S;
-                const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
-                const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
-                if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
-                    s_abort = 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * 4096));
-                bulk_g2s_stream(smem + slot * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
-                                static_cast<uint32_t>(n * 4096), &full[slot], pol);
-            }
-        }
+        if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
     } else if (warp < C::kMmaWarps) {
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const int g = lane >> 2, c = lane & 3;
-        const bool has_tok = g < ntok;
-        const int xoff = (c >> 1) * cs + g * 16 + (c & 1) * 8;
-        if (!mbar_wait(x_ready, 0, p.status)) s_abort = 1;
+        const int g = lane >> 2, cq = lane & 3;
+        const bool has_tok = g < c.ntok;
+        const int xoff = (cq >> 1) * c.cs + g * 16 + (cq & 1) * 8;
+        if (!mbar_wait(c.x_ready, 0, p.status)) s_abort = 1;
         for (int it = 0; it < nst && !s_abort; ++it) {
             const int slot = it % S;
             if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
                 s_abort = 1;
                 break;
             }
-            const int n = static_cast<int>(imin64(SKB, kb_end - (kb_begin + static_cast<int64_t>(it) * SKB)));
+            const int n = static_cast<int>(imin64(SKB, c.kb_end - (c.kb_begin + static_cast<int64_t>(it) * SKB)));
             const unsigned char* st = smem + slot * C::kStageBytes;
-            const unsigned char* xk0 = xs + (it * SKB) * bs + xoff;
+            const unsigned char* xk0 = c.xs + (it * SKB) * 8 * c.cs + xoff;
 #pragma unroll
             for (int j = 0; j < SKB; ++j) {
                 if (j < n) {
@@ -681,7 +1138,7 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 2) k_ctarq_fused(FusedPara
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
                         uint2 b = make_uint2(0u, 0u);
-                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * bs + 2 * s * cs);
+                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * 8 * c.cs + 2 * s * c.cs);
                         uint32_t a[4];
                         dequant_word(words[s], a);
                         mma_16816(acc[s & 1], a, b.x, b.y);
@@ -692,238 +1149,28 @@ __global__ void __launch_bounds__(FusedCfg::kThreads, 2) k_ctarq_fused(FusedPara
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
         const int r0 = warp * 16 + g;
-        accbuf[r0 * C::kLd + 2 * c] = acc[0][0] + acc[1][0];
-        accbuf[r0 * C::kLd + 2 * c + 1] = acc[0][1] + acc[1][1];
-        accbuf[(r0 + 8) * C::kLd + 2 * c] = acc[0][2] + acc[1][2];
-        accbuf[(r0 + 8) * C::kLd + 2 * c + 1] = acc[0][3] + acc[1][3];
+        accbuf[r0 * C::kLd + 2 * cq] = acc[0][0] + acc[1][0];
+        accbuf[r0 * C::kLd + 2 * cq + 1] = acc[0][1] + acc[1][1];
+        accbuf[(r0 + 8) * C::kLd + 2 * cq] = acc[0][2] + acc[1][2];
+        accbuf[(r0 + 8) * C::kLd + 2 * cq + 1] = acc[0][3] + acc[1][3];
+    } else {
+        fused_aux_front(c, at, corr);
     }
-    // auxiliary warps: staging, routing, dW; thread `at` owns row `at` of the tile
-    float corr[NT];
-#pragma unroll
-    for (int t = 0; t < NT; ++t) corr[t] = 0.0f;
-    const int at = tid - C::kAuxWarp0 * 32;
-    if (warp >= C::kAuxWarp0) {
-        const int wi = warp - C::kAuxWarp0;
-        pdl_wait();
-        const int64_t slice0 = fp.x_col0 + kb_begin * 64;             // first staged column of x
-        const int64_t slice1 = fp.x_col0 + imin64(kb_end * 64, p.K);  // end of its real columns
-        const bool vec = fp.x_dtype == SC_F16 && ((reinterpret_cast<uintptr_t>(fp.x) | (fp.x_stride * 2)) & 15) == 0 &&
-                         (fp.x_col0 & 7) == 0;
-        const int nin = nkb * 8;                                        // staged 8-column chunks
-        float a1[NT], a2[NT], a3[NT];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) a1[t] = a2[t] = a3[t] = 0.0f;
-        // pass 1: stage the slice (ntp token rows; rows >= ntok and columns >= K are zero)
-        for (int ci = at; ci < nin; ci += C::kAuxThreads) {
-            const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
-            const bool inb = colx < slice1;
-            unsigned char* dst = xs + ci * cs;
-#pragma unroll
-            for (int g4 = 0; g4 < NT; g4 += 4) {
-                if (g4 < fp.ntp) {
-                    uint4 v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        v[u] = make_uint4(0u, 0u, 0u, 0u);
-                        if (g4 + u < ntok && inb)
-                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
-                        if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(x_ready);
-        // pass 2 (rows shards): this CTA's share of the columns outside the layer's slice
-        const int64_t nch = fp.Kfull / 8;
-        const int64_t in0 = fp.x_col0 / 8, in1 = (fp.x_col0 + p.K) / 8;
-        const int64_t nout = nch - (in1 - in0);
-        const int64_t o0 = (nout * split) / ks, o1 = (nout * (split + 1)) / ks;
-        for (int64_t j = o0 + at; j < o1; j += C::kAuxThreads) {
-            const int64_t ch = j < in0 ? j : j + (in1 - in0);
-#pragma unroll
-            for (int g4 = 0; g4 < NT; g4 += 4) {
-                if (g4 < ntok) {
-                    uint4 v[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        v[u] = make_uint4(0u, 0u, 0u, 0u);
-                        if (g4 + u < ntok)
-                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
-                }
-            }
-        }
-        // block sums of this CTA (f64 from here on)
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-            if (t < ntok) {
-                double d1 = a1[t], d2 = a2[t], d3 = a3[t];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    d1 += __shfl_down_sync(0xffffffffu, d1, o);
-                    d2 += __shfl_down_sync(0xffffffffu, d2, o);
-                    d3 += __shfl_down_sync(0xffffffffu, d3, o);
-                }
-                if (lane == 0) {
-                    s_red[0][t][wi] = d1;
-                    s_red[1][t][wi] = d2;
-                    s_red[2][t][wi] = d3;
-                }
-            }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (ks > 1) {
-            cluster_wait();  // every mbarrier of the cluster is initialised
-            if (wi == 0 && lane < ks) {
-                // lane r sends this CTA's sums to rank r, into slot [split]
-                const uint32_t dst = dsmem_addr(rstats + split * NT * 3, static_cast<uint32_t>(lane));
-                const uint32_t bar = dsmem_addr(stats_bar, static_cast<uint32_t>(lane));
-                for (int t = 0; t < ntok; ++t)
-                    for (int q = 0; q < 3; ++q)
-                        st_async_f64(dst + (t * 3 + q) * 8,
-                                     ((s_red[q][t][0] + s_red[q][t][1]) + s_red[q][t][2]) + s_red[q][t][3], bar);
-            }
-        } else if (at == 0) {
-            for (int t = 0; t < ntok; ++t)
-                for (int q = 0; q < 3; ++q)
-                    rstats[t * 3 + q] = ((s_red[q][t][0] + s_red[q][t][1]) + s_red[q][t][2]) + s_red[q][t][3];
-        }
-        if (at == 0) {
-            bool ok = ks == 1 || mbar_wait(stats_bar, 0, p.status);
-            // each thread summed at most T values sequentially in f32 (both passes)
-            const int64_t kbmax = (p.KB + ks - 1) / ks;
-            const int64_t omax = (nout + ks - 1) / ks;
-            const double T = 8.0 * static_cast<double>((kbmax * 8 + C::kAuxThreads - 1) / C::kAuxThreads +
-                                                       (omax + C::kAuxThreads - 1) / C::kAuxThreads);
-            const double u = 5.9604644775390625e-08;
-            const double gT = 2.0 * T * u / (1.0 - T * u);
-            unsigned m = 0u;
-            for (int t = 0; t < ntok && ok; ++t) {
-                double S1 = 0.0, S2 = 0.0, SA = 0.0;
-                for (int r = 0; r < ks; ++r) {
-                    S1 += rstats[(r * NT + t) * 3 + 0];
-                    S2 += rstats[(r * NT + t) * 3 + 1];
-                    SA += rstats[(r * NT + t) * 3 + 2];
-                }
-                const void* xrow = static_cast<const unsigned char*>(fp.x) + (p.tok0 + t) * fp.x_stride * 2;
-                const bool r = p.route_all ? true
-                                           : route_token(S1, S2, SA, fp.Kfull, fp.t4, fp.t8, xrow, fp.x_dtype, nullptr,
-                                                         gT * SA, gT * S2);
-                if (r) m |= 1u << t;
-            }
-            if (!ok) s_abort = 1;
-            s_mask = m;
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        const unsigned mask = s_mask;
-        if (blockIdx.x == 0 && wi == 0) {
-            for (int t = lane; t < ntok; t += 32) {
-                const int r = (mask >> t) & 1u;
-                if (fp.mask_out) fp.mask_out[p.tok0 + t] = static_cast<uint8_t>(r);
-                if (fp.ridx_out && r) fp.ridx_out[__popc(mask & ((1u << t) - 1u))] = static_cast<int32_t>(p.tok0 + t);
-            }
-            if (lane == 0 && fp.nrouted_out) *fp.nrouted_out = __popc(mask);
-        }
-        // dW of this thread's row for the routed tokens, x from the staged copy, column order
-        const int64_t row = rt * 128 + at;
-        if (mask != 0u && row < p.N && p.nnz > 0) {
-            auto add_entry = [&](int64_t cl, int8_t q) {
-                const float v = __fmul_rn(static_cast<float>(q), p.ds);
-                const unsigned char* xp = xs + ((cl >> 3) * fp.ntp) * 16 + (cl & 7) * 2;
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                    if ((mask >> t) & 1u)
-                        corr[t] = __fadd_rn(corr[t], __fmul_rn(h2f(*reinterpret_cast<const uint16_t*>(xp + t * 16)), v));
-            };
-            if (use_blk) {
-                if (!mbar_wait(dw_ready, 0, p.status)) {
-                    s_abort = 1;
-                } else {
-                    const uint16_t* roff = reinterpret_cast<const uint16_t*>(dws);
-                    const int n = roff[128];
-                    const uint16_t* bcol = reinterpret_cast<const uint16_t*>(dws + 272);
-                    const int8_t* bval = reinterpret_cast<const int8_t*>(dws + 272 + ((n * 2 + 15) / 16) * 16);
-                    for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
-                }
-            } else {
-                const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
-                const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, kb_begin * 64);
-                const int64_t e1 = (ks == 1) ? hi : lower_bound_u16(p.col, e0, hi, kb_end * 64);
-                for (int64_t e = e0; e < e1; e += 8) {
-                    const int cnt = static_cast<int>(imin64(8, e1 - e));
-                    int64_t cc[8];
-                    int8_t vv[8];
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        cc[u] = u < cnt ? static_cast<int64_t>(p.col[e + u]) - kb_begin * 64 : 0;
-                        vv[u] = u < cnt ? p.val[e + u] : 0;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 8; ++u)
-                        if (u < cnt) add_entry(cc[u], vv[u]);
-                }
-            }
-        }
-    } else if (ks > 1) {
-        __syncwarp();
-        cluster_wait();
-    }
+    __syncwarp();
+    if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
     __syncthreads();
     if (s_abort && warp == C::kProducerWarp && lane == 0) {
         for (int it = issued > S ? issued - S : 0; it < issued; ++it)
             mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
-        if (use_blk) mbar_wait(dw_ready, 0, nullptr, kDrainNs);
+        if (c.use_blk) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
     }
     if (warp < C::kAuxWarp0) return;
-    pdl_wait();
-    // thread `at`: this split's contribution to row `at` (acc * row scale + dW; 0 past N)
-    const int64_t row = rt * 128 + at;
-    const float sc = row < p.N ? p.scale[row] : 0.0f;
+    const int64_t row = c.rt * 128 + at;
+    const float sc = row < p.N ? __ldg(p.scale + row) : 0.0f;
     float v[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;
-    auto store_row = [&](int64_t r, const float* w) {
-        for (int t = 0; t < ntok; ++t) {
-            const int64_t oi = (p.tok0 + t) * p.N + r;
-            if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = w[t];
-            else store_output(p.y, p.y_dtype, oi, w[t], p.bias, r);
-        }
-    };
-    if (ks == 1) {
-        if (!s_abort && row < p.N) store_row(row, v);
-        return;
-    }
-    {
-        // push the row to its owner: rank o owns rows [128 o / ks, 128 (o+1) / ks)
-        const int o = (at * ks + ks - 1) / 128;
-        const int orb = (128 * o) / ks, onr = (128 * (o + 1)) / ks - orb;
-        const uint32_t dst = dsmem_addr(rbuf + (split * onr + (at - orb)) * NT, static_cast<uint32_t>(o));
-        const uint32_t bar = dsmem_addr(red_bar, static_cast<uint32_t>(o));
-        st_async_v4_f32(dst, v[0], v[1], v[2], v[3], bar);
-        st_async_v4_f32(dst + 16, v[4], v[5], v[6], v[7], bar);
-    }
-    if (at < nr) {
-        // owner: rows rb + at, the splits added in rank order
-        const bool ok = mbar_wait(red_bar, 0, p.status);
-        const int64_t r = rt * 128 + rb + at;
-        if (ok && !s_abort && r < p.N) {
-            float w[NT];
-#pragma unroll
-            for (int t = 0; t < NT; ++t) w[t] = 0.0f;
-            for (int sp = 0; sp < ks; ++sp) {
-#pragma unroll
-                for (int t = 0; t < NT; ++t) w[t] = __fadd_rn(w[t], rbuf[(sp * nr + at) * NT + t]);
-            }
-            store_row(r, w);
-        }
-    }
+    fused_aux_finish(c, at, v);
 }
 
 // ---------------------------------------------------------------- launchers
@@ -1190,22 +1437,39 @@ cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
     fp.dwblk = L.dwblk;
     fp.dwoff = L.dwoff;
     fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
-    static std::atomic<uint64_t> flags{0};
+    fp.rc = route_consts(fp.Kfull);
+    {
+        // each auxiliary thread adds at most T values sequentially in f32 (both passes), then
+        // five shuffle levels add partial sums; the bound uses the depth, doubled for safety
+        const int64_t ks = p.ksplit;
+        const int64_t kbmax = (L.KB + ks - 1) / ks;
+        const int64_t nout = fp.Kfull / 8 - L.K / 8;
+        const int64_t omax = (nout + ks - 1) / ks;
+        constexpr int64_t A = FusedRegions::kAuxThreads;
+        const int64_t T = 8 * ((kbmax * 8 + A - 1) / A + (omax + A - 1) / A) + 5;
+        const double u = 5.9604644775390625e-08;
+        fp.gT = 2.0 * static_cast<double>(T) * u / (1.0 - static_cast<double>(T) * u);
+    }
+    const bool tc = L.mode == SC_MODE_FAST_TC;
+    auto kern = tc ? k_ctarq_fused_tc : k_ctarq_fused_mma;
+    const int threads = tc ? FusedTcCfg::kThreads : FusedMmaCfg::kThreads;
+    const int smem = tc ? FusedTcCfg::kTotal : FusedMmaCfg::kTotal;
+    static std::atomic<uint64_t> flags[2] = {{0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    if (!(flags.load() & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, FusedCfg::kTotal);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (!(flags[tc].load() & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e == cudaSuccess)  // two CTAs per SM need the largest shared-memory carveout
-            e = cudaFuncSetAttribute(k_ctarq_fused, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
-        flags.fetch_or(bit);
+        flags[tc].fetch_or(bit);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((L.Np / 128) * p.ksplit));
-    cfg.blockDim = dim3(FusedCfg::kThreads);
-    cfg.dynamicSmemBytes = FusedCfg::kTotal;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1216,12 +1480,12 @@ cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = p.ksplit > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, k_ctarq_fused, fp);
+    return cudaLaunchKernelEx(&cfg, kern, fp);
 }
 
 int fused_max_kb(int64_t m) {
     const int ntp = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
-    return FusedCfg::kXsBytes / (128 * ntp);
+    return FusedRegions::kXsBytes / (128 * ntp);
 }
 
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s) {

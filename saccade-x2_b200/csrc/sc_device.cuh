@@ -107,6 +107,10 @@ __device__ __forceinline__ double ld_dsmem_f64(uint32_t addr) {
 }
 // Split cluster barrier: every thread of the cluster arrives once and waits once.
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+// Relaxed arrive: enough after mbarrier initialisation, which fence_mbar_init() has released.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 // Stores into the shared memory of a cluster CTA (addresses from dsmem_addr) that complete
 // their bytes on that CTA's mbarrier `rbar`; the receiver waits on its own mbarrier.
@@ -310,6 +314,13 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         : "memory");
 }
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
+// One lane of a converged warp (the same one every time): issues tcgen05 work in warp-uniform
+// loops so that addresses and descriptors stay in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+    return pred != 0;
+}
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
@@ -400,14 +411,23 @@ static __device__ __noinline__ float exact_variance(const void* xrow, int x_dtyp
 //
 // S1, S2, SA may themselves carry a summation error: E1x, E2x bound |S1 - sum x| and
 // |S2 - sum x^2| (0 for exact sums); they widen the band accordingly.
-__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, float t4, float t8,
-                                            const void* xrow, int x_dtype, float* score_out, double E1x = 0.0,
-                                            double E2x = 0.0) {
+// Constants of the bound below for a token of n values: inv_n = 1/n and
+// gam = gamma_{n-1} = (n-1)u / (1 - (n-1)u).
+struct RouteConsts {
+    double inv_n, gam;
+};
+__host__ __device__ inline RouteConsts route_consts(int64_t Kfull) {
     const double n = static_cast<double>(Kfull);
-    const double inv_n = 1.0 / n;  // products with 1/n differ from quotients by f64 ulps, far inside B
+    const double nu = (n - 1.0) * 5.9604644775390625e-08;
+    return RouteConsts{1.0 / n, nu / (1.0 - nu)};
+}
+
+__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, const RouteConsts& rc,
+                                            float t4, float t8, const void* xrow, int x_dtype, float* score_out,
+                                            double E1x = 0.0, double E2x = 0.0) {
     const double u = 5.9604644775390625e-08;  // 2^-24
-    const double nu = (n - 1.0) * u;
-    const double gam = nu / (1.0 - nu);
+    const double inv_n = rc.inv_n;            // products with 1/n differ from quotients by f64 ulps, far inside B
+    const double gam = rc.gam;
     const double E1 = gam * (SA + E1x) + E1x, E2 = gam * (S2 + E2x) + E2x;
     const double mean = S1 * inv_n, A = S2 * inv_n;
     const double errMean = (E1 + u * (fabs(S1) + E1)) * inv_n;
@@ -426,6 +446,11 @@ __device__ __forceinline__ bool route_token(double S1, double S2, double SA, int
     const float score = exact_variance(xrow, x_dtype, Kfull);
     if (score_out) *score_out = score;
     return route_rule_f32(score, t4, t8);
+}
+__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, float t4, float t8,
+                                            const void* xrow, int x_dtype, float* score_out, double E1x = 0.0,
+                                            double E2x = 0.0) {
+    return route_token(S1, S2, SA, Kfull, route_consts(Kfull), t4, t8, xrow, x_dtype, score_out, E1x, E2x);
 }
 
 }  // namespace sc

@@ -61,6 +61,7 @@ constexpr int64_t kDwBlockMax = 16 * 1024;
 #endif
 constexpr int kMaxFusedCluster = SC_FUSED_MAX_CLUSTER;  // CTAs of one row tile (cluster size)
 constexpr int kFusedCtasPerSm = SC_FUSED_CTAS_PER_SM;   // grid target of the fused kernel
+
 int fused_ksplit(const Layer& L);
 bool use_fused(const Layer& L, int64_t m);  // the router-fused decode kernel serves this call
 

@@ -13,7 +13,7 @@ LIB_PATH = os.environ.get("SACCADE_CTARQ_LIB", os.path.join(PKG_ROOT, "libsaccad
 
 SC_OK, SC_EINVAL, SC_ENONCONTIG, SC_ECUDA, SC_ETIMEOUT, SC_EDEVICE, SC_ENOMEM, SC_EUNSUPPORTED = range(8)
 SC_F16, SC_BF16, SC_F32 = 0, 1, 2
-SC_MODE_FAST, SC_MODE_EXACT = 0, 1
+SC_MODE_FAST, SC_MODE_EXACT, SC_MODE_FAST_TC = 0, 1, 2
 SC_SHARD_NONE, SC_SHARD_COLUMNS, SC_SHARD_ROWS = 0, 1, 2
 
 STATUS_NAMES = {

@@ -53,6 +53,15 @@ class SparseDeltaMatrix:
     scale: torch.Tensor
 
 
+_MODES = {"fast": _lib.SC_MODE_FAST, "exact": _lib.SC_MODE_EXACT, "fast_tc": _lib.SC_MODE_FAST_TC}
+
+
+def _mode_code(mode: str) -> int:
+    if mode not in _MODES:
+        raise ValueError(f"mode must be one of {sorted(_MODES)}, got {mode!r}")
+    return _MODES[mode]
+
+
 def _f16_bits(t: torch.Tensor) -> int:
     return int(t.reshape(-1)[:1].to(torch.float16).view(torch.int16).item()) & 0xFFFF
 
@@ -93,7 +102,8 @@ class SaccadeLinearOp:
 
     packed_base u32 [N, K/8] (8 nibbles of q+8 per word along K, compress.rs:54-83),
     scale_base f16 [N], optional SparseDeltaMatrix, SaccadeConfig thresholds.
-    mode "fast" (tensor cores, default) or "exact" (op.rs's f32 order, bit-identical).
+    mode "fast" (tensor cores, default), "fast_tc" (the same contract; decode dequantises the
+    weights into tensor memory for tcgen05 MMAs) or "exact" (op.rs's f32 order, bit-identical).
     shard=("columns"|"rows", index, count) keeps a tensor-parallel slice.
     """
 
@@ -152,7 +162,7 @@ class SaccadeLinearOp:
         d.t8 = float(config.t8)
         d.device = dev_index
         d.buffers_on_device = 1 if on_dev else 0
-        d.mode = _lib.SC_MODE_EXACT if mode == "exact" else _lib.SC_MODE_FAST
+        d.mode = _mode_code(mode)
         if shard is not None:
             kind, idx, cnt = shard
             d.shard_kind = {"columns": _lib.SC_SHARD_COLUMNS, "rows": _lib.SC_SHARD_ROWS}[kind]
@@ -190,7 +200,7 @@ class SaccadeLinearOp:
         LIB.sc_layer_get_info(self._h, ctypes.byref(self.info))
 
     def set_mode(self, mode: str) -> None:
-        check(LIB.sc_layer_set_mode(self._h, _lib.SC_MODE_EXACT if mode == "exact" else _lib.SC_MODE_FAST))
+        check(LIB.sc_layer_set_mode(self._h, _mode_code(mode)))
         self.mode = mode
 
     def check_device(self) -> None:
@@ -213,13 +223,21 @@ class SaccadeLinearOp:
         return m
 
     def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16,
-                bias: Optional[torch.Tensor] = None, return_routing: bool = False):
+                bias: Optional[torch.Tensor] = None, return_routing: bool = False,
+                out: Optional[torch.Tensor] = None):
         """op.rs:10-185.  x [..., K] f16/bf16 on this device -> y [..., N] (f16 by default).
-        bias (f32 [N]) is added after the f16 rounding; out_dtype f32/bf16 widens/rounds after."""
+        bias (f32 [N]) is added after the f16 rounding; out_dtype f32/bf16 widens/rounds after.
+        out: optional contiguous tensor of y's shape and out_dtype to write into (it is returned)."""
         if self.shard_kind == "rows":
             raise ValueError("a rows shard yields partial sums: use forward_partial + all-reduce + finalize")
         m = self._prep_x(x, self.in_features)
-        y = torch.empty(x.shape[:-1] + (self.out_features,), dtype=out_dtype, device=self.device)
+        shape = x.shape[:-1] + (self.out_features,)
+        if out is None:
+            y = torch.empty(shape, dtype=out_dtype, device=self.device)
+        else:
+            if out.shape != shape or out.dtype != out_dtype or out.device != self.device or not out.is_contiguous():
+                raise ValueError(f"out must be a contiguous {out_dtype} tensor of shape {tuple(shape)} on {self.device}")
+            y = out
         mask = torch.empty(m, dtype=torch.uint8, device=self.device) if return_routing else None
         ridx = torch.empty(max(m, 1), dtype=torch.int32, device=self.device) if return_routing else None
         nr = torch.zeros(1, dtype=torch.int32, device=self.device) if return_routing else None

@@ -80,10 +80,14 @@ def test_exact_mode_bit_identical(sc, n, k, m, fill):
     assert np.array_equal(y_bits(y), yr), "exact mode must reproduce op.rs bit for bit"
 
 
+FAST_MODES = ["fast", "fast_tc"]  # mma.sync and tcgen05 decode engines, one tolerance
+
+
+@pytest.mark.parametrize("mode", FAST_MODES)
 @pytest.mark.parametrize("n,k,m,fill", SHAPES)
-def test_fast_mode_within_tolerance(sc, n, k, m, fill):
+def test_fast_mode_within_tolerance(sc, n, k, m, fill, mode):
     case = make_case(n, k, m, fill, seed=n * 3 + k + m)
-    op = to_op(sc, case, mode="fast")
+    op = to_op(sc, case, mode=mode)
     y, mask, ridx = run_gpu(op, case.x_bits)
     yr, rr, acc_ref = case.oracle().forward(case.x_bits)
     assert np.array_equal(mask, rr), "router mask must equal the reference's"
@@ -99,7 +103,7 @@ def test_threshold_token_exactly_on_t4(sc):
     case = make_case(4864, 896, 16, 0.01, seed=42, boost=[1, 6, 9, 14])
     scores = [O.variance(case.x_bits[t]) for t in range(16)]
     assert case.t4 in scores
-    for mode in ("fast", "exact"):
+    for mode in ("fast", "fast_tc", "exact"):
         op = to_op(sc, case, mode=mode)
         _, mask, _ = run_gpu(op, case.x_bits)
         _, rr, _ = case.oracle().forward(case.x_bits)
@@ -113,7 +117,7 @@ def test_bf16_input(sc):
     xbf = torch.from_numpy(xf).to(torch.bfloat16)
     bf_bits = xbf.view(torch.int16).numpy().view(np.uint16)
     x16 = O.bf16_bits_to_f16_bits(bf_bits)
-    for mode in ("exact", "fast"):
+    for mode in ("exact", "fast", "fast_tc"):
         op = to_op(sc, case, mode=mode)
         y, mask, _ = op.forward(xbf.to("cuda:0"), return_routing=True)[:3]
         yr, rr, _ = case.oracle().forward(x16)
@@ -143,7 +147,7 @@ def test_no_delta_and_dense_delta(sc):
         case = make_case(96, 128, 5, fill, seed=11)
         if thr_case == "none":
             assert case.c.nnz == 0
-        for mode in ("exact", "fast"):
+        for mode in ("exact", "fast", "fast_tc"):
             op = to_op(sc, case, mode=mode)
             y, mask, _ = run_gpu(op, case.x_bits)
             yr, rr, _ = case.oracle().forward(case.x_bits)
@@ -169,7 +173,7 @@ def test_bypass(sc):
     case = make_case(128, 256, 4, 0.05, seed=3)
     try:
         sc.set_bypass_c_tarq(True)
-        for mode in ("exact", "fast"):
+        for mode in ("exact", "fast", "fast_tc"):
             op = to_op(sc, case, mode=mode)
             y, mask, _ = run_gpu(op, case.x_bits)
             yr, _, _ = case.oracle().forward(case.x_bits, bypass=True)
@@ -215,9 +219,11 @@ def test_rejects_bad_inputs(sc):
                                sc.SaccadeConfig(0.0, 1.0), 32, 64, device="cuda:0")
 
 
-def test_repeated_calls_reuse_workspace(sc):
-    case = make_case(384, 640, 12, 0.02, seed=8)
-    op = to_op(sc, case)
+@pytest.mark.parametrize("mode", FAST_MODES)
+@pytest.mark.parametrize("m", [3, 12])  # router-fused decode (cluster split-K) and router + decode
+def test_repeated_calls_reuse_workspace(sc, m, mode):
+    case = make_case(3840, 2560, m, 0.02, seed=8)
+    op = to_op(sc, case, mode=mode)
     yr, rr, _ = case.oracle().forward(case.x_bits)
     first = None
     for _ in range(3):
@@ -228,10 +234,11 @@ def test_repeated_calls_reuse_workspace(sc):
         assert np.array_equal(y_bits(y), first), "the fast path is deterministic run to run"
 
 
-@pytest.mark.parametrize("n,k,m", [(3584, 3584, 1), (18944, 3584, 4), (3584, 18944, 16)])
-def test_qwen2_7b_shapes(sc, n, k, m):
+@pytest.mark.parametrize("mode", FAST_MODES)
+@pytest.mark.parametrize("n,k,m", [(3584, 3584, 1), (18944, 3584, 4), (3584, 18944, 16), (512, 3584, 1)])
+def test_qwen2_7b_shapes(sc, n, k, m, mode):
     case = make_case(n, k, m, 0.01, seed=n + m, boost=[0])
-    op = to_op(sc, case, mode="fast")
+    op = to_op(sc, case, mode=mode)
     y, mask, _ = run_gpu(op, case.x_bits)
     yr, rr, acc_ref = case.oracle().forward(case.x_bits)
     assert np.array_equal(mask, rr)
@@ -254,14 +261,15 @@ def test_column_shards_concatenate(sc, count):
     assert np.array_equal(np.concatenate(parts, axis=1), yr)
 
 
+@pytest.mark.parametrize("mode", FAST_MODES)
 @pytest.mark.parametrize("count", [2, 4])
-def test_row_shards_sum_to_full(sc, count):
+def test_row_shards_sum_to_full(sc, count, mode):
     case = make_case(300, 1024, 5, 0.02, seed=41)
     _, rr, acc_ref = case.oracle().forward(case.x_bits)
     x = torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")
     total = None
     for i in range(count):
-        op = to_op(sc, case, mode="fast", shard=("rows", i, count))
+        op = to_op(sc, case, mode=mode, shard=("rows", i, count))
         part, mask = op.forward_partial(x, return_routing=True)
         assert np.array_equal(mask.cpu().numpy(), rr), "every shard routes on the whole token"
         total = part if total is None else total + part
