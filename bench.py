@@ -51,9 +51,11 @@ def parse():
     ap.add_argument("--fill", type=float, default=0.01)
     ap.add_argument("--route-frac", type=float, default=0.25)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="fast", choices=["fast", "fast_tc", "exact"])
+    ap.add_argument("--mode", default="fast", choices=["fast", "fast_tc", "fast_tc8", "exact"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-group", action="store_true",
+                    help="one launch per projection, the reference's calling pattern (no grouped q/k/v, gate/up)")
     return ap.parse_args()
 
 
@@ -65,10 +67,17 @@ def launches_per_call(args):
     return 1 + (1 if args.mode == "exact" else -(-args.tokens // 32))
 
 
+def launches_per_step(args, units):
+    """Kernels of one step: a group of layers takes one launch when it decodes fused."""
+    per = launches_per_call(args)
+    return sum(1 if (grp is not None and per == 1) else per * len(idx) for idx, grp in units)
+
+
 def launch_kind(args):
     if args.mode != "exact" and args.tokens <= 8:
-        return "k_ctarq_fused_tc (router-fused decode, tcgen05)" if args.mode == "fast_tc" else \
-            "k_ctarq_fused_mma (router-fused decode, mma.sync)"
+        return {"fast_tc": "k_ctarq_fused_tc<f16> (router-fused decode, tcgen05)",
+                "fast_tc8": "k_ctarq_fused_tc<fp8> (router-fused decode, tcgen05 e4m3)"}.get(
+            args.mode, "k_ctarq_fused_mma (router-fused decode, mma.sync)")
     return "k_decode_exact (+ k_router)" if args.mode == "exact" else "k_ctarq_tc / k_ctarq_mma (+ k_router)"
 
 
@@ -76,14 +85,24 @@ def call_bytes(n, k, m, nnz, routed):
     return 2 * m * k + n * k // 2 + 2 * n + (3 * nnz + 4 * (n + 1) if routed else 0) + 2 * m * n
 
 
+# Projections reading the same activations in the decoder (model.rs:217-219, 296-297): q, k, v
+# take the normed hidden state, gate and up the post-attention normed state.
+INPUT_OF = {"q": "attn", "k": "attn", "v": "attn", "o": "o", "gate": "mlp", "up": "mlp", "down": "down"}
+
+
 def stack_spec(layers, m, route_frac, seed):
-    """(layer, proj, N, K, boosted-token list) for every call of one step."""
+    """(layer, proj, N, K, boosted-token list) for every call of one step; calls that read the
+    same activations share their boosted tokens (each token of each input is boosted with
+    probability route_frac)."""
     rng = np.random.default_rng(seed)
     calls = []
     for li in range(layers):
+        boosted_of = {}
         for name, n, k in PROJ:
-            boosted = [t for t in range(m) if rng.random() < route_frac]
-            calls.append((li, name, n, k, boosted))
+            inp = INPUT_OF[name]
+            if inp not in boosted_of:
+                boosted_of[inp] = [t for t in range(m) if rng.random() < route_frac]
+            calls.append((li, name, n, k, boosted_of[inp]))
     return calls
 
 
@@ -280,6 +299,7 @@ def run_ours(args, rank, world):
     calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234 + rank)
     ops, xs, step_bytes, big = [], [], 0, []
     routed_calls = 0
+    x_of = {}  # (layer, input) -> activations shared by the calls that read them
     for li, name, n, k, boosted in calls:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
         scale = ((0.02 * (3.0 + torch.rand(n, device=dev, generator=gen))) / 7.0).to(torch.float16)
@@ -295,10 +315,13 @@ def run_ours(args, rank, world):
         op = sc.SaccadeLinearOp(packed, scale, sp, sc.SaccadeConfig(T4_BOOSTED, T8_NEVER), n, k, device=dev,
                                 mode=args.mode)
         del packed, scale, flat, rows, cols, rp, vals
-        x = torch.randn((args.tokens, k), device=dev, generator=gen)
-        for t in boosted:
-            x[t] *= 8.0
-        x = x.to(torch.float16)
+        key = (li, INPUT_OF[name])
+        if key not in x_of:
+            x = torch.randn((args.tokens, k), device=dev, generator=gen)
+            for t in boosted:
+                x[t] *= 8.0
+            x_of[key] = x.to(torch.float16)
+        x = x_of[key]
         b = call_bytes(n, k, args.tokens, op.delta_nnz, len(boosted) > 0)
         routed_calls += len(boosted) > 0
         ops.append(op)
@@ -309,34 +332,69 @@ def run_ours(args, rank, world):
     torch.cuda.synchronize()
 
     ys = [None] * len(ops)
+    # launches of one step: a group per input shared by several projections (q,k,v and gate,up),
+    # unless --no-group asks for one call per projection (the reference's calling pattern)
+    units = []  # (op indices, group or None)
+    i = 0
+    while i < len(ops):
+        j = i
+        while j + 1 < len(ops) and calls[j + 1][0] == calls[i][0] and \
+                INPUT_OF[calls[j + 1][1]] == INPUT_OF[calls[i][1]]:
+            j += 1
+        idx = list(range(i, j + 1))
+        if len(idx) > 1 and not args.no_group:
+            units.append((idx, sc.SaccadeLinearGroup([ops[t] for t in idx])))
+        else:
+            units.extend(([t], None) for t in idx)
+        i = j + 1
+
+    def run_unit(idx, grp, outs=None):
+        x = xs[idx[0]]
+        if grp is None:
+            return [ops[idx[0]].forward(x, out=None if outs is None else outs[0])]
+        return grp.forward(x, outs=outs)
 
     def step():
-        for i, op in enumerate(ops):
-            ys[i] = op.forward(xs[i])
+        for idx, grp in units:
+            for t, y in zip(idx, run_unit(idx, grp)):
+                ys[t] = y
+
+    big_set = {i for i, _ in big}
+    big_units = [(idx, grp) for idx, grp in units if idx[0] in big_set]
 
     def big_step():
-        for i, _ in big:
-            ys[i] = ops[i].forward(xs[i])
+        for idx, grp in big_units:
+            for t, y in zip(idx, run_unit(idx, grp)):
+                ys[t] = y
 
     g_step = sc.CapturedStep(step, dev)
     g_big = sc.CapturedStep(big_step, dev)
 
     # end to end through the public API: every call's input from one pinned host buffer (one
     # host->device copy), every output into one device buffer read back by one device->host copy
-    xsz = [x.numel() for x in xs]
+    first_of = {}
+    for t, x in enumerate(xs):
+        first_of.setdefault(id(x), t)
+    uniq = sorted(first_of.values())
+    xsz = [xs[t].numel() for t in uniq]
     ysz = [args.tokens * op.out_features for op in ops]
-    x_host = torch.cat([x.reshape(-1) for x in xs]).cpu().pin_memory()
+    x_host = torch.cat([xs[t].reshape(-1) for t in uniq]).cpu().pin_memory()
     y_host = torch.empty(sum(ysz), dtype=torch.float16).pin_memory()
     x_dev = torch.empty_like(x_host, device=dev)
     y_dev = torch.empty(sum(ysz), dtype=torch.float16, device=dev)
-    x_views = list(torch.split(x_dev, xsz))
+    x_views_u = dict(zip(uniq, torch.split(x_dev, xsz)))
+    x_views = [x_views_u[first_of[id(x)]] for x in xs]
     y_views = list(torch.split(y_dev, ysz))
 
     def e2e_step():
         x_dev.copy_(x_host, non_blocking=True)
-        for i, op in enumerate(ops):
-            op.forward(x_views[i].view(args.tokens, op.in_features),
-                       out=y_views[i].view(args.tokens, op.out_features))
+        for idx, grp in units:
+            x = x_views[idx[0]].view(args.tokens, ops[idx[0]].in_features)
+            outs = [y_views[t].view(args.tokens, ops[t].out_features) for t in idx]
+            if grp is None:
+                ops[idx[0]].forward(x, out=outs[0])
+            else:
+                grp.forward(x, outs=outs)
         y_host.copy_(y_dev, non_blocking=True)
 
     g_e2e = sc.CapturedStep(e2e_step, dev)
@@ -401,17 +459,19 @@ def run_ours(args, rank, world):
                    "layers": args.layers, "calls_per_step": len(ops), "routed_calls_per_step": routed_calls,
                    "dw_fill": args.fill, "mode": args.mode, "bytes_per_step": step_bytes,
                    "weights": "int4 base + i8 dW, f32 accumulation", "l2": "inputs > L2 (3.3 GB of weights)",
-                   "parallelism": f"replicas{world}", "graph": "one CUDA graph per step"},
+                   "parallelism": f"replicas{world}", "graph": "one CUDA graph per step",
+                   "launch_units": "q,k,v and gate,up grouped (sc_forward_group)" if not args.no_group
+                   else "one launch per projection", "launches_per_step": launches_per_step(args, units)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": launch_kind(args) + " on the gate/up/down calls (84 launches per step)",
+                     "kernel": launch_kind(args) + f" on the gate/up/down calls ({len(big_units)} launches per step)",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
         "e2e": {"value": round(step_bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "how": "one pinned host->device copy of all inputs, the 196 calls, one device->host copy of "
                        "all outputs; captured step, host sync each step"},
-        "gpu_launches": launches_per_call(args) * len(ops) * args.steps,
+        "gpu_launches": launches_per_step(args, units) * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args)

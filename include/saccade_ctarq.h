@@ -39,6 +39,7 @@ extern "C" {
 #endif
 
 #define SC_ABI_VERSION 1
+#define SC_GROUP_MAX 4      /* layers per sc_group */
 
 #if defined(__GNUC__)
 #define SC_API __attribute__((visibility("default")))
@@ -63,8 +64,11 @@ typedef enum sc_dtype { SC_F16 = 0, SC_BF16 = 1, SC_F32 = 2 } sc_dtype;
 typedef enum sc_mode {
     SC_MODE_FAST = 0,   /* tensor cores, f32 accumulation in hardware order (default) */
     SC_MODE_EXACT = 1,  /* CUDA cores in op.rs's exact 4-accumulator f32 order: bit-identical Y */
-    SC_MODE_FAST_TC = 2 /* as SC_MODE_FAST (same tolerance); decode of <= 8 tokens dequantises the
-                         * weights into tensor memory and runs tcgen05 MMAs instead of mma.sync */
+    SC_MODE_FAST_TC = 2, /* as SC_MODE_FAST (same tolerance); decode of <= 8 tokens dequantises the
+                          * weights into tensor memory and runs tcgen05 MMAs instead of mma.sync */
+    SC_MODE_FAST_TC8 = 3 /* as SC_MODE_FAST_TC; one-token decode runs fp8 (e4m3) tcgen05 MMAs on an
+                          * exact 8-column e4m3 split of x (elements below 2^-34 of their slice's
+                          * maximum keep an error under that bound; inf/nan inputs give nan rows) */
 } sc_mode;
 
 typedef enum sc_shard { SC_SHARD_NONE = 0, SC_SHARD_COLUMNS = 1, SC_SHARD_ROWS = 2 } sc_shard;
@@ -146,6 +150,25 @@ SC_API sc_status sc_forward_ws(const sc_layer* layer, const void* x, int x_dtype
                         void* y, int y_dtype, const float* bias,
                         uint8_t* mask_out, int32_t* routed_idx_out, int32_t* n_routed_out,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Groups: layers that read the same input -- the q, k and v projections of an attention block,
+ * or the gate and up projections of an MLP -- computed by one launch.  No counterpart in the
+ * reference, which applies each projection separately (saccade-runner/src/model.rs:217-219 and
+ * 296-297); every output, mask and routed list is bit for bit what sc_forward on that layer
+ * gives.  A group holds 1..SC_GROUP_MAX layers on one device with the same in_features and input
+ * columns (no ROWS shards); it references the layers, which must outlive it.  sc_forward_group
+ * takes arrays of `count` outputs (y) and optional per-layer arrays (bias, mask_out,
+ * routed_idx_out, n_routed_out; NULL for none); the workspace is as for sc_forward_ws, sized for
+ * the largest sc_workspace_size of the group's layers.  Layers whose decode cannot share one
+ * launch (different split or engine, more than 8 tokens) run one after another on the stream. */
+typedef struct sc_group sc_group;
+SC_API sc_status sc_group_create(sc_layer* const* layers, int count, sc_group** out);
+SC_API void sc_group_destroy(sc_group* group);
+SC_API sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, int64_t m,
+                                  void* const* y, int y_dtype, const float* const* bias,
+                                  uint8_t* const* mask_out, int32_t* const* routed_idx_out,
+                                  int32_t* const* n_routed_out, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 /* sc_forward_static has no counterpart in the reference.  It is sc_forward without any
  * allocation: its scratch is a file-scope __device__ array of SC_STATIC_SCRATCH_BYTES inside

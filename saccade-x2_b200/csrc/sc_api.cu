@@ -188,7 +188,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         f.ws_partial = reinterpret_cast<float*>(base + w.partial);
         f.ws_rtcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
         f.ksplit = w.ksplit;
-        cudaError_t e = launch_decode_fused(f, stream);
+        cudaError_t e = launch_decode_fused(&f, 1, stream);
         if (e != cudaSuccess) return cuda_fail(e, "fused decode launch");
         return SC_OK;
     }
@@ -294,6 +294,10 @@ struct sc_layer {
     Layer L;
 };
 
+struct sc_group {
+    std::vector<const sc_layer*> layers;
+};
+
 extern "C" {
 
 int sc_abi_version(void) { return SC_ABI_VERSION; }
@@ -352,7 +356,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
         set_error("sc_layer_create: delta_nnz > 0 needs row_ptrs, col_indices and values");
         return SC_EINVAL;
     }
-    if (desc->mode != SC_MODE_FAST && desc->mode != SC_MODE_EXACT && desc->mode != SC_MODE_FAST_TC) {
+    if (desc->mode < SC_MODE_FAST || desc->mode > SC_MODE_FAST_TC8) {
         set_error("sc_layer_create: unknown mode");
         return SC_EINVAL;
     }
@@ -633,7 +637,7 @@ sc_status sc_layer_set_thresholds(sc_layer* layer, float t4, float t8) {
 }
 
 sc_status sc_layer_set_mode(sc_layer* layer, int mode) {
-    if (!layer || (mode != SC_MODE_FAST && mode != SC_MODE_EXACT && mode != SC_MODE_FAST_TC)) {
+    if (!layer || mode < SC_MODE_FAST || mode > SC_MODE_FAST_TC8) {
         set_error("sc_layer_set_mode: bad argument");
         return SC_EINVAL;
     }
@@ -729,6 +733,108 @@ sc_status sc_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dty
     }
     cudaError_t e = launch_finalize(acc, m, n, y, y_dtype, bias, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sc_finalize launch");
+    return SC_OK;
+}
+
+sc_status sc_group_create(sc_layer* const* layers, int count, sc_group** out) {
+    if (!out || !layers || count < 1 || count > SC_GROUP_MAX) {
+        set_error("sc_group_create: need 1.." + std::to_string(SC_GROUP_MAX) + " layers");
+        return SC_EINVAL;
+    }
+    *out = nullptr;
+    for (int i = 0; i < count; ++i) {
+        if (!layers[i]) {
+            set_error("sc_group_create: null layer");
+            return SC_EINVAL;
+        }
+        const Layer& L = layers[i]->L;
+        const Layer& L0 = layers[0]->L;
+        if (L.device != L0.device || L.K != L0.K || L.fullK != L0.fullK || L.col_begin != L0.col_begin) {
+            set_error("sc_group_create: layers of a group share the device and the input columns");
+            return SC_EINVAL;
+        }
+        if (L.shard_kind == SC_SHARD_ROWS) {
+            set_error("sc_group_create: ROWS shards produce partial sums; group them through sc_forward_partial");
+            return SC_EINVAL;
+        }
+    }
+    sc_group* g = new sc_group;
+    g->layers.assign(layers, layers + count);
+    *out = g;
+    return SC_OK;
+}
+
+void sc_group_destroy(sc_group* group) { delete group; }
+
+sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, int64_t m, void* const* y, int y_dtype,
+                           const float* const* bias, uint8_t* const* mask_out, int32_t* const* routed_idx_out,
+                           int32_t* const* n_routed_out, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!group || !y) {
+        set_error("sc_forward_group: null group or output array");
+        return SC_EINVAL;
+    }
+    if (m <= 0) return m == 0 ? SC_OK : (set_error("sc_forward_group: negative token count"), SC_EINVAL);
+    const int n = static_cast<int>(group->layers.size());
+    const Layer& L0 = group->layers[0]->L;
+    DeviceGuard guard(L0.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward_group: set device");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // one launch when every layer takes the router-fused decode with the same split
+    bool one = true;
+    for (int i = 0; i < n; ++i) {
+        const Layer& L = group->layers[i]->L;
+        one = one && use_fused(L, m) && L.ks_fused == L0.ks_fused && L.mode == L0.mode;
+    }
+    if (one) {
+        if (x_dtype != SC_F16 && x_dtype != SC_BF16) {
+            set_error("sc_forward_group: x dtype must be F16 or BF16");
+            return SC_EINVAL;
+        }
+        if (y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32) {
+            set_error("sc_forward_group: y dtype must be F16, BF16 or F32");
+            return SC_EINVAL;
+        }
+        if (!x) {
+            set_error("sc_forward_group: null x");
+            return SC_EINVAL;
+        }
+        const bool bypass_now = g_bypass.load() != 0;
+        FusedArgs f[SC_GROUP_MAX];
+        for (int i = 0; i < n; ++i) {
+            const Layer& L = group->layers[i]->L;
+            if (!y[i]) {
+                set_error("sc_forward_group: null output " + std::to_string(i));
+                return SC_EINVAL;
+            }
+            FusedArgs& a = f[i];
+            a.L = &L;
+            a.x = x;
+            a.x_dtype = x_dtype;
+            a.x_stride = L.K;
+            a.x_col0 = 0;
+            a.m = m;
+            a.route_all = bypass_now ? 1 : 0;
+            a.y = y[i];
+            a.y_dtype = y_dtype;
+            a.bias = bias ? bias[i] : nullptr;
+            a.partial_out = 0;
+            a.mask_out = mask_out ? mask_out[i] : nullptr;
+            a.ridx_out = routed_idx_out ? routed_idx_out[i] : nullptr;
+            a.nrouted_out = n_routed_out ? n_routed_out[i] : nullptr;
+            a.ws_partial = nullptr;
+            a.ws_rtcount = nullptr;
+            a.ksplit = L.ks_fused;
+        }
+        const cudaError_t e = launch_decode_fused(f, n, s);
+        if (e != cudaSuccess) return cuda_fail(e, "grouped decode launch");
+        return SC_OK;
+    }
+    for (int i = 0; i < n; ++i) {
+        const sc_status st = sc_forward_ws(group->layers[i], x, x_dtype, m, y[i], y_dtype, bias ? bias[i] : nullptr,
+                                           mask_out ? mask_out[i] : nullptr, routed_idx_out ? routed_idx_out[i] : nullptr,
+                                           n_routed_out ? n_routed_out[i] : nullptr, workspace, workspace_bytes, stream);
+        if (st != SC_OK) return st;
+    }
     return SC_OK;
 }
 

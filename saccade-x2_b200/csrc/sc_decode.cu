@@ -534,18 +534,56 @@ struct FusedParams {
     double gT;              // bound factor of this kernel's own f32 sums (gamma of their depth, doubled)
 };
 
+// Up to kGroupMax layers reading the same x in one launch: layer i owns the CTAs
+// [cta_start[i], cta_start[i+1]) (whole clusters, all layers with the same ksplit).
+constexpr int kGroupMax = SC_GROUP_MAX;
+struct FusedGroup {
+    int n;
+    int cta_start[kGroupMax + 1];
+    FusedParams p[kGroupMax];
+};
+
+// This CTA's layer; its parameters copied to shared memory by one thread (static indices only,
+// so the parameter block stays in the constant bank).
+__device__ __forceinline__ int fused_group_layer(const FusedGroup& g, int* bid) {
+    int gi = 0, start = 0;
+#pragma unroll
+    for (int i = 1; i < kGroupMax; ++i)
+        if (i < g.n && static_cast<int>(blockIdx.x) >= g.cta_start[i]) {
+            gi = i;
+            start = g.cta_start[i];
+        }
+    *bid = static_cast<int>(blockIdx.x) - start;
+    return gi;
+}
+__device__ __forceinline__ void fused_copy_params(const FusedGroup& g, int gi, FusedParams& dst) {
+#pragma unroll
+    for (int i = 0; i < kGroupMax; ++i)
+        if (i == gi) dst = g.p[i];
+}
+
 // Shared-memory regions after the weight ring, common to both engines.
 struct FusedRegions {
     static constexpr int NT = 8;
     static constexpr int kAuxThreads = 128;
     static constexpr int kXsBytes = 32 * 1024;   // staged x: 32768 / (128 * ntp) column blocks
     static constexpr int kPad = 128;             // MMA operand rows past the last staged chunk read here
+    // fp8 engine (one token): f16 x in [0, 8 KB), its e4m3 split in [8 KB, 32 KB) of the same region
+    static constexpr int kXb8 = 8 * 1024;
+    static constexpr int kMaxKbF8 = (kXsBytes - kXb8) / 512;
     static constexpr int kXs = 0;
     static constexpr int kDw = kXsBytes + kPad;
     static constexpr int kStats = kDw + static_cast<int>(kDwBlockMax);             // [ranks][8 tokens][3] f64
     static constexpr int kRed = kStats + kMaxFusedCluster * NT * 3 * 8;            // [ks][rows of rank][8] f32
     static constexpr int kBytes = kRed + (128 + kMaxFusedCluster) * NT * 4;
     static constexpr int kBars = 4;                                                // x_ready dw_ready stats red
+};
+
+// Scale and flags of the e4m3 split of this CTA's slice of x (one token).
+struct F8Split {
+    float wmax[4];   // per auxiliary warp: max |x|
+    int exp;         // x = 2^exp * sum_c 2^(-4c) X_c
+    int nonfinite;   // the slice holds an inf or nan: the fp8 engine writes nan for the tile
 };
 
 struct FusedCtx {
@@ -561,13 +599,16 @@ struct FusedCtx {
     int* s_abort;
     unsigned* s_mask;
     double (*s_red)[FusedRegions::NT][4];
+    struct F8Split* split8;  // e4m3 x split (fp8 engine) or null
+    unsigned char* xb8;      // e4m3 x columns: [32-column step][2 halves][8 columns][16 B]
     int64_t rt, kb_begin, kb_end;
+    int bid;  // CTA index within this layer's part of the grid
     int split, ks, nkb, ntok, cs, rb, nr;
     bool use_blk;
 };
 
-__device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, unsigned char* regions, uint64_t* bars, int* s_abort,
-                                              unsigned* s_mask, double (*s_red)[FusedRegions::NT][4]) {
+__device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, unsigned char* regions, uint64_t* bars,
+                                              int* s_abort, unsigned* s_mask, double (*s_red)[FusedRegions::NT][4]) {
     using R = FusedRegions;
     const TCParams& p = fp.t;
     FusedCtx c;
@@ -585,8 +626,9 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, unsigned ch
     c.s_red = s_red;
     c.ks = p.ksplit;
     c.ntok = p.ntok;
-    c.rt = blockIdx.x / c.ks;
-    c.split = static_cast<int>(blockIdx.x - c.rt * c.ks);   // = cluster rank
+    c.bid = bid;
+    c.rt = bid / c.ks;
+    c.split = static_cast<int>(bid - c.rt * c.ks);   // = cluster rank
     c.kb_begin = (p.KB * c.split) / c.ks;
     c.kb_end = (p.KB * (c.split + 1)) / c.ks;
     c.nkb = static_cast<int>(c.kb_end - c.kb_begin);
@@ -594,6 +636,8 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, unsigned ch
     c.rb = (128 * c.split) / c.ks;
     c.nr = (128 * (c.split + 1)) / c.ks - c.rb;
     c.use_blk = fp.dwblk != nullptr && p.nnz > 0;
+    c.split8 = nullptr;
+    c.xb8 = regions + R::kXs + R::kXb8;
     return c;
 }
 
@@ -628,7 +672,7 @@ __device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* r
                         &full[it], pol);
     }
     if (c.use_blk) {
-        const uint32_t o0 = c.fp->dwoff[blockIdx.x], o1 = c.fp->dwoff[blockIdx.x + 1];
+        const uint32_t o0 = c.fp->dwoff[c.bid], o1 = c.fp->dwoff[c.bid + 1];
         mbar_arrive_expect_tx(c.dw_ready, o1 - o0);
         bulk_g2s(const_cast<unsigned char*>(c.dws), c.fp->dwblk + o0, o1 - o0, c.dw_ready);
     }
@@ -666,6 +710,76 @@ __device__ __forceinline__ void sum_x8(uint4 v, float& a1, float& a2, float& a3)
         a1 += hi;
         a2 = fmaf(hi, hi, a2);
         a3 += fabsf(hi);
+    }
+}
+
+// fp8 engine, auxiliary threads after staging one token: split the staged slice of x into 8
+// e4m3 columns with x = 2^e * sum_c 2^(-4c) X_c.  e puts the slice's max |x| in [128, 256); each
+// column takes the e4m3 rounding of the residual scaled by 16^c and leaves an exact f32 residual,
+// so every element of magnitude >= max * 2^-34 is represented exactly (an f16 needs at most 3
+// columns once it is an e4m3 normal, and each column lifts a smaller one by 2^4); smaller ones
+// keep an error below 2^-34 of the slice maximum.  Columns are written as the MMA's K-major B
+// operand: [32-column step][2 halves of 16][8 columns][16 bytes].
+__device__ __forceinline__ void fused_split8(const FusedCtx& c, int at) {
+    const int wi = at >> 5, lane = at & 31;
+    const int nin = c.nkb * 8;
+    F8Split& sp = *c.split8;
+    float amax = 0.0f;
+    bool bad = false;
+    for (int ci = at; ci < nin; ci += FusedRegions::kAuxThreads) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(c.xs + ci * c.cs);
+        const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float lo = h2f(lo16(w[q])), hi = h2f(hi16(w[q]));
+            bad |= !isfinite(lo) || !isfinite(hi);
+            amax = fmaxf(amax, fmaxf(fabsf(lo), fabsf(hi)));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane == 0) {
+        sp.wmax[wi] = amax;
+        if (bad) sp.nonfinite = 1;
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const float m = fmaxf(fmaxf(sp.wmax[0], sp.wmax[1]), fmaxf(sp.wmax[2], sp.wmax[3]));
+    int e = 0;
+    if (m > 0.0f) {
+        frexpf(m, &e);  // m in [2^(e-1), 2^e)
+        e -= 8;         // m * 2^-e in [128, 256)
+    }
+    if (at == 0) sp.exp = e;
+    const float down = ldexpf(1.0f, -e);  // exact power of two (e in [-32, 8] for finite f16 input)
+    for (int ci = at; ci < nin; ci += FusedRegions::kAuxThreads) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(c.xs + ci * c.cs);
+        const uint32_t w[4] = {hv.x, hv.y, hv.z, hv.w};
+        float t[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            t[2 * q] = h2f(lo16(w[q])) * down;
+            t[2 * q + 1] = h2f(hi16(w[q])) * down;
+        }
+        unsigned char* b = c.xb8 + (ci >> 2) * 256 + ((ci >> 1) & 1) * 128 + (ci & 1) * 8;
+#pragma unroll 1
+        for (int col = 0; col < 8; ++col) {
+            uint32_t part[4];
+            bool rest = false;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                part[q] = cvt_e4m3x2_f32(t[2 * q], t[2 * q + 1]);
+                const uint32_t back = cvt_f16x2_e4m3x2(part[q]);
+                t[2 * q] = (t[2 * q] - h2f(lo16(back))) * 16.0f;          // exact residual, scaled exactly
+                t[2 * q + 1] = (t[2 * q + 1] - h2f(hi16(back))) * 16.0f;
+                rest |= t[2 * q] != 0.0f || t[2 * q + 1] != 0.0f;
+            }
+            *reinterpret_cast<uint2*>(b + col * 16) = make_uint2(part[0] | (part[1] << 16), part[2] | (part[3] << 16));
+            if (!rest) {
+                for (int z = col + 1; z < 8; ++z) *reinterpret_cast<uint2*>(b + z * 16) = make_uint2(0u, 0u);
+                break;
+            }
+        }
     }
 }
 
@@ -711,6 +825,7 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
             }
         }
     }
+    if (c.split8) fused_split8(c, at);
     fence_proxy_async_smem();  // the tensor cores read the staged x through the async proxy
     __syncwarp();
     if (lane == 0) mbar_arrive(c.x_ready);
@@ -791,7 +906,7 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
     const unsigned mask = *c.s_mask;
-    if (blockIdx.x == 0 && wi == 0) {
+    if (c.bid == 0 && wi == 0) {
         for (int t = lane; t < ntok; t += 32) {
             const int r = (mask >> t) & 1u;
             if (fp.mask_out) fp.mask_out[p.tok0 + t] = static_cast<uint8_t>(r);
@@ -886,6 +1001,10 @@ __device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, cons
 }
 
 // ---- engine 1: tcgen05 (weights dequantised into tensor memory)
+// The fp8 variant (F8, one token): weights (q - 8, exact in e4m3) go to tensor memory as e4m3 and
+// x as an exact split into 8 e4m3 columns with power-of-two scales (fused_split8), so each MMA
+// (kind::f8f6f4, K = 32) covers twice the columns of the f16 one and the A tiles are half the bytes.
+template <bool F8>
 struct FusedTcCfg {
     static constexpr int kDqWarps = 8;               // two per TMEM sub-partition, one 16-row tile each
     static constexpr int kProducerWarp = 8;
@@ -893,24 +1012,32 @@ struct FusedTcCfg {
     static constexpr int kAuxWarp0 = 10;
     static constexpr int kThreads = 14 * 32;
     // One ring stage is one hand-off between the dequantising warps and the MMA thread: every
-    // hand-off costs a few hundred cycles of latency, so it carries 3 blocks (12 MMAs).
+    // hand-off costs a few hundred cycles of latency, so it carries 3 blocks.
     static constexpr int SKB = 3;
     static constexpr int S = 4;
     static constexpr int kStageBytes = SKB * 4096;
-    static constexpr int kAB = 2;                    // TMEM A buffers, one stage (SKB * 32 columns) each
-    static constexpr uint32_t kTmemCols = 256;       // D in [0, 16), A buffers in [32, 32 + 2 * 96)
+    static constexpr int kColsPerBlock = F8 ? 16 : 32;        // TMEM columns of one 64-column block of A
+    static constexpr int kAB = F8 ? 4 : 2;                    // TMEM A buffers, one stage each
+    static constexpr uint32_t kTmemCols = 256;                // D in [0, 16), A buffers from column 32
     static constexpr int kRegions = S * kStageBytes;
     static constexpr int kBarOff = kRegions + FusedRegions::kBytes;
     static constexpr int kNumBars = 2 * S + 2 * kAB + 1 + FusedRegions::kBars;
     static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
     static constexpr int kTotal = kTmemSlotOff + 16;
-    static_assert(32 + kAB * SKB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
-    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+    static_assert(32 + kAB * SKB * kColsPerBlock <= static_cast<int>(kTmemCols), "tensor memory");
+    static_assert(2 * (kTotal + 2048 + 1024) <= 228 * 1024, "two CTAs per SM (with static and reserved smem)");
 };
 
-__global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(FusedParams fp) {
-    using C = FusedTcCfg;
-    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = FusedRegions::NT;
+template <bool F8>
+__global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(FusedGroup g) {
+    using C = FusedTcCfg<F8>;
+    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = FusedRegions::NT, CPB = C::kColsPerBlock;
+    pdl_launch_dependents();
+    __shared__ FusedParams fp;
+    int bid;
+    const int gi = fused_group_layer(g, &bid);
+    if (threadIdx.x == 0) fused_copy_params(g, gi, fp);
+    __syncthreads();
     const TCParams& p = fp.t;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -922,10 +1049,11 @@ __global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(Fuse
     __shared__ int s_abort;
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
-    const FusedCtx c = fused_ctx(fp, smem + C::kRegions, done + 1, &s_abort, &s_mask, s_red);
+    __shared__ F8Split s_split;
+    FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, done + 1, &s_abort, &s_mask, s_red);
+    if (F8) c.split8 = &s_split;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
@@ -939,6 +1067,7 @@ __global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(Fuse
         fused_init_bars(c);
         s_abort = 0;
         s_mask = 0u;
+        s_split.nonfinite = 0;
     }
     if (warp == C::kMmaWarp) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -957,26 +1086,31 @@ __global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(Fuse
         if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
     } else if (warp == C::kMmaWarp) {
         // the whole warp runs the loop (uniform); one elected lane issues
-        constexpr uint32_t idesc = idesc_f16_f32(128, 16);
+        constexpr uint32_t idesc = idesc_f16_f32(128, 16);  // e4m3 operands share the type code 0 of f16
         bool ok = __all_sync(0xffffffffu, mbar_wait(c.x_ready, 0, p.status));
         const int nst = (c.nkb + SKB - 1) / SKB;
-        // B descriptor of staged chunk `ch`: base + ch * ntp (start address in 16-byte units)
-        const uint64_t bd0 = desc_kmajor(c.xs, c.cs, 0);
-        const uint64_t ntp = static_cast<uint64_t>(fp.ntp);
+        // B descriptors: f16 x staged as [chunk][ntp][16 B] (one K = 16 step = 2 chunks); e4m3 x as
+        // [32-column step][2 halves][8 columns][16 B] (one K = 32 step = 256 B); rows 8..15 of the
+        // N = 16 operand alias rows 0..7 (SBO = 0) and are not read back
+        const uint64_t bd0 = F8 ? desc_kmajor(c.xb8, 128, 0) : desc_kmajor(c.xs, c.cs, 0);
+        const uint64_t step = F8 ? 16u : static_cast<uint64_t>(fp.ntp) * 2u;  // per K step, in 16-byte units
+        constexpr int kSteps = F8 ? 2 : 4;                                    // K steps per 64-column block
         for (int u = 0; u < nst && ok; ++u) {
             const int b = u % AB;
             ok = __all_sync(0xffffffffu, mbar_wait(&a_full[b], (u / AB) & 1, p.status));
             if (!ok) break;
             tc_fence_after();
             const int n = c.nkb - u * SKB < SKB ? c.nkb - u * SKB : SKB;
-            const uint32_t a0 = tmem + 32 + b * SKB * 32;
-            const uint64_t bu = bd0 + static_cast<uint64_t>(u * SKB * 8) * ntp;
+            const uint32_t a0 = tmem + 32 + b * SKB * CPB;
+            const uint64_t bu = bd0 + static_cast<uint64_t>(u * SKB * kSteps) * step;
             if (elect_one()) {
                 for (int k = 0; k < n; ++k) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)  // B: [chunk][ntp][16 B]; rows past ntok are not read back
-                        tc_mma_ts(tmem, a0 + k * 32 + i * 8, bu + static_cast<uint64_t>(k * 8 + 2 * i) * ntp, idesc,
-                                  (u | k | i) ? 1u : 0u);
+                    for (int i = 0; i < kSteps; ++i) {
+                        const uint64_t bdesc = bu + static_cast<uint64_t>(k * kSteps + i) * step;
+                        if (F8) tc_mma_ts_f8(tmem, a0 + k * CPB + i * 8, bdesc, idesc, (u | k | i) ? 1u : 0u);
+                        else tc_mma_ts(tmem, a0 + k * CPB + i * 8, bdesc, idesc, (u | k | i) ? 1u : 0u);
+                    }
                 }
                 tc_commit(&a_empty[b]);
             }
@@ -1015,11 +1149,23 @@ __global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(Fuse
             for (int k = 0; k < SKB; ++k) {
                 if (k < n) {
                     const uint32_t words[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
+                    const uint32_t col = tmem + lane_addr + 32 + (b * SKB + k) * CPB;
+                    if (F8) {
+                        // K = 32 step t covers the 16-column steps 2t, 2t+1: TMEM column 4 * (s % 2) + c
 #pragma unroll
-                    for (int st = 0; st < 4; ++st) {
-                        uint32_t h[4];
-                        dequant_word(words[st], h);
-                        tc_st_16x256b(tmem + lane_addr + 32 + (b * SKB + k) * 32 + st * 8, h[0], h[2], h[1], h[3]);
+                        for (int t = 0; t < 2; ++t) {
+                            uint32_t g0, g80, g1, g81;
+                            dequant_word_e4m3(words[2 * t], g0, g80);
+                            dequant_word_e4m3(words[2 * t + 1], g1, g81);
+                            tc_st_16x128b_x2(col + t * 8, g0, g80, g1, g81);
+                        }
+                    } else {
+#pragma unroll
+                        for (int st = 0; st < 4; ++st) {
+                            uint32_t h[4];
+                            dequant_word(words[st], h);
+                            tc_st_16x256b(col + st * 8, h[0], h[2], h[1], h[3]);
+                        }
                     }
                 }
             }
@@ -1044,9 +1190,20 @@ __global__ void __launch_bounds__(FusedTcCfg::kThreads, 2) k_ctarq_fused_tc(Fuse
         tc_ld8(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16), d);
         tc_wait_ld();
         if (!ok) s_abort = 1;
+        if (F8) {
+            // acc = 2^e * sum_c 2^(-4c) D_c (token 0), summed in f64 and rounded once
+            double a = 0.0;
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
-            v[t] = row < p.N ? __fadd_rn(__fmul_rn(__uint_as_float(d[t]), sc), corr[t]) : 0.0f;
+            for (int col = 0; col < 8; ++col) a += ldexp(static_cast<double>(__uint_as_float(d[col])), s_split.exp - 4 * col);
+            const float acc = s_split.nonfinite ? __int_as_float(0x7fc00000) : static_cast<float>(a);
+            v[0] = row < p.N ? __fadd_rn(__fmul_rn(acc, sc), corr[0]) : 0.0f;
+#pragma unroll
+            for (int t = 1; t < NT; ++t) v[t] = 0.0f;
+        } else {
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                v[t] = row < p.N ? __fadd_rn(__fmul_rn(__uint_as_float(d[t]), sc), corr[t]) : 0.0f;
+        }
     }
     __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
     tc_fence_before();
@@ -1078,12 +1235,18 @@ struct FusedMmaCfg {
     static constexpr int kRegions = kAccOff + 128 * kLd * 4;
     static constexpr int kBarOff = kRegions + FusedRegions::kBytes;
     static constexpr int kTotal = kBarOff + (2 * S + FusedRegions::kBars) * 8;
-    static_assert(2 * (kTotal + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+    static_assert(2 * (kTotal + 2048 + 1024) <= 228 * 1024, "two CTAs per SM (with static and reserved smem)");
 };
 
-__global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(FusedParams fp) {
+__global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(FusedGroup g) {
     using C = FusedMmaCfg;
     constexpr int SKB = C::SKB, S = C::S, NT = FusedRegions::NT;
+    pdl_launch_dependents();
+    __shared__ FusedParams fp;
+    int bid;
+    const int gi = fused_group_layer(g, &bid);
+    if (threadIdx.x == 0) fused_copy_params(g, gi, fp);
+    __syncthreads();
     const TCParams& p = fp.t;
     extern __shared__ __align__(1024) unsigned char smem[];
     float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
@@ -1092,11 +1255,10 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     __shared__ int s_abort;
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
-    const FusedCtx c = fused_ctx(fp, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red);
+    const FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nst = (c.nkb + SKB - 1) / SKB;
 
-    pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
@@ -1396,9 +1558,8 @@ __global__ void __launch_bounds__(128) k_decode_exact(ExactParams p) {
     }
 }
 
-cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
+static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     const Layer& L = *f.L;
-    FusedParams fp;
     TCParams& p = fp.t;
     p.wq = L.wq;
     p.scale = L.scale;
@@ -1438,36 +1599,53 @@ cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
     fp.dwoff = L.dwoff;
     fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
     fp.rc = route_consts(fp.Kfull);
-    {
-        // each auxiliary thread adds at most T values sequentially in f32 (both passes), then
-        // five shuffle levels add partial sums; the bound uses the depth, doubled for safety
-        const int64_t ks = p.ksplit;
-        const int64_t kbmax = (L.KB + ks - 1) / ks;
-        const int64_t nout = fp.Kfull / 8 - L.K / 8;
-        const int64_t omax = (nout + ks - 1) / ks;
-        constexpr int64_t A = FusedRegions::kAuxThreads;
-        const int64_t T = 8 * ((kbmax * 8 + A - 1) / A + (omax + A - 1) / A) + 5;
-        const double u = 5.9604644775390625e-08;
-        fp.gT = 2.0 * static_cast<double>(T) * u / (1.0 - static_cast<double>(T) * u);
+    // each auxiliary thread adds at most T values sequentially in f32 (both passes), then five
+    // shuffle levels add partial sums; the bound uses the depth, doubled for safety
+    const int64_t ks = p.ksplit;
+    const int64_t kbmax = (L.KB + ks - 1) / ks;
+    const int64_t nout = fp.Kfull / 8 - L.K / 8;
+    const int64_t omax = (nout + ks - 1) / ks;
+    constexpr int64_t A = FusedRegions::kAuxThreads;
+    const int64_t T = 8 * ((kbmax * 8 + A - 1) / A + (omax + A - 1) / A) + 5;
+    const double u = 5.9604644775390625e-08;
+    fp.gT = 2.0 * static_cast<double>(T) * u / (1.0 - static_cast<double>(T) * u);
+}
+
+cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s) {
+    if (n < 1 || n > kGroupMax) return cudaErrorInvalidValue;
+    FusedGroup g = {};
+    g.n = n;
+    int ctas = 0;
+    for (int i = 0; i < n; ++i) {
+        if (f[i].ksplit != f[0].ksplit || f[i].L->mode != f[0].L->mode) return cudaErrorInvalidValue;
+        fill_fused_params(f[i], g.p[i]);
+        g.cta_start[i] = ctas;
+        ctas += static_cast<int>((f[i].L->Np / 128) * f[i].ksplit);
     }
-    const bool tc = L.mode == SC_MODE_FAST_TC;
-    auto kern = tc ? k_ctarq_fused_tc : k_ctarq_fused_mma;
-    const int threads = tc ? FusedTcCfg::kThreads : FusedMmaCfg::kThreads;
-    const int smem = tc ? FusedTcCfg::kTotal : FusedMmaCfg::kTotal;
-    static std::atomic<uint64_t> flags[2] = {{0}, {0}};
+    for (int i = n; i <= kGroupMax; ++i) g.cta_start[i] = ctas;
+    const int ksplit = f[0].ksplit;
+    const bool tc = f[0].L->mode == SC_MODE_FAST_TC || f[0].L->mode == SC_MODE_FAST_TC8;
+    // one token in SC_MODE_FAST_TC8: the fp8 variant when the e4m3 split of x fits
+    bool f8 = f[0].L->mode == SC_MODE_FAST_TC8 && f[0].m == 1;
+    for (int i = 0; i < n && f8; ++i) f8 = (f[i].L->KB + ksplit - 1) / ksplit <= FusedRegions::kMaxKbF8;
+    const int which = f8 ? 2 : tc ? 1 : 0;
+    auto kern = f8 ? k_ctarq_fused_tc<true> : tc ? k_ctarq_fused_tc<false> : k_ctarq_fused_mma;
+    const int threads = f8 ? FusedTcCfg<true>::kThreads : tc ? FusedTcCfg<false>::kThreads : FusedMmaCfg::kThreads;
+    const int smem = f8 ? FusedTcCfg<true>::kTotal : tc ? FusedTcCfg<false>::kTotal : FusedMmaCfg::kTotal;
+    static std::atomic<uint64_t> flags[3] = {{0}, {0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    if (!(flags[tc].load() & bit)) {
+    if (!(flags[which].load() & bit)) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e == cudaSuccess)  // two CTAs per SM need the largest shared-memory carveout
             e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
-        flags[tc].fetch_or(bit);
+        flags[which].fetch_or(bit);
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>((L.Np / 128) * p.ksplit));
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
     cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -1475,12 +1653,12 @@ cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = static_cast<unsigned>(p.ksplit);
+    attr[1].val.clusterDim.x = static_cast<unsigned>(ksplit);
     attr[1].val.clusterDim.y = 1;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = p.ksplit > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, fp);
+    cfg.numAttrs = ksplit > 1 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, g);
 }
 
 int fused_max_kb(int64_t m) {

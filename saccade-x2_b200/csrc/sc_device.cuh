@@ -313,6 +313,52 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// kind::f8f6f4 (e4m3 A from tensor memory, e4m3 B from shared memory, f32 D), K = 32.
+__device__ __forceinline__ void tc_mma_ts_f8(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 16 lanes x 128 bits, twice along the columns: thread t writes r0 -> (lane t/4, column t%4),
+// r1 -> (lane t/4 + 8, column t%4), r2 -> (lane t/4, column 4 + t%4), r3 -> (lane t/4 + 8, column 4 + t%4).
+__device__ __forceinline__ void tc_st_16x128b_x2(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x128b.x2.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
+                 : "memory");
+}
+
+// ---------------------------------------------------------------- e4m3 (fp8) conversions
+// Two f16 -> two e4m3 (round to nearest even, saturating); low half -> low byte.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint32_t h2) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;" : "=h"(r) : "r"(h2));
+    return r;
+}
+// Two f32 -> two e4m3 (nearest even, saturating): lo -> low byte, hi -> high byte.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f32(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+// Two e4m3 (low byte, high byte) -> two f16 (exact).
+__device__ __forceinline__ uint32_t cvt_f16x2_e4m3x2(uint32_t e2) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(e2)));
+    return r;
+}
+
+// One device-layout word as e4m3 weights q - 8 (exact: |q - 8| <= 8): r_g = row g, columns
+// 4c..4c+3 of the 16-column step (bytes in column order), r_g8 = row g + 8 (see dequant_word).
+__device__ __forceinline__ void dequant_word_e4m3(uint32_t w, uint32_t& r_g, uint32_t& r_g8) {
+    uint32_t h[4];
+    dequant_word(w, h);  // h0 = row g cols 0,1; h1 = row g+8 cols 0,1; h2 = row g cols 2,3; h3 = row g+8 cols 2,3
+    r_g = __byte_perm(cvt_e4m3x2_f16x2(h[0]), cvt_e4m3x2_f16x2(h[2]), 0x5410);
+    r_g8 = __byte_perm(cvt_e4m3x2_f16x2(h[1]), cvt_e4m3x2_f16x2(h[3]), 0x5410);
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
 // One lane of a converged warp (the same one every time): issues tcgen05 work in warp-uniform
 // loops so that addresses and descriptors stay in uniform registers.

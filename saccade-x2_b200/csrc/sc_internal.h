@@ -167,7 +167,8 @@ struct FusedArgs {
     uint32_t* ws_rtcount;
     int ksplit;
 };
-cudaError_t launch_decode_fused(const FusedArgs& f, cudaStream_t s);
+// One launch for n (<= SC_GROUP_MAX) layers that read the same x, all with the same ksplit and mode.
+cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s);
 int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
 
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,

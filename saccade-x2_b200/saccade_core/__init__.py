@@ -8,11 +8,11 @@ from ._lib import CTarqError, LIB_PATH
 from .graph import CapturedStep
 from .compress import (ProfileRunner, compress_tensor_to_saccade, compute_percentile_threshold,
                        saccade_op_from_compressed)
-from .op import (SaccadeConfig, SaccadeLinearOp, SparseDeltaMatrix, finalize, is_c_tarq_bypassed,
-                 set_bypass_c_tarq, variance_heuristic)
+from .op import (SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDeltaMatrix, finalize,
+                 is_c_tarq_bypassed, set_bypass_c_tarq, variance_heuristic)
 
 __all__ = [
-    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearOp", "SparseDeltaMatrix",
+    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearGroup", "SaccadeLinearOp", "SparseDeltaMatrix",
     "compress_tensor_to_saccade", "compute_percentile_threshold", "finalize", "is_c_tarq_bypassed",
     "saccade_op_from_compressed", "set_bypass_c_tarq", "variance_heuristic",
 ]

@@ -13,7 +13,7 @@ LIB_PATH = os.environ.get("SACCADE_CTARQ_LIB", os.path.join(PKG_ROOT, "libsaccad
 
 SC_OK, SC_EINVAL, SC_ENONCONTIG, SC_ECUDA, SC_ETIMEOUT, SC_EDEVICE, SC_ENOMEM, SC_EUNSUPPORTED = range(8)
 SC_F16, SC_BF16, SC_F32 = 0, 1, 2
-SC_MODE_FAST, SC_MODE_EXACT, SC_MODE_FAST_TC = 0, 1, 2
+SC_MODE_FAST, SC_MODE_EXACT, SC_MODE_FAST_TC, SC_MODE_FAST_TC8 = 0, 1, 2, 3
 SC_SHARD_NONE, SC_SHARD_COLUMNS, SC_SHARD_ROWS = 0, 1, 2
 
 STATUS_NAMES = {
@@ -91,6 +91,9 @@ SIGNATURES = {
     "sc_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "sc_forward_ws": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_forward_static": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
+    "sc_group_create": (_int, [_vp, _int, _vp]),
+    "sc_group_destroy": (None, [_vp]),
+    "sc_forward_group": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_forward_partial": (_int, [_vp, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_finalize": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
     "sc_variance_heuristic": (_int, [_vp, _int, _i64, _i64, _vp, _vp]),

@@ -53,7 +53,8 @@ class SparseDeltaMatrix:
     scale: torch.Tensor
 
 
-_MODES = {"fast": _lib.SC_MODE_FAST, "exact": _lib.SC_MODE_EXACT, "fast_tc": _lib.SC_MODE_FAST_TC}
+_MODES = {"fast": _lib.SC_MODE_FAST, "exact": _lib.SC_MODE_EXACT, "fast_tc": _lib.SC_MODE_FAST_TC,
+          "fast_tc8": _lib.SC_MODE_FAST_TC8}
 
 
 def _mode_code(mode: str) -> int:
@@ -103,7 +104,8 @@ class SaccadeLinearOp:
     packed_base u32 [N, K/8] (8 nibbles of q+8 per word along K, compress.rs:54-83),
     scale_base f16 [N], optional SparseDeltaMatrix, SaccadeConfig thresholds.
     mode "fast" (tensor cores, default), "fast_tc" (the same contract; decode dequantises the
-    weights into tensor memory for tcgen05 MMAs) or "exact" (op.rs's f32 order, bit-identical).
+    weights into tensor memory for tcgen05 MMAs), "fast_tc8" (as fast_tc, one-token decode on fp8
+    tcgen05 MMAs with an exact e4m3 split of x) or "exact" (op.rs's f32 order, bit-identical).
     shard=("columns"|"rows", index, count) keeps a tensor-parallel slice.
     """
 
@@ -295,3 +297,62 @@ def variance_heuristic(x: torch.Tensor) -> torch.Tensor:
     check(LIB.sc_variance_heuristic(x.data_ptr(), _DT[x.dtype], m, k, out.data_ptr(),
                                     ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)))
     return out
+
+
+class SaccadeLinearGroup:
+    """Layers that read the same input -- q, k and v, or gate and up -- computed by one launch
+    (sc_group_create / sc_forward_group).  No reference counterpart (the reference applies each
+    projection separately, saccade-runner/src/model.rs:217-219, 296-297); forward(x) returns one
+    output per layer, bit for bit what that layer's forward(x) gives."""
+
+    def __init__(self, ops):
+        ops = list(ops)
+        if not 1 <= len(ops) <= 4:
+            raise ValueError("a group holds 1..4 layers")
+        self.ops = ops
+        self.device = ops[0].device
+        arr = (ctypes.c_void_p * len(ops))(*[op._h for op in ops])
+        h = ctypes.c_void_p()
+        check(LIB.sc_group_create(arr, len(ops), ctypes.byref(h)))
+        self._h = h
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and LIB is not None:
+            LIB.sc_group_destroy(h)
+            self._h = None
+
+    def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16, outs=None,
+                return_routing: bool = False):
+        n = len(self.ops)
+        m = self.ops[0]._prep_x(x, self.ops[0].in_features)
+        shapes = [x.shape[:-1] + (op.out_features,) for op in self.ops]
+        if outs is None:
+            ys = [torch.empty(sh, dtype=out_dtype, device=self.device) for sh in shapes]
+        else:
+            ys = list(outs)
+            for y, sh in zip(ys, shapes):
+                if y.shape != sh or y.dtype != out_dtype or not y.is_contiguous() or y.device != self.device:
+                    raise ValueError(f"outs must be contiguous {out_dtype} tensors of shapes {shapes}")
+        routing = None
+        if return_routing:
+            routing = [(torch.empty(m, dtype=torch.uint8, device=self.device),
+                        torch.empty(max(m, 1), dtype=torch.int32, device=self.device),
+                        torch.zeros(1, dtype=torch.int32, device=self.device)) for _ in range(n)]
+        if m > 0:
+            stream = torch.cuda.current_stream(self.device)
+            need = max(op.workspace_size(m) for op in self.ops)
+            ws = WORKSPACES.get(self.device, stream, need)
+            yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+            mp = rp = np_ = None
+            if routing is not None:
+                mp = (ctypes.c_void_p * n)(*[r[0].data_ptr() for r in routing])
+                rp = (ctypes.c_void_p * n)(*[r[1].data_ptr() for r in routing])
+                np_ = (ctypes.c_void_p * n)(*[r[2].data_ptr() for r in routing])
+            check(LIB.sc_forward_group(self._h, x.data_ptr(), _DT[x.dtype], m, yp, _DT[out_dtype], None, mp, rp, np_,
+                                       ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream)))
+        if return_routing:
+            return ys, routing
+        return ys
+
+    __call__ = forward

@@ -66,7 +66,7 @@ def test_oracle_reproduces_digests(name):
 # ------------------------------------------------------------------ the CUDA library on the fixtures
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["exact", "fast", "fast_tc"])
+@pytest.mark.parametrize("mode", ["exact", "fast", "fast_tc", "fast_tc8"])
 @pytest.mark.parametrize("spec", META["small"], ids=[s["name"] for s in META["small"]])
 def test_library_on_small_fixture(spec, mode):
     torch = pytest.importorskip("torch")

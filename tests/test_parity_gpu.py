@@ -80,7 +80,7 @@ def test_exact_mode_bit_identical(sc, n, k, m, fill):
     assert np.array_equal(y_bits(y), yr), "exact mode must reproduce op.rs bit for bit"
 
 
-FAST_MODES = ["fast", "fast_tc"]  # mma.sync and tcgen05 decode engines, one tolerance
+FAST_MODES = ["fast", "fast_tc", "fast_tc8"]  # mma.sync, tcgen05 f16 and fp8 decode engines, one tolerance
 
 
 @pytest.mark.parametrize("mode", FAST_MODES)
@@ -328,3 +328,65 @@ def test_end_to_end_from_dense_weights(sc):
     y, mask, _ = run_gpu(op, case.x_bits)
     yr, rr, _ = case.oracle().forward(case.x_bits)
     assert np.array_equal(mask, rr) and np.array_equal(y_bits(y), yr)
+
+
+# ------------------------------------------------------------------ groups (one launch, shared x)
+
+@pytest.mark.parametrize("mode", FAST_MODES + ["exact"])
+@pytest.mark.parametrize("shapes,m", [
+    ([(3584, 3584), (512, 3584), (512, 3584)], 1),   # q, k, v
+    ([(1024, 1024), (1024, 1024)], 4),               # gate/up-like pair
+    ([(256, 512), (128, 512), (384, 512), (130, 512)], 3),
+    ([(640, 768), (256, 768)], 20),                  # more than 8 tokens: one launch per layer
+])
+def test_group_matches_individual_calls(sc, shapes, m, mode):
+    k = shapes[0][1]
+    cases = [make_case(n, k, m, 0.02, seed=1000 + i, boost=[0]) for i, (n, _) in enumerate(shapes)]
+    x_bits = cases[0].x_bits
+    ops = [to_op(sc, c, mode=mode) for c in cases]
+    grp = sc.SaccadeLinearGroup(ops)
+    x = torch.from_numpy(x_bits.view(np.float16)).to("cuda:0")
+    ys, routing = grp.forward(x, return_routing=True)
+    torch.cuda.synchronize()
+    for op, c, y, (mask, ridx, nr) in zip(ops, cases, ys, routing):
+        yi, mi, ri, ni = op.forward(x, return_routing=True)
+        torch.cuda.synchronize()
+        op.check_device()
+        assert np.array_equal(y_bits(y), y_bits(yi)), "a group must reproduce the layer's own call bit for bit"
+        assert np.array_equal(mask.cpu().numpy(), mi.cpu().numpy())
+        assert int(nr.item()) == int(ni.item())
+        assert np.array_equal(ridx.cpu().numpy()[: int(nr.item())], ri.cpu().numpy()[: int(ni.item())])
+        yr, rr, _ = c.oracle().forward(x_bits)
+        assert np.array_equal(mask.cpu().numpy(), rr)
+        if mode == "exact":
+            assert np.array_equal(y_bits(y), yr)
+        else:
+            assert_fast_close(y_bits(y), yr, f"group {c.n}x{c.k} {mode}")
+
+
+@pytest.mark.parametrize("kind", ["wide", "zeros", "tiny", "one_hot"])
+def test_one_token_extreme_inputs(sc, kind):
+    # one-token decode: fast_tc runs the fp8 engine (x split into e4m3 columns); every engine
+    # must stay within the tolerance on inputs spanning the f16 range
+    n, k = 1024, 2048
+    case = make_case(n, k, 1, 0.02, seed=55, boost=[0])
+    rng = np.random.default_rng(5)
+    if kind == "wide":
+        x = (rng.standard_normal(k) * 10.0 ** rng.uniform(-7, 4, k)).astype(np.float32)
+    elif kind == "zeros":
+        x = np.zeros(k, dtype=np.float32)
+    elif kind == "tiny":
+        x = (rng.standard_normal(k) * 1e-6).astype(np.float32)
+    else:
+        x = np.zeros(k, dtype=np.float32)
+        x[777] = 3.0e4
+        x[5] = 1e-3
+    case.x_bits = x.astype(np.float16).view(np.uint16).reshape(1, k)
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    for mode in FAST_MODES:
+        op = to_op(sc, case, mode=mode)
+        y, mask, _ = run_gpu(op, case.x_bits)
+        assert np.array_equal(mask, rr)
+        assert_fast_close(y_bits(y), yr, f"{kind} {mode}")
+        acc = op.forward_partial(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")).cpu().numpy()
+        assert_acc_close(acc, acc_ref, f"{kind} {mode} acc")
