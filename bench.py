@@ -444,13 +444,16 @@ def run_ours(args, rank, world):
     big_bytes = sum(b for _, b in big)
     achieved = big_bytes / (ms_big / 1e3) / 1e9
     peak, peak_kind = measured_peak()
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "decode_tc_traffic.json")
+    # DRAM traffic of the dominant launch from the committed ncu capture (profiles/): the gate+up
+    # group of one layer; reported with that launch's algorithmic bytes for comparison
+    traffic = traffic_alg = None
+    tp = os.path.join(ROOT, "profiles", "decode_fused_traffic.json")
     if os.path.exists(tp):
         try:
-            traffic = json.load(open(tp)).get("bytes_per_launch_scaled")
+            tj = json.load(open(tp))
+            traffic, traffic_alg = tj.get("dram_bytes_per_launch"), tj.get("algorithmic_bytes_per_launch")
         except ValueError:
-            traffic = None
+            pass
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
@@ -464,6 +467,8 @@ def run_ours(args, rank, world):
                    else "one launch per projection", "launches_per_step": launches_per_step(args, units)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "traffic_note": None if traffic is None else
+                     f"ncu DRAM bytes of one gate+up group launch (algorithmic {traffic_alg})",
                      "kernel": launch_kind(args) + f" on the gate/up/down calls ({len(big_units)} launches per step)",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
