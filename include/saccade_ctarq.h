@@ -154,8 +154,9 @@ SC_API sc_status sc_forward_ws(const sc_layer* layer, const void* x, int x_dtype
 /* Groups: layers that read the same input -- the q, k and v projections of an attention block,
  * or the gate and up projections of an MLP -- computed by one launch.  No counterpart in the
  * reference, which applies each projection separately (saccade-runner/src/model.rs:217-219 and
- * 296-297); every output, mask and routed list is bit for bit what sc_forward on that layer
- * gives.  A group holds 1..SC_GROUP_MAX layers on one device with the same in_features and input
+ * 296-297).  Masks and routed lists are those of sc_forward on each layer; outputs too, bit for
+ * bit in SC_MODE_EXACT, and within the fast-mode tolerance otherwise (the group splits the columns
+ * for its combined grid, so f32 partial sums are added in another order; still deterministic).  A group holds 1..SC_GROUP_MAX layers on one device with the same in_features and input
  * columns (no ROWS shards); it references the layers, which must outlive it.  sc_forward_group
  * takes arrays of `count` outputs (y) and optional per-layer arrays (bias, mask_out,
  * routed_idx_out, n_routed_out; NULL for none); the workspace is as for sc_forward_ws, sized for

@@ -56,18 +56,95 @@ static int sm_count(int dev) {
 // thread-block cluster (at most kMaxFusedCluster CTAs) that reduces through distributed
 // shared memory; aim at two CTAs per SM, with each CTA's column slice of x fitting its
 // shared-memory copy.  0 when the layer is too wide for one cluster.
-int fused_ksplit(const Layer& L) {
-    const int64_t RT = L.Np / 128;
-    const int64_t target = kFusedCtasPerSm * static_cast<int64_t>(L.sms);
-    int64_t ks = (target + RT / 2) / RT;
-    ks = std::max<int64_t>(1, std::min<int64_t>(ks, std::min<int64_t>(kMaxFusedCluster, std::max<int64_t>(1, L.KB / 2))));
-    ks = std::max<int64_t>(ks, (L.KB + fused_max_kb(1) - 1) / fused_max_kb(1));
-    return ks <= kMaxFusedCluster ? static_cast<int>(ks) : 0;
+// The split count (= cluster size) for a launch of `rt` row tiles of `kb` column blocks: the
+// largest ks whose rt clusters can all be resident at once (one wave: cluster packing into the
+// GPCs decides, measured by the occupancy query), with at least two column blocks per CTA and
+// each CTA's slice of x within its shared-memory copy.  0 when no split fits a cluster.
+int choose_ksplit(int64_t rt, int64_t kb) {
+    const int64_t min_ks = (kb + fused_max_kb(1) - 1) / fused_max_kb(1);
+    if (min_ks > kMaxFusedCluster) return 0;
+    int best = 0;
+    for (int ks = 1; ks <= kMaxFusedCluster; ++ks) {
+        if (ks < min_ks || (ks > 1 && kb / ks < 2)) continue;
+        const int cap = fused_max_active_clusters(ks);
+        if (best == 0 || (cap > 0 && rt <= cap)) best = ks;  // larger ks wins while one wave holds
+    }
+    return best;
 }
 
-bool use_fused(const Layer& L, int64_t m) {
-    if (L.mode == SC_MODE_EXACT || m > 8 || L.ks_fused <= 0) return false;
-    return (L.KB + L.ks_fused - 1) / L.ks_fused <= fused_max_kb(m);  // the x slice fits the CTA's copy
+int fused_ksplit(const Layer& L) { return choose_ksplit(L.Np / 128, L.KB); }
+
+bool use_fused_ks(const Layer& L, int64_t m, int ks) {
+    if (L.mode == SC_MODE_EXACT || m > 8 || ks <= 0) return false;
+    return (L.KB + ks - 1) / ks <= fused_max_kb(m);  // the x slice fits the CTA's copy
+}
+
+bool use_fused(const Layer& L, int64_t m) { return use_fused_ks(L, m, L.ks_fused); }
+
+// dW blocks of the router-fused decode for `ks` column splits, from the host CSR (columns local
+// to the layer, ascending per row): for every (row tile, split), 129 u16 row offsets (272 B), the
+// u16 columns relative to the split, then the i8 values, each padded to 16 B; off[rt * ks + sp]
+// is the byte offset of a block.  Left empty (the kernel then reads the CSR) when a block would
+// exceed the kernel's shared-memory copy.
+struct DwBlocks {
+    uint8_t* blk = nullptr;
+    uint32_t* off = nullptr;
+    int64_t bytes = 0;
+};
+
+static cudaError_t build_dw_blocks(const Layer& L, int ks, const uint32_t* srp, const uint16_t* scol,
+                                   const int8_t* sval, DwBlocks* out) {
+    *out = DwBlocks{};
+    if (L.nnz == 0 || ks <= 0) return cudaSuccess;
+    const int64_t RT = L.Np / 128;
+    std::vector<uint32_t> off(RT * ks + 1, 0);
+    std::vector<uint8_t> blob;
+    std::vector<uint16_t> roff(129), cols;
+    std::vector<int8_t> vals;
+    for (int64_t rt = 0; rt < RT; ++rt) {
+        for (int64_t sp = 0; sp < ks; ++sp) {
+            const int64_t bc0 = (L.KB * sp / ks) * 64, bc1 = (L.KB * (sp + 1) / ks) * 64;
+            cols.clear();
+            vals.clear();
+            for (int r = 0; r < 128; ++r) {
+                roff[r] = static_cast<uint16_t>(cols.size());
+                const int64_t row = rt * 128 + r;
+                if (row < L.N) {
+                    for (uint32_t q = srp[row]; q < srp[row + 1]; ++q) {
+                        if (scol[q] >= bc0 && scol[q] < bc1) {
+                            cols.push_back(static_cast<uint16_t>(scol[q] - bc0));
+                            vals.push_back(sval[q]);
+                        }
+                    }
+                }
+            }
+            const size_t n = cols.size();
+            if (n > 65535) return cudaSuccess;  // u16 row offsets cannot describe the block
+            roff[128] = static_cast<uint16_t>(n);
+            const size_t bytes = 272 + ((n * 2 + 15) / 16) * 16 + ((n + 15) / 16) * 16;
+            if (static_cast<int64_t>(bytes) > kDwBlockMax) return cudaSuccess;
+            const size_t at = blob.size();
+            blob.resize(at + bytes, 0);
+            std::memcpy(&blob[at], roff.data(), 129 * 2);
+            if (n) {
+                std::memcpy(&blob[at + 272], cols.data(), n * 2);
+                std::memcpy(&blob[at + 272 + ((n * 2 + 15) / 16) * 16], vals.data(), n);
+            }
+            off[rt * ks + sp + 1] = static_cast<uint32_t>(blob.size());
+        }
+    }
+    cudaError_t e = cudaMalloc(&out->blk, blob.size());
+    if (e == cudaSuccess) e = cudaMalloc(&out->off, off.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(out->blk, blob.data(), blob.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(out->off, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(out->blk);
+        cudaFree(out->off);
+        *out = DwBlocks{};
+        return e;
+    }
+    out->bytes = static_cast<int64_t>(blob.size() + off.size() * 4);
+    return cudaSuccess;
 }
 
 WsLayout plan_workspace(const Layer& L, int64_t m) {
@@ -188,6 +265,8 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         f.ws_partial = reinterpret_cast<float*>(base + w.partial);
         f.ws_rtcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
         f.ksplit = w.ksplit;
+        f.dwblk = L.dwblk;
+        f.dwoff = L.dwoff;
         cudaError_t e = launch_decode_fused(&f, 1, stream);
         if (e != cudaSuccess) return cuda_fail(e, "fused decode launch");
         return SC_OK;
@@ -296,6 +375,14 @@ struct sc_layer {
 
 struct sc_group {
     std::vector<const sc_layer*> layers;
+    int ksplit = 0;                 // column splits of the group's one-launch decode
+    std::vector<DwBlocks> own;      // dW blocks built for `ksplit` (empty: the layer's own serve)
+    ~sc_group() {
+        for (DwBlocks& b : own) {
+            cudaFree(b.blk);
+            cudaFree(b.off);
+        }
+    }
 };
 
 extern "C" {
@@ -540,50 +627,11 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     if (e == cudaSuccess) {
         // dW blocks of the router-fused decode kernel
         L.ks_fused = fused_ksplit(L);
-        const int64_t RT = L.Np / 128, ks = std::max(1, L.ks_fused);
-        std::vector<uint32_t> off(RT * ks + 1, 0);
-        std::vector<uint8_t> blob;
-        int64_t maxb = 0;
-        for (int64_t rt = 0; rt < RT; ++rt) {
-            for (int64_t sp = 0; sp < ks; ++sp) {
-                const int64_t bc0 = (L.KB * sp / ks) * 64, bc1 = (L.KB * (sp + 1) / ks) * 64;
-                std::vector<uint16_t> roff(129, 0), cols;
-                std::vector<int8_t> vals;
-                for (int r = 0; r < 128; ++r) {
-                    roff[r] = static_cast<uint16_t>(cols.size());
-                    const int64_t row = rt * 128 + r;
-                    if (row < L.N) {
-                        for (uint32_t q = srp[row]; q < srp[row + 1]; ++q) {
-                            if (scol[q] >= bc0 && scol[q] < bc1) {
-                                cols.push_back(static_cast<uint16_t>(scol[q] - bc0));
-                                vals.push_back(sval[q]);
-                            }
-                        }
-                    }
-                }
-                roff[128] = static_cast<uint16_t>(cols.size());
-                const size_t n = cols.size();
-                const size_t bytes = 272 + ((n * 2 + 15) / 16) * 16 + ((n + 15) / 16) * 16;
-                const size_t at = blob.size();
-                blob.resize(at + bytes, 0);
-                std::memcpy(&blob[at], roff.data(), 129 * 2);
-                if (n) {
-                    std::memcpy(&blob[at + 272], cols.data(), n * 2);
-                    std::memcpy(&blob[at + 272 + ((n * 2 + 15) / 16) * 16], vals.data(), n);
-                }
-                off[rt * ks + sp + 1] = static_cast<uint32_t>(blob.size());
-                maxb = std::max<int64_t>(maxb, static_cast<int64_t>(bytes));
-                if (n > 65535) maxb = INT64_MAX;  // u16 row offsets cannot describe the block
-            }
-        }
-        L.dw_max_block = maxb;
-        if (L.nnz > 0 && L.ks_fused > 0 && maxb <= kDwBlockMax) {
-            if ((e = cudaMalloc(&L.dwblk, blob.size())) == cudaSuccess &&
-                (e = cudaMalloc(&L.dwoff, off.size() * 4)) == cudaSuccess &&
-                (e = cudaMemcpy(L.dwblk, blob.data(), blob.size(), cudaMemcpyHostToDevice)) == cudaSuccess)
-                e = cudaMemcpy(L.dwoff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
-            L.device_bytes += static_cast<int64_t>(blob.size() + off.size() * 4);
-        }
+        DwBlocks b;
+        e = build_dw_blocks(L, L.ks_fused, srp.data(), scol.data(), sval.data(), &b);
+        L.dwblk = b.blk;
+        L.dwoff = b.off;
+        L.device_bytes += b.bytes;
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(tmp_packed);
@@ -760,6 +808,31 @@ sc_status sc_group_create(sc_layer* const* layers, int count, sc_group** out) {
     }
     sc_group* g = new sc_group;
     g->layers.assign(layers, layers + count);
+    g->own.resize(count);
+    const Layer& L0 = layers[0]->L;
+    DeviceGuard guard(L0.device);
+    if (!guard.ok) {
+        delete g;
+        return cuda_fail(cudaErrorInvalidDevice, "sc_group_create: set device");
+    }
+    int64_t rt = 0;
+    for (int i = 0; i < count; ++i) rt += layers[i]->L.Np / 128;
+    g->ksplit = choose_ksplit(rt, L0.KB);
+    for (int i = 0; i < count; ++i) {
+        const Layer& L = layers[i]->L;
+        if (L.nnz == 0 || g->ksplit == L.ks_fused || g->ksplit <= 0) continue;
+        std::vector<uint32_t> srp(L.N + 1);
+        std::vector<uint16_t> scol(L.nnz);
+        std::vector<int8_t> sval(L.nnz);
+        cudaError_t e = cudaMemcpy(srp.data(), L.rowptr, (L.N + 1) * 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(scol.data(), L.col, L.nnz * 2, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(sval.data(), L.val, L.nnz, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = build_dw_blocks(L, g->ksplit, srp.data(), scol.data(), sval.data(), &g->own[i]);
+        if (e != cudaSuccess) {
+            delete g;
+            return cuda_fail(e, "sc_group_create: dW blocks");
+        }
+    }
     *out = g;
     return SC_OK;
 }
@@ -780,10 +853,10 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
     if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward_group: set device");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // one launch when every layer takes the router-fused decode with the same split
-    bool one = true;
+    bool one = group->ksplit > 0;
     for (int i = 0; i < n; ++i) {
         const Layer& L = group->layers[i]->L;
-        one = one && use_fused(L, m) && L.ks_fused == L0.ks_fused && L.mode == L0.mode;
+        one = one && use_fused_ks(L, m, group->ksplit) && L.mode == L0.mode;
     }
     if (one) {
         if (x_dtype != SC_F16 && x_dtype != SC_BF16) {
@@ -823,7 +896,11 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
             a.nrouted_out = n_routed_out ? n_routed_out[i] : nullptr;
             a.ws_partial = nullptr;
             a.ws_rtcount = nullptr;
-            a.ksplit = L.ks_fused;
+            a.ksplit = group->ksplit;
+            const bool own = group->own[i].blk != nullptr;
+            const bool layers_fit = group->ksplit == L.ks_fused;
+            a.dwblk = own ? group->own[i].blk : layers_fit ? L.dwblk : nullptr;
+            a.dwoff = own ? group->own[i].off : layers_fit ? L.dwoff : nullptr;
         }
         const cudaError_t e = launch_decode_fused(f, n, s);
         if (e != cudaSuccess) return cuda_fail(e, "grouped decode launch");

@@ -1595,8 +1595,8 @@ static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     fp.mask_out = f.mask_out;
     fp.ridx_out = f.ridx_out;
     fp.nrouted_out = f.nrouted_out;
-    fp.dwblk = L.dwblk;
-    fp.dwoff = L.dwoff;
+    fp.dwblk = f.dwblk;
+    fp.dwoff = f.dwoff;
     fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
     fp.rc = route_consts(fp.Kfull);
     // each auxiliary thread adds at most T values sequentially in f32 (both passes), then five
@@ -1659,6 +1659,40 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s) {
     cfg.attrs = attr;
     cfg.numAttrs = ksplit > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, g);
+}
+
+int fused_max_active_clusters(int ks) {
+    static std::atomic<int> cache[64][kMaxFusedCluster + 1];  // 0: not queried yet
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || ks < 1 || ks > kMaxFusedCluster) return 0;
+    const int have = cache[dev][ks].load();
+    if (have > 0) return have;
+    // the three engines take the same grid shape and near-identical shared memory; the mma.sync
+    // engine (the largest footprint) stands for all of them
+    auto kern = k_ctarq_fused_mma;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FusedMmaCfg::kTotal) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(ks * 64));
+    cfg.blockDim = dim3(FusedMmaCfg::kThreads);
+    cfg.dynamicSmemBytes = FusedMmaCfg::kTotal;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(ks);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    cache[dev][ks].store(n);
+    return n;
 }
 
 int fused_max_kb(int64_t m) {

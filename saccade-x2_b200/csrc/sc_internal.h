@@ -48,7 +48,6 @@ struct Layer {
     int ks_fused = 0;            // column splits (= cluster size) of the fused kernel; 0: not usable
     uint8_t* dwblk = nullptr;
     uint32_t* dwoff = nullptr;   // byte offset of block (rt * ks_fused + split); [RT*ks_fused + 1]
-    int64_t dw_max_block = 0;    // largest block in bytes
 };
 
 // Shared-memory budget of one dW block in the fused decode kernel.
@@ -63,6 +62,8 @@ constexpr int kMaxFusedCluster = SC_FUSED_MAX_CLUSTER;  // CTAs of one row tile 
 constexpr int kFusedCtasPerSm = SC_FUSED_CTAS_PER_SM;   // grid target of the fused kernel
 
 int fused_ksplit(const Layer& L);
+int choose_ksplit(int64_t rt, int64_t kb);  // splits of a one-wave launch of rt row tiles x kb column blocks
+bool use_fused_ks(const Layer& L, int64_t m, int ks);
 bool use_fused(const Layer& L, int64_t m);  // the router-fused decode kernel serves this call
 
 // Completion-counter region at the start of every workspace (see plan_workspace).
@@ -166,9 +167,14 @@ struct FusedArgs {
     float* ws_partial;
     uint32_t* ws_rtcount;
     int ksplit;
+    const uint8_t* dwblk;   // dW blocks built for this ksplit (null: the kernel reads the CSR)
+    const uint32_t* dwoff;
 };
 // One launch for n (<= SC_GROUP_MAX) layers that read the same x, all with the same ksplit and mode.
 cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s);
+// How many thread-block clusters of `ks` CTAs of the router-fused decode kernel can be resident
+// at once on the current device (cached per device).
+int fused_max_active_clusters(int ks);
 int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
 
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,

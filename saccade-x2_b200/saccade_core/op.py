@@ -303,7 +303,8 @@ class SaccadeLinearGroup:
     """Layers that read the same input -- q, k and v, or gate and up -- computed by one launch
     (sc_group_create / sc_forward_group).  No reference counterpart (the reference applies each
     projection separately, saccade-runner/src/model.rs:217-219, 296-297); forward(x) returns one
-    output per layer, bit for bit what that layer's forward(x) gives."""
+    output per layer: the layer's own masks and routed lists, its outputs bit for bit in exact mode
+    and within the fast-mode tolerance otherwise (the group may split the columns differently)."""
 
     def __init__(self, ops):
         ops = list(ops)

@@ -352,7 +352,10 @@ def test_group_matches_individual_calls(sc, shapes, m, mode):
         yi, mi, ri, ni = op.forward(x, return_routing=True)
         torch.cuda.synchronize()
         op.check_device()
-        assert np.array_equal(y_bits(y), y_bits(yi)), "a group must reproduce the layer's own call bit for bit"
+        if mode == "exact":
+            assert np.array_equal(y_bits(y), y_bits(yi)), "exact mode: a group reproduces the layer's own call"
+        else:  # the group may split the columns differently: f32 split-K sums in another order
+            assert_fast_close(y_bits(y), y_bits(yi), f"group vs single {c.n}x{c.k} {mode}")
         assert np.array_equal(mask.cpu().numpy(), mi.cpu().numpy())
         assert int(nr.item()) == int(ni.item())
         assert np.array_equal(ridx.cpu().numpy()[: int(nr.item())], ri.cpu().numpy()[: int(ni.item())])
