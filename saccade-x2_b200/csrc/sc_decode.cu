@@ -785,7 +785,8 @@ __device__ __forceinline__ void fused_split8(const FusedCtx& c, int at) {
 
 // Auxiliary warps (four consecutive warps; thread `at` = 32 * (warp % 4) + lane owns row `at`
 // of the tile): stage x, route, publish the mask, and accumulate this row's dW into corr.
-__device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float (&corr)[FusedRegions::NT]) {
+__device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float (&corr)[FusedRegions::NT],
+                                                float& row_scale) {
     using R = FusedRegions;
     constexpr int NT = R::NT;
     const FusedParams& fp = *c.fp;
@@ -794,6 +795,8 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
     const int ntok = c.ntok, ks = c.ks;
 #pragma unroll
     for (int t = 0; t < NT; ++t) corr[t] = 0.0f;
+    // this row's scale: a weight, so it is read before waiting on the previous kernel
+    row_scale = c.rt * 128 + at < p.N ? __ldg(p.scale + c.rt * 128 + at) : 0.0f;
     pdl_wait();
     const int64_t slice0 = fp.x_col0 + c.kb_begin * 64;             // first staged column of x
     const int64_t slice1 = fp.x_col0 + imin64(c.kb_end * 64, p.K);  // end of its real columns
@@ -1081,6 +1084,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
 
     int issued = 0;
     float corr[NT];
+    float row_scale = 0.0f;
     const int at = 32 * (warp & 3) + lane;  // auxiliary threads: tile row, in this warp's TMEM lanes
     if (warp == C::kProducerWarp) {
         if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
@@ -1175,7 +1179,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
             if (lane == 0) mbar_arrive(&a_full[b]);
         }
     } else {
-        fused_aux_front(c, at, corr);
+        fused_aux_front(c, at, corr, row_scale);
     }
     __syncwarp();
     if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
@@ -1183,7 +1187,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
     float v[NT];
     if (warp >= C::kAuxWarp0) {
         const int64_t row = c.rt * 128 + at;
-        const float sc = row < p.N ? __ldg(p.scale + row) : 0.0f;
+        const float sc = row_scale;
         uint32_t d[8];
         const bool ok = mbar_wait(done, 0, p.status);
         tc_fence_after();
@@ -1274,6 +1278,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
 
     int issued = 0;
     float corr[NT];
+    float row_scale = 0.0f;
     const int at = 32 * (warp & 3) + lane;
     if (warp == C::kProducerWarp) {
         if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
@@ -1316,7 +1321,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
         accbuf[(r0 + 8) * C::kLd + 2 * cq] = acc[0][2] + acc[1][2];
         accbuf[(r0 + 8) * C::kLd + 2 * cq + 1] = acc[0][3] + acc[1][3];
     } else {
-        fused_aux_front(c, at, corr);
+        fused_aux_front(c, at, corr, row_scale);
     }
     __syncwarp();
     if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
@@ -1328,7 +1333,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     }
     if (warp < C::kAuxWarp0) return;
     const int64_t row = c.rt * 128 + at;
-    const float sc = row < p.N ? __ldg(p.scale + row) : 0.0f;
+    const float sc = row_scale;
     float v[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;

@@ -53,7 +53,7 @@ struct Layer {
 // Shared-memory budget of one dW block in the fused decode kernel.
 constexpr int64_t kDwBlockMax = 16 * 1024;
 #ifndef SC_FUSED_MAX_CLUSTER
-#define SC_FUSED_MAX_CLUSTER 8
+#define SC_FUSED_MAX_CLUSTER 16
 #endif
 #ifndef SC_FUSED_CTAS_PER_SM
 #define SC_FUSED_CTAS_PER_SM 2
