@@ -568,9 +568,12 @@ struct FusedRegions {
     static constexpr int kAuxThreads = 128;
     static constexpr int kXsBytes = 32 * 1024;   // staged x: 32768 / (128 * ntp) column blocks
     static constexpr int kPad = 128;             // MMA operand rows past the last staged chunk read here
-    // fp8 engine (one token): f16 x in [0, 8 KB), its e4m3 split in [8 KB, 32 KB) of the same region
+    // fp8 and integer engines (one token): f16 x in [0, 8 KB), its e4m3 split (512 B per 64-column
+    // block) or its base-256 digit columns (384 B per block) in [8 KB, 32 KB) of the same region
     static constexpr int kXb8 = 8 * 1024;
     static constexpr int kMaxKbF8 = (kXsBytes - kXb8) / 512;
+    static constexpr int kMaxKbI8 = (kXsBytes - kXb8) / 384;
+    static_assert(kMaxKbI8 * 128 <= kXb8, "the f16 slice of the integer engine fits below its digits");
     static constexpr int kXs = 0;
     static constexpr int kDw = kXsBytes + kPad;
     static constexpr int kStats = kDw + static_cast<int>(kDwBlockMax);             // [ranks][8 tokens][3] f64
@@ -654,7 +657,8 @@ __device__ __forceinline__ void fused_init_bars(const FusedCtx& c) {
     }
 }
 
-// Producer lane: weights through the ring (stages of SKB 4 KB blocks), dW block up front.
+// Producer lane: the CTA's dW block first (the auxiliary warps wait on it; the weights are
+// consumed progressively), then the weights through the ring (stages of SKB 4 KB blocks).
 // Returns the number of stages issued.
 template <int SKB, int S>
 __device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* ring, uint64_t* full, uint64_t* empty) {
@@ -664,17 +668,17 @@ __device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* r
     const uint64_t pol = policy_evict_first();
     const int pre = nst < S ? nst : S;
     int issued = 0;
+    if (c.use_blk) {
+        const uint32_t o0 = c.fp->dwoff[c.bid], o1 = c.fp->dwoff[c.bid + 1];
+        mbar_arrive_expect_tx(c.dw_ready, o1 - o0);
+        bulk_g2s(const_cast<unsigned char*>(c.dws), c.fp->dwblk + o0, o1 - o0, c.dw_ready);
+    }
     for (int it = 0; it < pre; ++it, ++issued) {
         const int64_t kb0 = c.kb_begin + static_cast<int64_t>(it) * SKB;
         const int n = static_cast<int>(imin64(SKB, c.kb_end - kb0));
         mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
         bulk_g2s_stream(ring + it * kStage, p.wq + (c.rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096),
                         &full[it], pol);
-    }
-    if (c.use_blk) {
-        const uint32_t o0 = c.fp->dwoff[c.bid], o1 = c.fp->dwoff[c.bid + 1];
-        mbar_arrive_expect_tx(c.dw_ready, o1 - o0);
-        bulk_g2s(const_cast<unsigned char*>(c.dws), c.fp->dwblk + o0, o1 - o0, c.dw_ready);
     }
     for (int it = pre; it < nst; ++it, ++issued) {
         const int slot = it % S;
@@ -1242,6 +1246,13 @@ struct FusedMmaCfg {
     static_assert(2 * (kTotal + 2048 + 1024) <= 228 * 1024, "two CTAs per SM (with static and reserved smem)");
 };
 
+// I8 (one token): the integer variant.  The weights become s8 bytes 16 (q - 8) (dequant_word_s8,
+// 3 instructions a word instead of 9) and x becomes six signed base-256 digit columns of the
+// integer x * 2^24 (f16_digits), so m16n8k32 s8 MMAs (two per 64-column block instead of four
+// f16 ones) accumulate the products exactly in s32; the row is recombined in f64 and rounded once
+// to f32.  A CTA whose slice of x holds an inf or nan runs the f16 loop instead, so the
+// non-finite results are those of the f16 engine.
+template <bool I8>
 __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(FusedGroup g) {
     using C = FusedMmaCfg;
     constexpr int SKB = C::SKB, S = C::S, NT = FusedRegions::NT;
@@ -1257,6 +1268,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
     uint64_t* empty = full + S;
     __shared__ int s_abort;
+    __shared__ int s_f16;  // this CTA accumulates in f32 (always without I8; with I8 for a non-finite slice)
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
     const FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red);
@@ -1270,6 +1282,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
         }
         fused_init_bars(c);
         s_abort = 0;
+        s_f16 = I8 ? 0 : 1;
         s_mask = 0u;
     }
     for (int i = tid; i < 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
@@ -1283,43 +1296,112 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     if (warp == C::kProducerWarp) {
         if (lane == 0) issued = fused_produce<SKB, S>(c, smem, full, empty);
     } else if (warp < C::kMmaWarps) {
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         const int g = lane >> 2, cq = lane & 3;
-        const bool has_tok = g < c.ntok;
-        const int xoff = (cq >> 1) * c.cs + g * 16 + (cq & 1) * 8;
+        const int r0 = warp * 16 + g;
         if (!mbar_wait(c.x_ready, 0, p.status)) s_abort = 1;
-        for (int it = 0; it < nst && !s_abort; ++it) {
-            const int slot = it % S;
-            if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
-                s_abort = 1;
-                break;
+        if constexpr (I8) {
+            // digit columns of the slice: block kb, lane (g, c) with g < 6 holds at byte
+            // kb * 384 + (4 g + c) * 16 the four B words {b0, b1} x 2 MMAs of digit g; word s of a
+            // lane packs the digits of columns 16 s + 4c + {0, 2, 1, 3} (the order of the weight
+            // bytes of dequant_word_s8)
+            bool bad = false;
+            for (int q = tid; q < c.nkb * 16; q += 32 * C::kMmaWarps) {
+                const int kb = q >> 4, sg = (q >> 2) & 3, cc = q & 3;
+                const uint2 u = *reinterpret_cast<const uint2*>(c.xs + (kb * 8 + 2 * sg + (cc >> 1)) * 16 + (cc & 1) * 8);
+                const uint32_t u0 = u.x, u1 = u.y;  // columns 4c, 4c+1 and 4c+2, 4c+3 of the step
+                uint32_t lo[4], hi[4];
+                f16_digits(u0 & 0xFFFFu, lo[0], hi[0], bad);
+                f16_digits(u1 & 0xFFFFu, lo[1], hi[1], bad);
+                f16_digits(u0 >> 16, lo[2], hi[2], bad);
+                f16_digits(u1 >> 16, lo[3], hi[3], bad);
+                // byte transpose: word of digit d = byte d of the four elements
+                const uint32_t t0 = __byte_perm(lo[0], lo[1], 0x5140), t1 = __byte_perm(lo[0], lo[1], 0x7362);
+                const uint32_t t2 = __byte_perm(lo[2], lo[3], 0x5140), t3 = __byte_perm(lo[2], lo[3], 0x7362);
+                const uint32_t h0 = __byte_perm(hi[0], hi[1], 0x5140), h1 = __byte_perm(hi[2], hi[3], 0x5140);
+                uint32_t* dst = reinterpret_cast<uint32_t*>(c.xb8 + kb * 384 + cc * 16 + sg * 4);
+                dst[0] = __byte_perm(t0, t2, 0x5410);
+                dst[16] = __byte_perm(t0, t2, 0x7632);
+                dst[32] = __byte_perm(t1, t3, 0x5410);
+                dst[48] = __byte_perm(t1, t3, 0x7632);
+                dst[64] = __byte_perm(h0, h1, 0x5410);
+                dst[80] = __byte_perm(h0, h1, 0x7632);
             }
-            const int n = static_cast<int>(imin64(SKB, c.kb_end - (c.kb_begin + static_cast<int64_t>(it) * SKB)));
-            const unsigned char* st = smem + slot * C::kStageBytes;
-            const unsigned char* xk0 = c.xs + (it * SKB) * 8 * c.cs + xoff;
+            if (__any_sync(0xffffffffu, bad) && lane == 0) s_f16 = 1;
+            asm volatile("bar.sync 2, 256;" ::: "memory");  // the eight MMA warps
+        }
+        if (!I8 || s_f16) {
+            float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            const bool has_tok = g < c.ntok;
+            const int xoff = (cq >> 1) * c.cs + g * 16 + (cq & 1) * 8;
+            for (int it = 0; it < nst && !s_abort; ++it) {
+                const int slot = it % S;
+                if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                const int n = static_cast<int>(imin64(SKB, c.kb_end - (c.kb_begin + static_cast<int64_t>(it) * SKB)));
+                const unsigned char* st = smem + slot * C::kStageBytes;
+                const unsigned char* xk0 = c.xs + (it * SKB) * 8 * c.cs + xoff;
 #pragma unroll
-            for (int j = 0; j < SKB; ++j) {
-                if (j < n) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(st + j * 4096 + warp * 512 + lane * 16);
-                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+                for (int j = 0; j < SKB; ++j) {
+                    if (j < n) {
+                        const uint4 wv = *reinterpret_cast<const uint4*>(st + j * 4096 + warp * 512 + lane * 16);
+                        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        uint2 b = make_uint2(0u, 0u);
-                        if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * 8 * c.cs + 2 * s * c.cs);
-                        uint32_t a[4];
-                        dequant_word(words[s], a);
-                        mma_16816(acc[s & 1], a, b.x, b.y);
+                        for (int s = 0; s < 4; ++s) {
+                            uint2 b = make_uint2(0u, 0u);
+                            if (has_tok) b = *reinterpret_cast<const uint2*>(xk0 + j * 8 * c.cs + 2 * s * c.cs);
+                            uint32_t a[4];
+                            dequant_word(words[s], a);
+                            mma_16816(acc[s & 1], a, b.x, b.y);
+                        }
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
+            accbuf[r0 * C::kLd + 2 * cq] = acc[0][0] + acc[1][0];
+            accbuf[r0 * C::kLd + 2 * cq + 1] = acc[0][1] + acc[1][1];
+            accbuf[(r0 + 8) * C::kLd + 2 * cq] = acc[0][2] + acc[1][2];
+            accbuf[(r0 + 8) * C::kLd + 2 * cq + 1] = acc[0][3] + acc[1][3];
+        } else {
+            int acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+            for (int it = 0; it < nst && !s_abort; ++it) {
+                const int slot = it % S;
+                if (!mbar_wait(&full[slot], (it / S) & 1, p.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                const int n = static_cast<int>(imin64(SKB, c.kb_end - (c.kb_begin + static_cast<int64_t>(it) * SKB)));
+                const unsigned char* st = smem + slot * C::kStageBytes;
+                const unsigned char* dg = c.xb8 + (it * SKB) * 384 + lane * 16;
+#pragma unroll
+                for (int j = 0; j < SKB; ++j) {
+                    if (j < n) {
+                        const uint4 wv = *reinterpret_cast<const uint4*>(st + j * 4096 + warp * 512 + lane * 16);
+                        uint4 dv = make_uint4(0u, 0u, 0u, 0u);  // digit columns 6 and 7 are zero
+                        if (lane < 24) dv = *reinterpret_cast<const uint4*>(dg + j * 384);
+                        uint32_t a[4];
+                        dequant_word_s8(wv.x, a[0], a[1]);
+                        dequant_word_s8(wv.y, a[2], a[3]);
+                        mma_16832_s8(acc[0], a, dv.x, dv.y);
+                        dequant_word_s8(wv.z, a[0], a[1]);
+                        dequant_word_s8(wv.w, a[2], a[3]);
+                        mma_16832_s8(acc[1], a, dv.z, dv.w);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[slot]);
+            }
+            // row r0 (and r0 + 8), digit columns 2c and 2c + 1 (6 and 7 are zero)
+            int* ai = reinterpret_cast<int*>(accbuf);
+            if (cq < 3) {
+                ai[r0 * C::kLd + 2 * cq] = acc[0][0] + acc[1][0];
+                ai[r0 * C::kLd + 2 * cq + 1] = acc[0][1] + acc[1][1];
+                ai[(r0 + 8) * C::kLd + 2 * cq] = acc[0][2] + acc[1][2];
+                ai[(r0 + 8) * C::kLd + 2 * cq + 1] = acc[0][3] + acc[1][3];
+            }
         }
-        const int r0 = warp * 16 + g;
-        accbuf[r0 * C::kLd + 2 * cq] = acc[0][0] + acc[1][0];
-        accbuf[r0 * C::kLd + 2 * cq + 1] = acc[0][1] + acc[1][1];
-        accbuf[(r0 + 8) * C::kLd + 2 * cq] = acc[0][2] + acc[1][2];
-        accbuf[(r0 + 8) * C::kLd + 2 * cq + 1] = acc[0][3] + acc[1][3];
     } else {
         fused_aux_front(c, at, corr, row_scale);
     }
@@ -1335,8 +1417,22 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     const int64_t row = c.rt * 128 + at;
     const float sc = row_scale;
     float v[NT];
+    if (I8 && !s_f16) {
+        // sum_k 16 (q_k - 8) X_k = sum_d 256^d S_d with X = x * 2^24: recombined in f64 (exact while
+        // below 2^53, one rounding beyond), scaled by 2^-28 exactly, rounded once to f32
+        const int* ai = reinterpret_cast<const int*>(accbuf) + at * C::kLd;
+        double sum = static_cast<double>(ai[5]);
 #pragma unroll
-    for (int t = 0; t < NT; ++t) v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;
+        for (int d = 4; d >= 0; --d) sum = sum * 256.0 + static_cast<double>(ai[d]);
+        const float a0 = static_cast<float>(sum * 0x1p-28);
+        v[0] = row < p.N ? __fadd_rn(__fmul_rn(a0, sc), corr[0]) : 0.0f;
+#pragma unroll
+        for (int t = 1; t < NT; ++t) v[t] = 0.0f;
+    } else {
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+            v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;
+    }
     fused_aux_finish(c, at, v);
 }
 
@@ -1633,11 +1729,14 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s) {
     // one token in SC_MODE_FAST_TC8: the fp8 variant when the e4m3 split of x fits
     bool f8 = f[0].L->mode == SC_MODE_FAST_TC8 && f[0].m == 1;
     for (int i = 0; i < n && f8; ++i) f8 = (f[i].L->KB + ksplit - 1) / ksplit <= FusedRegions::kMaxKbF8;
-    const int which = f8 ? 2 : tc ? 1 : 0;
-    auto kern = f8 ? k_ctarq_fused_tc<true> : tc ? k_ctarq_fused_tc<false> : k_ctarq_fused_mma;
+    // one token in SC_MODE_FAST: the integer variant when the digit columns of x fit
+    bool i8 = SC_FUSED_INT8 && f[0].L->mode == SC_MODE_FAST && f[0].m == 1;
+    for (int i = 0; i < n && i8; ++i) i8 = (f[i].L->KB + ksplit - 1) / ksplit <= FusedRegions::kMaxKbI8;
+    const int which = f8 ? 2 : tc ? 1 : i8 ? 3 : 0;
+    auto kern = f8 ? k_ctarq_fused_tc<true> : tc ? k_ctarq_fused_tc<false> : i8 ? k_ctarq_fused_mma<true> : k_ctarq_fused_mma<false>;
     const int threads = f8 ? FusedTcCfg<true>::kThreads : tc ? FusedTcCfg<false>::kThreads : FusedMmaCfg::kThreads;
     const int smem = f8 ? FusedTcCfg<true>::kTotal : tc ? FusedTcCfg<false>::kTotal : FusedMmaCfg::kTotal;
-    static std::atomic<uint64_t> flags[3] = {{0}, {0}, {0}};
+    static std::atomic<uint64_t> flags[4] = {{0}, {0}, {0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
@@ -1675,7 +1774,7 @@ int fused_max_active_clusters(int ks) {
     if (have > 0) return have;
     // the three engines take the same grid shape and near-identical shared memory; the mma.sync
     // engine (the largest footprint) stands for all of them
-    auto kern = k_ctarq_fused_mma;
+    auto kern = k_ctarq_fused_mma<false>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FusedMmaCfg::kTotal) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
         cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)

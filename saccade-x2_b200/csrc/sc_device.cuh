@@ -359,6 +359,38 @@ __device__ __forceinline__ void dequant_word_e4m3(uint32_t w, uint32_t& r_g, uin
     r_g8 = __byte_perm(cvt_e4m3x2_f16x2(h[1]), cvt_e4m3x2_f16x2(h[3]), 0x5410);
 }
 
+// ---- integer engine (one token): exact s8 x s8 -> s32 products
+// D[16x8] += A[16x32] * B[32x8], s8 inputs, s32 accumulation (register operands).
+__device__ __forceinline__ void mma_16832_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One W4U word as s8 bytes 16 * (q - 8) (the nibble moved to the top of its byte, top bit
+// flipped): r_g = row g, nibbles 0, 2, 4, 6 (columns 4c, 4c+2, 4c+1, 4c+3 of the 16-column
+// step), r_g8 = row g + 8, nibbles 1, 3, 5, 7 (the same columns).
+__device__ __forceinline__ void dequant_word_s8(uint32_t w, uint32_t& r_g, uint32_t& r_g8) {
+    r_g = ((w << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+    r_g8 = (w & 0xF0F0F0F0u) ^ 0x80808080u;
+}
+
+// An f16 value x as the integer X = x * 2^24 (exact: |X| < 2^40 for every finite f16) in six
+// signed base-256 digits, X = sum_i d_i 256^i with d_i in [-128, 127]: the bytes of
+// X + 0x808080808080 are d_i + 128, and flipping their top bits gives d_i as s8.  lo holds
+// digits 0-3, hi digits 4-5.  Infinities and NaNs set `bad` (their digits are meaningless).
+__device__ __forceinline__ void f16_digits(uint32_t h, uint32_t& lo, uint32_t& hi, bool& bad) {
+    const uint32_t e = (h >> 10) & 31u, m = h & 1023u;
+    bad |= e == 31u;
+    const uint64_t mag = static_cast<uint64_t>(e ? (m | 1024u) : m) << (e ? e - 1u : 0u);
+    const uint64_t X = (h & 0x8000u) ? 0ull - mag : mag;
+    const uint64_t Y = (X + 0x808080808080ull) ^ 0x808080808080ull;
+    lo = static_cast<uint32_t>(Y);
+    hi = static_cast<uint32_t>(Y >> 32);
+}
+
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
 // One lane of a converged warp (the same one every time): issues tcgen05 work in warp-uniform
 // loops so that addresses and descriptors stay in uniform registers.

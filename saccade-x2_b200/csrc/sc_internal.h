@@ -55,6 +55,9 @@ constexpr int64_t kDwBlockMax = 16 * 1024;
 #ifndef SC_FUSED_MAX_CLUSTER
 #define SC_FUSED_MAX_CLUSTER 16
 #endif
+#ifndef SC_FUSED_INT8
+#define SC_FUSED_INT8 1  // one-token decode in SC_MODE_FAST runs the s8 integer variant
+#endif
 #ifndef SC_FUSED_CTAS_PER_SM
 #define SC_FUSED_CTAS_PER_SM 2
 #endif

@@ -393,3 +393,30 @@ def test_one_token_extreme_inputs(sc, kind):
         assert_fast_close(y_bits(y), yr, f"{kind} {mode}")
         acc = op.forward_partial(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")).cpu().numpy()
         assert_acc_close(acc, acc_ref, f"{kind} {mode} acc")
+
+
+@pytest.mark.parametrize("kind", ["inf", "neg_inf", "nan"])
+def test_one_token_non_finite_inputs(sc, kind):
+    # one-token decode: the integer engine of "fast" cannot represent inf/nan and runs the f16 loop
+    # for the column split holding one, so every row keeps the reference's nan / +inf / -inf
+    # (inf times a zero weight is nan, otherwise the weight's sign); the fp8 engine of "fast_tc8"
+    # documents nan rows instead
+    n, k = 512, 3584
+    case = make_case(n, k, 1, 0.01, seed=77, boost=[0])
+    x = np.random.default_rng(9).standard_normal(k).astype(np.float32)
+    x[1234] = {"inf": np.inf, "neg_inf": -np.inf, "nan": np.nan}[kind]
+    case.x_bits = x.astype(np.float16).view(np.uint16).reshape(1, k)
+    yr, rr, _ = case.oracle().forward(case.x_bits)
+    r = yr.view(np.float16).astype(np.float32)
+    assert not np.isfinite(r).any()
+    for mode in FAST_MODES:
+        op = to_op(sc, case, mode=mode)
+        y, mask, _ = run_gpu(op, case.x_bits)
+        assert np.array_equal(mask, rr)
+        got = y_bits(y).view(np.float16).astype(np.float32)
+        if mode == "fast_tc8":
+            assert not np.isfinite(got).any(), mode
+            continue
+        assert np.array_equal(np.isnan(got), np.isnan(r)), mode
+        assert np.array_equal(np.isposinf(got), np.isposinf(r)), mode
+        assert np.array_equal(np.isneginf(got), np.isneginf(r)), mode
