@@ -75,9 +75,10 @@ def launches_per_step(args, units):
 
 def launch_kind(args):
     if args.mode != "exact" and args.tokens <= 8:
+        fast = ("k_ctarq_fused_mma<int8> (router-fused decode, s8 mma.sync on base-256 digits of x)"
+                if args.tokens == 1 else "k_ctarq_fused_mma (router-fused decode, f16 mma.sync)")
         return {"fast_tc": "k_ctarq_fused_tc<f16> (router-fused decode, tcgen05)",
-                "fast_tc8": "k_ctarq_fused_tc<fp8> (router-fused decode, tcgen05 e4m3)"}.get(
-            args.mode, "k_ctarq_fused_mma (router-fused decode, mma.sync)")
+                "fast_tc8": "k_ctarq_fused_tc<fp8> (router-fused decode, tcgen05 e4m3)"}.get(args.mode, fast)
     return "k_decode_exact (+ k_router)" if args.mode == "exact" else "k_ctarq_tc / k_ctarq_mma (+ k_router)"
 
 

@@ -644,7 +644,9 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, un
     return c;
 }
 
-// One thread: the common mbarriers and the byte counts expected from the cluster.
+// One thread: the common mbarriers and the byte counts expected from the cluster (TK: token
+// capacity of the kernel, the f32 values pushed per row).
+template <int TK>
 __device__ __forceinline__ void fused_init_bars(const FusedCtx& c) {
     mbar_init(c.x_ready, 4);
     mbar_init(c.dw_ready, 1);
@@ -653,7 +655,7 @@ __device__ __forceinline__ void fused_init_bars(const FusedCtx& c) {
     fence_mbar_init();
     if (c.ks > 1) {
         mbar_arrive_expect_tx(c.stats_bar, static_cast<uint32_t>(c.ks * c.ntok * 24));
-        mbar_arrive_expect_tx(c.red_bar, static_cast<uint32_t>(c.ks * c.nr * FusedRegions::NT * 4));
+        mbar_arrive_expect_tx(c.red_bar, static_cast<uint32_t>(c.ks * c.nr * TK * 4));
     }
 }
 
@@ -789,10 +791,12 @@ __device__ __forceinline__ void fused_split8(const FusedCtx& c, int at) {
 
 // Auxiliary warps (four consecutive warps; thread `at` = 32 * (warp % 4) + lane owns row `at`
 // of the tile): stage x, route, publish the mask, and accumulate this row's dW into corr.
-__device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float (&corr)[FusedRegions::NT],
-                                                float& row_scale) {
+// TK: tokens the kernel handles (8; 1 for the one-token engines, whose code is then that much
+// shorter on this latency-bound path).
+template <int TK>
+__device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float (&corr)[TK], float& row_scale) {
     using R = FusedRegions;
-    constexpr int NT = R::NT;
+    constexpr int NT = TK;
     const FusedParams& fp = *c.fp;
     const TCParams& p = fp.t;
     const int wi = at >> 5, lane = at & 31;
@@ -822,12 +826,15 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     v[u] = make_uint4(0u, 0u, 0u, 0u);
-                    if (g4 + u < ntok && inb) v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
+                    if (g4 + u < NT && g4 + u < ntok && inb)
+                        v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
                 }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
-                    if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                    if (g4 + u < NT) {
+                        sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                        if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                    }
                 }
             }
         }
@@ -850,10 +857,12 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     v[u] = make_uint4(0u, 0u, 0u, 0u);
-                    if (g4 + u < ntok) v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
+                    if (g4 + u < NT && g4 + u < ntok)
+                        v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                for (int u = 0; u < 4; ++u)
+                    if (g4 + u < NT) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
             }
         }
     }
@@ -965,8 +974,9 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
 // Auxiliary thread `at` with this split's row contribution v: with one split, write y; else
 // push the row to the cluster CTA that owns it and, for owned rows, add the splits in rank
 // order and write y.
-__device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, const float (&v)[FusedRegions::NT]) {
-    constexpr int NT = FusedRegions::NT;
+template <int TK>
+__device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, const float (&v)[TK]) {
+    constexpr int NT = TK;
     const TCParams& p = c.fp->t;
     const int ks = c.ks;
     pdl_wait();
@@ -988,8 +998,13 @@ __device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, cons
         const int orb = (128 * o) / ks, onr = (128 * (o + 1)) / ks - orb;
         const uint32_t dst = dsmem_addr(c.rbuf + (c.split * onr + (at - orb)) * NT, static_cast<uint32_t>(o));
         const uint32_t bar = dsmem_addr(c.red_bar, static_cast<uint32_t>(o));
-        st_async_v4_f32(dst, v[0], v[1], v[2], v[3], bar);
-        st_async_v4_f32(dst + 16, v[4], v[5], v[6], v[7], bar);
+        if constexpr (NT == 1) {
+            st_async_f32(dst, v[0], bar);
+        } else {
+            static_assert(NT == 8, "rows are pushed as one f32 or two float4");
+            st_async_v4_f32(dst, v[0], v[1], v[2], v[3], bar);
+            st_async_v4_f32(dst + 16, v[4], v[5], v[6], v[7], bar);
+        }
     }
     if (at < c.nr) {
         const bool ok = mbar_wait(c.red_bar, 0, p.status);
@@ -1038,7 +1053,7 @@ struct FusedTcCfg {
 template <bool F8>
 __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(FusedGroup g) {
     using C = FusedTcCfg<F8>;
-    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = FusedRegions::NT, CPB = C::kColsPerBlock;
+    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = FusedRegions::NT, CPB = C::kColsPerBlock, TK = NT;
     pdl_launch_dependents();
     __shared__ FusedParams fp;
     int bid;
@@ -1071,7 +1086,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
             mbar_init(&a_empty[i], 1);
         }
         mbar_init(done, 1);
-        fused_init_bars(c);
+        fused_init_bars<TK>(c);
         s_abort = 0;
         s_mask = 0u;
         s_split.nonfinite = 0;
@@ -1183,7 +1198,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
             if (lane == 0) mbar_arrive(&a_full[b]);
         }
     } else {
-        fused_aux_front(c, at, corr, row_scale);
+        fused_aux_front<TK>(c, at, corr, row_scale);
     }
     __syncwarp();
     if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
@@ -1226,7 +1241,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
             mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
         if (c.use_blk) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
     }
-    if (warp >= C::kAuxWarp0) fused_aux_finish(c, at, v);
+    if (warp >= C::kAuxWarp0) fused_aux_finish<TK>(c, at, v);
 }
 
 // ---- engine 2: mma.sync on the same frame
@@ -1255,7 +1270,7 @@ struct FusedMmaCfg {
 template <bool I8>
 __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(FusedGroup g) {
     using C = FusedMmaCfg;
-    constexpr int SKB = C::SKB, S = C::S, NT = FusedRegions::NT;
+    constexpr int SKB = C::SKB, S = C::S, NT = FusedRegions::NT, TK = I8 ? 1 : NT;
     pdl_launch_dependents();
     __shared__ FusedParams fp;
     int bid;
@@ -1280,7 +1295,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], C::kMmaWarps);
         }
-        fused_init_bars(c);
+        fused_init_bars<TK>(c);
         s_abort = 0;
         s_f16 = I8 ? 0 : 1;
         s_mask = 0u;
@@ -1290,7 +1305,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     if (c.ks > 1) cluster_arrive_relaxed();
 
     int issued = 0;
-    float corr[NT];
+    float corr[TK];
     float row_scale = 0.0f;
     const int at = 32 * (warp & 3) + lane;
     if (warp == C::kProducerWarp) {
@@ -1403,7 +1418,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
             }
         }
     } else {
-        fused_aux_front(c, at, corr, row_scale);
+        fused_aux_front<TK>(c, at, corr, row_scale);
     }
     __syncwarp();
     if (warp < C::kAuxWarp0 && c.ks > 1) cluster_wait();
@@ -1416,7 +1431,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     if (warp < C::kAuxWarp0) return;
     const int64_t row = c.rt * 128 + at;
     const float sc = row_scale;
-    float v[NT];
+    float v[TK];
     if (I8 && !s_f16) {
         // sum_k 16 (q_k - 8) X_k = sum_d 256^d S_d with X = x * 2^24: recombined in f64 (exact while
         // below 2^53, one rounding beyond), scaled by 2^-28 exactly, rounded once to f32
@@ -1426,14 +1441,12 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
         for (int d = 4; d >= 0; --d) sum = sum * 256.0 + static_cast<double>(ai[d]);
         const float a0 = static_cast<float>(sum * 0x1p-28);
         v[0] = row < p.N ? __fadd_rn(__fmul_rn(a0, sc), corr[0]) : 0.0f;
-#pragma unroll
-        for (int t = 1; t < NT; ++t) v[t] = 0.0f;
     } else {
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
+        for (int t = 0; t < TK; ++t)
             v[t] = row < p.N ? __fadd_rn(__fmul_rn(accbuf[at * C::kLd + t], sc), corr[t]) : 0.0f;
     }
-    fused_aux_finish(c, at, v);
+    fused_aux_finish<TK>(c, at, v);
 }
 
 // ---------------------------------------------------------------- launchers

@@ -119,6 +119,11 @@ __device__ __forceinline__ void st_async_f64(uint32_t raddr, double v, uint32_t 
                  "r"(rbar)
                  : "memory");
 }
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+                 "r"(__float_as_uint(v)), "r"(rbar)
+                 : "memory");
+}
 __device__ __forceinline__ void st_async_v4_f32(uint32_t raddr, float a, float b, float c, float d, uint32_t rbar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
                      raddr),
