@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-group", action="store_true",
                     help="one launch per projection, the reference's calling pattern (no grouped q/k/v, gate/up)")
+    ap.add_argument("--sweep", metavar="PATH",
+                    help="instead of the step: time single calls over a grid of shapes x tokens x routed "
+                         "fractions (one GPU) and write a markdown table to PATH")
     return ap.parse_args()
 
 
@@ -485,10 +488,115 @@ def run_ours(args, rank, world):
         print(json.dumps(out), flush=True)
 
 
+SWEEP_SHAPES = [("q/o", 3584, 3584), ("k/v", 512, 3584), ("gate/up", 18944, 3584), ("down", 3584, 18944)]
+SWEEP_TOKENS = [1, 4, 16, 64, 256, 1024, 4096]
+SWEEP_ROUTED = [0.0, 0.25, 1.0]
+SWEEP_POOL_BYTES = 512 * 2 ** 20  # round-robin over >= 4x L2 of distinct layers
+
+
+def run_sweep(args):
+    """Single-call times over shapes x tokens x routed fractions (1 % dW): every point replays a
+    CUDA graph of one call on each layer of a pool of distinct copies of the layer (>= 512 MB of
+    weights, so each call reads its weights from HBM), and reports the algorithmic bytes and
+    flops per call against the measured HBM and bf16 peaks."""
+    import torch
+
+    import saccade_core as sc
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    hbm, _ = measured_peak()
+    tc = 1617.5
+    try:
+        tc = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        pass
+    rows = []
+    for label, n, k in SWEEP_SHAPES:
+        packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
+        scale = ((0.02 * (3.0 + torch.rand(n, device=dev, generator=gen))) / 7.0).to(torch.float16)
+        nnz = int(round(n * k * args.fill))
+        flat = torch.unique(torch.randint(0, n * k, (int(nnz * 1.02) + 16,), device=dev, generator=gen))[:nnz]
+        rr, cc = flat // k, flat % k
+        rp = torch.zeros(n + 1, dtype=torch.int64, device=dev)
+        rp[1:] = torch.cumsum(torch.bincount(rr, minlength=n), 0)
+        vals = torch.randint(-127, 128, (flat.numel(),), dtype=torch.int8, device=dev, generator=gen).view(torch.uint8)
+        sp = sc.SparseDeltaMatrix(rp.to(torch.int32), cc.to(torch.int32), vals,
+                                  torch.tensor([0.006 / 127.0], dtype=torch.float16))
+        wbytes = n * k // 2
+        pool = max(4, min(1024, -(-SWEEP_POOL_BYTES // wbytes)))
+        ops = [sc.SaccadeLinearOp(packed, scale, sp, sc.SaccadeConfig(T4_BOOSTED, T8_NEVER), n, k, device=dev,
+                                  mode=args.mode) for _ in range(pool)]
+        real_nnz = ops[0].delta_nnz
+        del packed, scale, flat, rr, cc, rp, vals, sp
+        for m in SWEEP_TOKENS:
+            y = torch.empty((m, n), dtype=torch.float16, device=dev)
+            for frac in SWEEP_ROUTED:
+                r = int(round(frac * m))
+                x = torch.randn((m, k), device=dev, generator=gen)
+                if r:
+                    x[torch.randperm(m, device=dev, generator=gen)[:r]] *= 8.0
+                x = x.to(torch.float16)
+
+                def one_pass():
+                    for op in ops:
+                        op.forward(x, out=y)
+
+                g = sc.CapturedStep(one_pass, dev)
+                for _ in range(2):
+                    g.replay()
+                g.synchronize()
+                reps = 1
+                while True:
+                    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    with torch.cuda.stream(g.stream):
+                        s_ev.record()
+                        for _ in range(reps):
+                            g.replay()
+                        e_ev.record()
+                    g.synchronize()
+                    ms = s_ev.elapsed_time(e_ev)
+                    if ms >= 20.0 or reps >= 64:
+                        break
+                    reps *= 4
+                us = ms * 1e3 / (reps * pool)
+                ops[0].check_device()
+                b = call_bytes(n, k, m, real_nnz, r > 0)
+                fl = 2.0 * m * n * k + 2.0 * real_nnz * r
+                t_hbm, t_tc = b / (hbm * 1e3), fl / (tc * 1e6)  # microseconds
+                rows.append((label, n, k, m, frac, us, b / us / 1e3, fl / us / 1e6,
+                             "hbm" if t_hbm >= t_tc else "tensor", max(t_hbm, t_tc) / us, pool))
+                del g
+            del y
+        del ops
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    with open(args.sweep, "w") as f:
+        f.write(f"# C-TARQ linear: single-call sweep ({args.mode} mode, {args.fill:.0%} dW, f16 x)\n\n")
+        f.write("Command: `python bench.py --sweep " + args.sweep + (f" --mode {args.mode}" if args.mode != "fast" else "")
+                + "`\n\n")
+        f.write(f"Peaks: HBM {hbm} GB/s, bf16 dense {tc} TFLOP/s (MEASURED_PEAKS.json). `bound` is the larger of "
+                "bytes/HBM and flops/tensor; `frac` = that bound time / measured time. Routed = fraction of "
+                "the tokens boosted x8 (their variance clears t4 = 8). Each point replays one call on every "
+                "layer of a pool of distinct copies (>= 512 MB of weights).\n\n")
+        f.write("| shape | N x K | M | routed | us / call | GB/s | TFLOP/s | bound | frac | pool |\n")
+        f.write("|---|---|---|---|---|---|---|---|---|---|\n")
+        for (label, n, k, m, frac, us, gbs, tfl, bound, fr, pool) in rows:
+            f.write(f"| {label} | {n}x{k} | {m} | {frac:.0%} | {us:.2f} | {gbs:.0f} | {tfl:.1f} | {bound} | "
+                    f"{fr:.3f} | {pool} |\n")
+    print(json.dumps({"sweep": args.sweep, "points": len(rows)}), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.sweep:
+        if rank == 0:
+            run_sweep(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank)
         return

@@ -53,20 +53,22 @@ static int sm_count(int dev) {
 // layer or the token count, so one workspace can serve every layer: each call returns the
 // counters it used to zero.  Everything after that region is scratch rewritten per call.
 // Column splits of the router-fused decode kernel.  The splits of one 128-row tile form a
-// thread-block cluster (at most kMaxFusedCluster CTAs) that reduces through distributed
-// shared memory; aim at two CTAs per SM, with each CTA's column slice of x fitting its
-// shared-memory copy.  0 when the layer is too wide for one cluster.
-// The split count (= cluster size) for a launch of `rt` row tiles of `kb` column blocks: the
-// largest ks whose rt clusters can all be resident at once (one wave: cluster packing into the
-// GPCs decides, measured by the occupancy query), with at least two column blocks per CTA and
-// each CTA's slice of x within its shared-memory copy.  0 when no split fits a cluster.
+// thread-block cluster (at most kMaxFusedCluster CTAs) that reduces through distributed shared
+// memory.  The split count (= cluster size) for a launch of `rt` row tiles of `kb` column
+// blocks: the largest ks whose rt clusters can all be resident at once (one wave: cluster
+// packing into the GPCs decides, measured by the occupancy query for two CTAs per SM), with at
+// least two column blocks per CTA and each CTA's slice of x within its shared-memory copy.  A
+// launch whose weights all fit the rings of one CTA per SM gets half the clusters (about one
+// CTA per SM): it then fits beside its neighbour in the stream, whose CTAs hold the other
+// slot, and loads all of its weights while that one runs.  0 when no split fits a cluster.
 int choose_ksplit(int64_t rt, int64_t kb) {
     const int64_t min_ks = (kb + fused_max_kb(1) - 1) / fused_max_kb(1);
     if (min_ks > kMaxFusedCluster) return 0;
+    const bool small = rt * kb * 4096 <= fused_prefetch_bytes();
     int best = 0;
     for (int ks = 1; ks <= kMaxFusedCluster; ++ks) {
         if (ks < min_ks || (ks > 1 && kb / ks < 2)) continue;
-        const int cap = fused_max_active_clusters(ks);
+        const int cap = fused_max_active_clusters(ks) / (small ? 2 : 1);
         if (best == 0 || (cap > 0 && rt <= cap)) best = ks;  // larger ks wins while one wave holds
     }
     return best;

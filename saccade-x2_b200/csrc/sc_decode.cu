@@ -530,6 +530,8 @@ struct FusedParams {
     const uint8_t* dwblk;   // blocked dW (null: read the CSR)
     const uint32_t* dwoff;
     int ntp;                // staged token rows: 1, 2, 4 or 8
+    int full_row;           // one token whose whole row fits the staging region: one bulk copy of
+                            // it, and the one-token kernels route on their own sums (no exchange)
     RouteConsts rc;         // of Kfull
     double gT;              // bound factor of this kernel's own f32 sums (gamma of their depth, doubled)
 };
@@ -579,7 +581,7 @@ struct FusedRegions {
     static constexpr int kStats = kDw + static_cast<int>(kDwBlockMax);             // [ranks][8 tokens][3] f64
     static constexpr int kRed = kStats + kMaxFusedCluster * NT * 3 * 8;            // [ks][rows of rank][8] f32
     static constexpr int kBytes = kRed + (128 + kMaxFusedCluster) * NT * 4;
-    static constexpr int kBars = 4;                                                // x_ready dw_ready stats red
+    static constexpr int kBars = 5;                                                // x_ready dw_ready stats red xrow
 };
 
 // Scale and flags of the e4m3 split of this CTA's slice of x (one token).
@@ -599,6 +601,8 @@ struct FusedCtx {
     uint64_t* dw_ready;  // bulk copy of the dW block
     uint64_t* stats_bar; // cluster sums received
     uint64_t* red_bar;   // split partials of owned rows received
+    uint64_t* xrow_bar;  // bulk copy of the whole token (full_row)
+    unsigned char* xrow; // the staged whole token (full_row); xs is this CTA's slice of it
     int* s_abort;
     unsigned* s_mask;
     double (*s_red)[FusedRegions::NT][4];
@@ -608,10 +612,13 @@ struct FusedCtx {
     int bid;  // CTA index within this layer's part of the grid
     int split, ks, nkb, ntok, cs, rb, nr;
     bool use_blk;
+    bool local;  // route on this CTA's own sums of the staged whole token (one-token kernels)
 };
 
+// one_token: the kernel handles one token (its auxiliary path can route locally on a full row).
 __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, unsigned char* regions, uint64_t* bars,
-                                              int* s_abort, unsigned* s_mask, double (*s_red)[FusedRegions::NT][4]) {
+                                              int* s_abort, unsigned* s_mask, double (*s_red)[FusedRegions::NT][4],
+                                              bool one_token) {
     using R = FusedRegions;
     const TCParams& p = fp.t;
     FusedCtx c;
@@ -624,6 +631,9 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, un
     c.dw_ready = bars + 1;
     c.stats_bar = bars + 2;
     c.red_bar = bars + 3;
+    c.xrow_bar = bars + 4;
+    c.xrow = regions + R::kXs;
+    c.local = false;
     c.s_abort = s_abort;
     c.s_mask = s_mask;
     c.s_red = s_red;
@@ -639,6 +649,8 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, un
     c.rb = (128 * c.split) / c.ks;
     c.nr = (128 * (c.split + 1)) / c.ks - c.rb;
     c.use_blk = fp.dwblk != nullptr && p.nnz > 0;
+    c.local = one_token && fp.full_row;
+    if (c.local) c.xs = c.xrow + (fp.x_col0 + c.kb_begin * 64) * 2;
     c.split8 = nullptr;
     c.xb8 = regions + R::kXs + R::kXb8;
     return c;
@@ -652,9 +664,10 @@ __device__ __forceinline__ void fused_init_bars(const FusedCtx& c) {
     mbar_init(c.dw_ready, 1);
     mbar_init(c.stats_bar, 1);
     mbar_init(c.red_bar, 1);
+    mbar_init(c.xrow_bar, 1);
     fence_mbar_init();
     if (c.ks > 1) {
-        mbar_arrive_expect_tx(c.stats_bar, static_cast<uint32_t>(c.ks * c.ntok * 24));
+        if (!c.local) mbar_arrive_expect_tx(c.stats_bar, static_cast<uint32_t>(c.ks * c.ntok * 24));
         mbar_arrive_expect_tx(c.red_bar, static_cast<uint32_t>(c.ks * c.nr * TK * 4));
     }
 }
@@ -814,55 +827,78 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
     float a1[NT], a2[NT], a3[NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) a1[t] = a2[t] = a3[t] = 0.0f;
-    // pass 1: stage the slice (ntp token rows; rows >= ntok and columns >= K are zero)
-    for (int ci = at; ci < nin; ci += R::kAuxThreads) {
-        const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
-        const bool inb = colx < slice1;
-        unsigned char* dst = c.xs + ci * c.cs;
+    bool local = false;
+    if constexpr (TK == 1) local = c.local;
+    if (local) {
+        // the whole token in one bulk copy (its start and length are 16-byte multiples), the
+        // slice's padding past the token zeroed, the sums taken from shared memory
+        const uint32_t bytes = static_cast<uint32_t>(fp.Kfull * 2);
+        if (at == 0) {
+            mbar_arrive_expect_tx(c.xrow_bar, bytes);
+            bulk_g2s(c.xrow, static_cast<const unsigned char*>(fp.x) + p.tok0 * fp.x_stride * 2, bytes, c.xrow_bar);
+        }
+        if (!mbar_wait(c.xrow_bar, 0, p.status)) *c.s_abort = 1;
+        for (int64_t ci = at; ci < fp.Kfull / 8; ci += R::kAuxThreads)
+            sum_x8(*reinterpret_cast<const uint4*>(c.xrow + ci * 16), a1[0], a2[0], a3[0]);
+        // the slice's columns past the layer's K (padding blocks) must read as zeros
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const int64_t pad1 = (fp.x_col0 + c.kb_end * 64) * 2;
+        for (int64_t o = (fp.x_col0 + p.K) * 2 + static_cast<int64_t>(at) * 16; o < pad1; o += R::kAuxThreads * 16)
+            *reinterpret_cast<uint4*>(c.xrow + o) = make_uint4(0u, 0u, 0u, 0u);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.x_ready);
+    } else {
+        // pass 1: stage the slice (ntp token rows; rows >= ntok and columns >= K are zero)
+        for (int ci = at; ci < nin; ci += R::kAuxThreads) {
+            const int64_t colx = slice0 + static_cast<int64_t>(ci) * 8;
+            const bool inb = colx < slice1;
+            unsigned char* dst = c.xs + ci * c.cs;
 #pragma unroll
-        for (int g4 = 0; g4 < NT; g4 += 4) {
-            if (g4 < fp.ntp) {
-                uint4 v[4];
+            for (int g4 = 0; g4 < NT; g4 += 4) {
+                if (g4 < fp.ntp) {
+                    uint4 v[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    v[u] = make_uint4(0u, 0u, 0u, 0u);
-                    if (g4 + u < NT && g4 + u < ntok && inb)
-                        v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
-                }
+                    for (int u = 0; u < 4; ++u) {
+                        v[u] = make_uint4(0u, 0u, 0u, 0u);
+                        if (g4 + u < NT && g4 + u < ntok && inb)
+                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + colx);
+                    }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    if (g4 + u < NT) {
-                        sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
-                        if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                    for (int u = 0; u < 4; ++u) {
+                        if (g4 + u < NT) {
+                            sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
+                            if (g4 + u < fp.ntp) *reinterpret_cast<uint4*>(dst + (g4 + u) * 16) = v[u];
+                        }
                     }
                 }
             }
         }
-    }
-    if (c.split8) fused_split8(c, at);
-    fence_proxy_async_smem();  // the tensor cores read the staged x through the async proxy
-    __syncwarp();
-    if (lane == 0) mbar_arrive(c.x_ready);
-    // pass 2 (rows shards): this CTA's share of the columns outside the layer's slice
-    const int64_t nch = fp.Kfull / 8;
-    const int64_t in0 = fp.x_col0 / 8, in1 = (fp.x_col0 + p.K) / 8;
-    const int64_t nout = nch - (in1 - in0);
-    const int64_t o0 = (nout * c.split) / ks, o1 = (nout * (c.split + 1)) / ks;
-    for (int64_t j = o0 + at; j < o1; j += R::kAuxThreads) {
-        const int64_t ch = j < in0 ? j : j + (in1 - in0);
+        if (c.split8) fused_split8(c, at);
+        fence_proxy_async_smem();  // the tensor cores read the staged x through the async proxy
+        __syncwarp();
+        if (lane == 0) mbar_arrive(c.x_ready);
+        // pass 2 (rows shards): this CTA's share of the columns outside the layer's slice
+        const int64_t nch = fp.Kfull / 8;
+        const int64_t in0 = fp.x_col0 / 8, in1 = (fp.x_col0 + p.K) / 8;
+        const int64_t nout = nch - (in1 - in0);
+        const int64_t o0 = (nout * c.split) / ks, o1 = (nout * (c.split + 1)) / ks;
+        for (int64_t j = o0 + at; j < o1; j += R::kAuxThreads) {
+            const int64_t ch = j < in0 ? j : j + (in1 - in0);
 #pragma unroll
-        for (int g4 = 0; g4 < NT; g4 += 4) {
-            if (g4 < ntok) {
-                uint4 v[4];
+            for (int g4 = 0; g4 < NT; g4 += 4) {
+                if (g4 < ntok) {
+                    uint4 v[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    v[u] = make_uint4(0u, 0u, 0u, 0u);
-                    if (g4 + u < NT && g4 + u < ntok)
-                        v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
+                    for (int u = 0; u < 4; ++u) {
+                        v[u] = make_uint4(0u, 0u, 0u, 0u);
+                        if (g4 + u < NT && g4 + u < ntok)
+                            v[u] = load_x8(fp.x, fp.x_dtype, vec, (p.tok0 + g4 + u) * fp.x_stride + ch * 8);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (g4 + u < NT) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
                 }
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    if (g4 + u < NT) sum_x8(v[u], a1[g4 + u], a2[g4 + u], a3[g4 + u]);
             }
         }
     }
@@ -885,7 +921,18 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
         }
     }
     asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (ks > 1) {
+    if (local) {
+        if (at == 0) {
+            const double S1 = ((c.s_red[0][0][0] + c.s_red[0][0][1]) + c.s_red[0][0][2]) + c.s_red[0][0][3];
+            const double S2 = ((c.s_red[1][0][0] + c.s_red[1][0][1]) + c.s_red[1][0][2]) + c.s_red[1][0][3];
+            const double SA = ((c.s_red[2][0][0] + c.s_red[2][0][1]) + c.s_red[2][0][2]) + c.s_red[2][0][3];
+            const void* xrow = static_cast<const unsigned char*>(fp.x) + p.tok0 * fp.x_stride * 2;
+            const bool r = p.route_all ? true
+                                       : route_token(S1, S2, SA, fp.Kfull, fp.rc, fp.t4, fp.t8, xrow, fp.x_dtype,
+                                                     nullptr, fp.gT * SA, fp.gT * S2);
+            *c.s_mask = r ? 1u : 0u;
+        }
+    } else if (ks > 1) {
         cluster_wait();  // every mbarrier of the cluster is initialised
         if (wi == 0 && lane < ks) {
             // lane r sends this CTA's sums to rank r, into slot [split]
@@ -901,7 +948,7 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
             for (int q = 0; q < 3; ++q)
                 c.rstats[t * 3 + q] = ((c.s_red[q][t][0] + c.s_red[q][t][1]) + c.s_red[q][t][2]) + c.s_red[q][t][3];
     }
-    if (at == 0) {
+    if (at == 0 && !local) {
         const bool ok = ks == 1 || mbar_wait(c.stats_bar, 0, p.status);
         unsigned m = 0u;
         for (int t = 0; t < ntok && ok; ++t) {
@@ -993,6 +1040,7 @@ __device__ __forceinline__ void fused_aux_finish(const FusedCtx& c, int at, cons
         return;
     }
     {
+        if (c.local) cluster_wait();  // every mbarrier of the cluster is initialised
         // rank o owns rows [128 o / ks, 128 (o+1) / ks)
         const int o = (at * ks + ks - 1) / 128;
         const int orb = (128 * o) / ks, onr = (128 * (o + 1)) / ks - orb;
@@ -1072,7 +1120,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
     __shared__ F8Split s_split;
-    FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, done + 1, &s_abort, &s_mask, s_red);
+    FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, done + 1, &s_abort, &s_mask, s_red, false);
     if (F8) c.split8 = &s_split;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -1286,7 +1334,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     __shared__ int s_f16;  // this CTA accumulates in f32 (always without I8; with I8 for a non-finite slice)
     __shared__ unsigned s_mask;
     __shared__ double s_red[3][NT][4];
-    const FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red);
+    const FusedCtx c = fused_ctx(fp, bid, smem + C::kRegions, empty + S, &s_abort, &s_mask, s_red, TK == 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nst = (c.nkb + SKB - 1) / SKB;
 
@@ -1720,7 +1768,13 @@ static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     const int64_t nout = fp.Kfull / 8 - L.K / 8;
     const int64_t omax = (nout + ks - 1) / ks;
     constexpr int64_t A = FusedRegions::kAuxThreads;
-    const int64_t T = 8 * ((kbmax * 8 + A - 1) / A + (omax + A - 1) / A) + 5;
+    int64_t T = 8 * ((kbmax * 8 + A - 1) / A + (omax + A - 1) / A) + 5;
+    // one f16 token whose whole row (and the slice padding past it) fits below the fp8/integer
+    // engines' second region, 16-byte aligned: one bulk copy, each thread sums its chunks of it
+    const int64_t row_end = std::max<int64_t>(fp.Kfull, fp.x_col0 + L.KB * 64) * 2;
+    fp.full_row = f.m == 1 && fp.x_dtype == SC_F16 && (reinterpret_cast<uintptr_t>(fp.x) & 15) == 0 &&
+                  (fp.Kfull * 2) % 16 == 0 && row_end <= FusedRegions::kXb8;
+    if (fp.full_row) T = 8 * ((fp.Kfull / 8 + A - 1) / A) + 5;
     const double u = 5.9604644775390625e-08;
     fp.gT = 2.0 * static_cast<double>(T) * u / (1.0 - static_cast<double>(T) * u);
 }
@@ -1815,6 +1869,22 @@ int fused_max_active_clusters(int ks) {
 int fused_max_kb(int64_t m) {
     const int ntp = m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8;
     return FusedRegions::kXsBytes / (128 * ntp);
+}
+
+int64_t fused_prefetch_bytes() {
+    static std::atomic<int> sms[64];  // 0: not queried yet
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 0;
+    int n = sms[dev].load();
+    if (n == 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        sms[dev].store(n);
+    }
+    return static_cast<int64_t>(n) * FusedMmaCfg::S * FusedMmaCfg::kStageBytes;
 }
 
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s) {

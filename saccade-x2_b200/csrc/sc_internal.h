@@ -58,11 +58,7 @@ constexpr int64_t kDwBlockMax = 16 * 1024;
 #ifndef SC_FUSED_INT8
 #define SC_FUSED_INT8 1  // one-token decode in SC_MODE_FAST runs the s8 integer variant
 #endif
-#ifndef SC_FUSED_CTAS_PER_SM
-#define SC_FUSED_CTAS_PER_SM 2
-#endif
 constexpr int kMaxFusedCluster = SC_FUSED_MAX_CLUSTER;  // CTAs of one row tile (cluster size)
-constexpr int kFusedCtasPerSm = SC_FUSED_CTAS_PER_SM;   // grid target of the fused kernel
 
 int fused_ksplit(const Layer& L);
 int choose_ksplit(int64_t rt, int64_t kb);  // splits of a one-wave launch of rt row tiles x kb column blocks
@@ -179,6 +175,7 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s);
 // at once on the current device (cached per device).
 int fused_max_active_clusters(int ks);
 int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
+int64_t fused_prefetch_bytes();  // weight bytes the fused kernel prefetches with one CTA on every SM
 
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                             cudaStream_t s);

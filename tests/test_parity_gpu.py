@@ -279,6 +279,27 @@ def test_row_shards_sum_to_full(sc, count, mode):
     assert_fast_close(y_bits(y), yr, "rows shards f16")
 
 
+@pytest.mark.parametrize("t4", [0.5, 2.0])   # the N(0, 1) token (variance ~1) routed / not routed
+@pytest.mark.parametrize("count", [1, 3])
+def test_row_shards_one_token(sc, count, t4):
+    # one token: the integer engine stages the whole token with one bulk copy and routes on its
+    # own sums; a rows shard's slice starts inside the token and the last one ends in a padded
+    # block (K = 1000 is not a multiple of 64)
+    case = make_case(300, 1000, 1, 0.05, seed=43, boost=[], thresholds=(t4, 3e38))
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    assert rr[0] == (t4 < 1.0)
+    x = torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")
+    total = None
+    for i in range(count):
+        op = to_op(sc, case, mode="fast", shard=("rows", i, count) if count > 1 else None)
+        part, mask = op.forward_partial(x, return_routing=True)
+        op.check_device()
+        assert np.array_equal(mask.cpu().numpy(), rr)
+        total = part if total is None else total + part
+    assert_acc_close(total.cpu().numpy(), acc_ref, "rows shards, one token")
+    assert_fast_close(y_bits(sc.finalize(total)), yr, "rows shards, one token, f16")
+
+
 # ------------------------------------------------------------------ format producer on the GPU
 
 @pytest.mark.parametrize("n,k,fill", [(4864, 896, 0.01), (77, 200, 0.15), (256, 64, 1.0), (33, 8, 0.5)])
