@@ -997,7 +997,21 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
         const int n = roff[128];
         const uint16_t* bcol = reinterpret_cast<const uint16_t*>(c.dws + 272);
         const int8_t* bval = reinterpret_cast<const int8_t*>(c.dws + 272 + ((n * 2 + 15) / 16) * 16);
-        for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
+        // eight entries' loads issued together, then their adds in column order
+        const int e1 = roff[at + 1];
+        for (int e = roff[at]; e < e1; e += 8) {
+            const int cnt = e1 - e < 8 ? e1 - e : 8;
+            int cc[8];
+            int8_t vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                cc[u] = u < cnt ? bcol[e + u] : 0;
+                vv[u] = u < cnt ? bval[e + u] : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (u < cnt) add_entry(cc[u], vv[u]);
+        }
     } else {
         const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
         const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, c.kb_begin * 64);
@@ -1293,13 +1307,19 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
 }
 
 // ---- engine 2: mma.sync on the same frame
+#ifndef SC_FUSED_MMA_SKB
+#define SC_FUSED_MMA_SKB 4  // 4 KB blocks per ring stage of the mma.sync engines
+#endif
+#ifndef SC_FUSED_MMA_STAGES
+#define SC_FUSED_MMA_STAGES 3
+#endif
 struct FusedMmaCfg {
     static constexpr int kMmaWarps = 8;
     static constexpr int kProducerWarp = 8;
     static constexpr int kAuxWarp0 = 9;
     static constexpr int kThreads = 13 * 32;
-    static constexpr int SKB = 4;
-    static constexpr int S = 3;
+    static constexpr int SKB = SC_FUSED_MMA_SKB;
+    static constexpr int S = SC_FUSED_MMA_STAGES;
     static constexpr int kStageBytes = SKB * 4096;
     static constexpr int kLd = FusedRegions::NT + 1;
     static constexpr int kAccOff = S * kStageBytes;
