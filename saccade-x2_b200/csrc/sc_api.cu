@@ -325,6 +325,22 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         if (e != cudaSuccess) return cuda_fail(e, "exact kernel launch");
         return SC_OK;
     }
+    if (m >= kGemmMinTokens) {
+        GemmArgs g;
+        g.L = &L;
+        g.xk = xk;
+        g.Mp = w.Mp;
+        g.M = m;
+        g.mask = mask;
+        g.route_all = bypass ? 1 : 0;
+        g.y = y;
+        g.y_dtype = partial ? SC_F32 : y_dtype;
+        g.bias = partial ? nullptr : bias;
+        g.partial_out = partial ? 1 : 0;
+        e = launch_gemm(g, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+        return SC_OK;
+    }
     for (int64_t t0 = 0; t0 < m; t0 += w.chunk_tokens) {
         d.tok0 = t0;
         d.ntok = std::min<int64_t>(w.chunk_tokens, m - t0);

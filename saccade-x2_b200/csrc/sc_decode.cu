@@ -997,21 +997,7 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
         const int n = roff[128];
         const uint16_t* bcol = reinterpret_cast<const uint16_t*>(c.dws + 272);
         const int8_t* bval = reinterpret_cast<const int8_t*>(c.dws + 272 + ((n * 2 + 15) / 16) * 16);
-        // eight entries' loads issued together, then their adds in column order
-        const int e1 = roff[at + 1];
-        for (int e = roff[at]; e < e1; e += 8) {
-            const int cnt = e1 - e < 8 ? e1 - e : 8;
-            int cc[8];
-            int8_t vv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                cc[u] = u < cnt ? bcol[e + u] : 0;
-                vv[u] = u < cnt ? bval[e + u] : 0;
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (u < cnt) add_entry(cc[u], vv[u]);
-        }
+        for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
     } else {
         const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
         const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, c.kb_begin * 64);

@@ -145,6 +145,25 @@ struct DecodeArgs {
     int ksplit;
 };
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
+
+// Many tokens (prefill): tcgen05 GEMM over 128-token tiles of the router's staged x.
+struct GemmArgs {
+    const Layer* L;
+    const uint16_t* xk;     // staged x (xk_index layout), Mp token rows
+    int64_t Mp, M;
+    const uint8_t* mask;
+    int route_all;
+    void* y;                // [M, N]; f32 partial when partial_out
+    int y_dtype;
+    const float* bias;
+    int partial_out;
+};
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
+int64_t gemm_tile_tokens();
+#ifndef SC_GEMM_MIN_TOKENS
+#define SC_GEMM_MIN_TOKENS 9  // calls of at least this many tokens (not decoded fused) run the GEMM
+#endif
+constexpr int64_t kGemmMinTokens = SC_GEMM_MIN_TOKENS;
 cudaError_t launch_decode_exact(const DecodeArgs& a, int bypass, cudaStream_t s);
 
 // Decode with the router fused in (<= 8 tokens): one launch reads x directly.
