@@ -175,6 +175,13 @@ WsLayout plan_workspace(const Layer& L, int64_t m) {
     if (use_fused(L, m)) {
         w.ksplit = L.ks_fused;  // reduced inside the cluster: no partial buffer
         w.partial = take(16);
+    } else if (L.mode != SC_MODE_EXACT && m >= kGemmMinTokens) {
+        // prefill GEMM: x again in routed-first order, that order, split partials
+        w.gemm_ks = gemm_ksplit(L, m);
+        w.xkp = take(static_cast<size_t>(L.KB * 64 * (w.Mp + 16) * 2));
+        w.perm = take(static_cast<size_t>(4 * (w.Mp + 16)));
+        const int64_t tiles = RT * ((m + gemm_tile_tokens() - 1) / gemm_tile_tokens() + 1);
+        w.partial = take(static_cast<size_t>(w.gemm_ks > 1 ? tiles * w.gemm_ks * gemm_tile_tokens() * 128 * 4 : 16));
     } else {
         w.ksplit = static_cast<int>(ks);
         w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
@@ -296,6 +303,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
     r.scores = reinterpret_cast<float*>(base + w.scores);
     r.ridx = ridx;
     r.nrouted = nrouted;
+    r.perm = w.gemm_ks > 0 ? reinterpret_cast<int32_t*>(base + w.perm) : nullptr;
     r.counter = reinterpret_cast<uint32_t*>(base + w.counter);
     r.status = L.status;
     cudaError_t e = launch_router(r, stream);
@@ -325,14 +333,20 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         if (e != cudaSuccess) return cuda_fail(e, "exact kernel launch");
         return SC_OK;
     }
-    if (m >= kGemmMinTokens) {
+    if (w.gemm_ks > 0) {
         GemmArgs g;
         g.L = &L;
         g.xk = xk;
+        g.xkp = reinterpret_cast<uint16_t*>(base + w.xkp);
+        g.perm = reinterpret_cast<const int32_t*>(base + w.perm);
+        g.nrouted = nrouted;
         g.Mp = w.Mp;
+        g.Mpp = w.Mp + 16;
         g.M = m;
-        g.mask = mask;
         g.route_all = bypass ? 1 : 0;
+        g.ks = w.gemm_ks;
+        g.partial = reinterpret_cast<float*>(base + w.partial);
+        g.tcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
         g.y = y;
         g.y_dtype = partial ? SC_F32 : y_dtype;
         g.bias = partial ? nullptr : bias;
@@ -431,8 +445,12 @@ static void free_layer(Layer& L) {
     cudaFree(L.status);
     cudaFree(L.dwblk);
     cudaFree(L.dwoff);
+    cudaFree(L.fold);
+    cudaFree(L.foldoff);
     L.dwblk = nullptr;
     L.dwoff = nullptr;
+    L.fold = nullptr;
+    L.foldoff = nullptr;
     L.wq = nullptr;
     L.scale = nullptr;
     L.rowptr = nullptr;
@@ -650,6 +668,12 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
         L.dwblk = b.blk;
         L.dwoff = b.off;
         L.device_bytes += b.bytes;
+    }
+    if (e == cudaSuccess && L.nnz > 0) {
+        // dW/s lists of the prefill GEMM, from the widened row scales
+        std::vector<float> hs(static_cast<size_t>(L.Np));
+        e = cudaMemcpy(hs.data(), L.scale, L.Np * 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = build_fold_lists(L, srp.data(), scol.data(), sval.data(), hs.data());
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(tmp_packed);

@@ -60,14 +60,6 @@ struct TCParams {
     uint32_t* status;
 };
 
-__device__ __forceinline__ int64_t lower_bound_u16(const uint16_t* col, int64_t lo, int64_t hi, int64_t key) {
-    while (lo < hi) {
-        const int64_t mid = (lo + hi) >> 1;
-        if (static_cast<int64_t>(col[mid]) < key) lo = mid + 1;
-        else hi = mid;
-    }
-    return lo;
-}
 
 // ---------------------------------------------------------------- shared pieces
 

@@ -252,6 +252,16 @@ __device__ __forceinline__ uint16_t hi16(uint32_t v) { return static_cast<uint16
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// First index in [lo, hi) of an ascending u16 column list whose column is >= key.
+__device__ __forceinline__ int64_t lower_bound_u16(const uint16_t* col, int64_t lo, int64_t hi, int64_t key) {
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (static_cast<int64_t>(col[mid]) < key) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
 // Index (in halves) of element (token t, column col) of the staged activation layout
 // xk[KB][Mp/8][8 chunks][8 tokens][8 halves]: for each 64-column block and group of 8
 // tokens, 8 "core matrices" of 8 tokens x 8 columns (128 B each), which is the canonical

@@ -1,32 +1,49 @@
 // sc_gemm.cu -- C-TARQ linear for many tokens (prefill): a tcgen05 GEMM over 128-token tiles.
 //
-// One CTA computes a 128-row x 128-token tile of Y over the whole K (op.rs:99-178 for those
-// rows and tokens).  The router (sc_router.cu) has decided every token and staged x as K-major
-// core matrices (xk_index): for one 64-column block the 8-token groups of a tile are 1 KB each
-// and contiguous, so a tile's activations arrive with one bulk copy per block and are the MMA's
-// B operand as they lie (LBO 128 B between 8-column chunks, SBO 1 KB between token groups).
+// One CTA computes a 128-row x 128-token tile of Y over a range of K (op.rs:99-178 for those
+// rows and tokens).  The router (sc_router.cu) has decided every token, staged x as K-major
+// core matrices (xk_index) and listed the tokens routed first (perm); k_gather_tokens copies
+// the staged x into that order, so the routed tokens fill whole tiles.  For one 64-column
+// block the 8-token groups of a tile are 1 KB each and contiguous, so a tile's activations
+// arrive with one bulk copy per block and are the MMA's B operand as they lie (LBO 128 B
+// between 8-column chunks, SBO 1 KB between token groups).
 //
-// Roles (10 warps, one CTA per SM):
-//   producer lane   weights (4 KB per block, contiguous per row tile) and the tile's x blocks
-//                   through a ring of S stages; the first stages' weights are requested before
-//                   the dependency wait (they do not depend on the previous kernel);
-//   8 dequantising  warps, one 16-row tile each: W4U words -> f16 (q - 8) with dequant_word, into
-//                   tensor memory with tcgen05.st.16x256b (A operand, natural K order);
+// Roles (18 warps, one CTA per SM):
+//   producer lane   weights (4 KB per block, contiguous per row tile), the tile's x blocks and,
+//                   for a tile of routed tokens, the blocks' dW lists, through a ring of S
+//                   stages; the first stages' weights are requested before the dependency wait;
+//   16 dequantising warps, one 16-row tile each, in two sets taking alternate blocks (two
+//                   independent store pipelines): W4U words -> f16 (q - 8) with dequant_word; in a
+//                   tile of routed tokens the row's dW is folded in as (q - 8) + dW/s (s the row
+//                   scale), one f16 per weight; then into tensor memory with tcgen05.st.16x256b;
 //   MMA warp        one elected lane issues tcgen05.mma.kind::f16 M=128 N=128 K=16 (A from tensor
-//                   memory, B from shared memory, f32 D in tensor memory), 4 per block, and
-//                   commits the A buffer and ring stage it consumed;
-//   epilogue        the dequantising warps read D (tcgen05.ld, 32 lanes x 8 tokens), add the
-//                   row's dW for routed tokens (CSR entries in column order, x from the staged
-//                   copy, op.rs:152-170) and write y = f16(acc * s + dW) (+ bias after rounding).
+//                   memory, B from shared memory, f32 D in tensor memory), 4 per block;
+//   epilogue        the dequantising warps read D (tcgen05.ld, 32 rows x 8 tokens) and write
+//                   y = f16(acc * s [+ dW]) (+ bias after rounding) for the tile's tokens.  A tile
+//                   holding both routed and other tokens (at most one per row tile), or a layer
+//                   without fold lists, adds the routed tokens' dW here from the CSR entries in
+//                   column order (op.rs:152-170).  With column splits each CTA writes its f32
+//                   partial and the last one of the tile adds them in split order.
 //
-// The MMA runs at N = 128 (64 cycles per instruction, 4x the tokens of the 32-token decode
-// kernel per instruction), and each weight block is fetched once per 128 tokens.
+// Numerics (fast mode): the products are f16 x f16 -> f32 on the tensor cores; folding dW/s into
+// the weight rounds it to f16 next to an integer of magnitude <= 8 (2^-8 absolute), so a routed
+// row's dW carries a relative error of up to ~2^-8 of its own, far below the fast-mode tolerance
+// on y.
+#include <cuda_fp16.h>
+
+#include <algorithm>
 #include <atomic>
+#include <cmath>
+#include <cstring>
+#include <vector>
 
 #include "sc_device.cuh"
 #include "sc_internal.h"
 
 namespace sc {
+
+constexpr int kFoldCap = 2048;  // bytes of one block's dW list in a ring stage
+constexpr int kFoldHdr = 528;   // its header: u16 entry offsets [8 tiles of 16 rows][33 lanes + end]
 
 struct GemmParams {
     const uint32_t* wq;
@@ -36,11 +53,18 @@ struct GemmParams {
     const int8_t* val;
     float ds;
     int64_t nnz;
-    const uint16_t* xk;
-    int64_t Mp, M;
-    const uint8_t* mask;
+    const uint8_t* fold;
+    const uint32_t* foldoff;
+    const uint16_t* xk;     // staged x in token order (read when perm is the identity)
+    const uint16_t* xkp;
+    const int32_t* perm;
+    const int32_t* nrouted;
+    int64_t Mp, M, Mpp;     // xk token rows, tokens, xkp positions
     int route_all;
-    int64_t N, KB, RT, T;   // rows, column blocks, row tiles, token tiles
+    int64_t N, KB, RT, T;   // rows, column blocks, row tiles, token tiles (one more than ceil(M/128))
+    int ks;
+    float* partial;
+    uint32_t* tcount;
     void* y;
     int y_dtype;
     const float* bias;
@@ -50,16 +74,17 @@ struct GemmParams {
 
 struct GemmCfg {
     static constexpr int NT = 128;                   // tokens per tile (MMA N)
-    static constexpr int kDqWarps = 8;               // two per TMEM sub-partition, one 16-row tile each
-    static constexpr int kProducerWarp = 8;
-    static constexpr int kMmaWarp = 9;
-    static constexpr int kThreads = 10 * 32;
+    static constexpr int kDqWarps = 16;              // 2 sets (even / odd blocks) x 8 tiles of 16 rows
+    static constexpr int kProducerWarp = 16;
+    static constexpr int kMmaWarp = 17;
+    static constexpr int kThreads = 18 * 32;
     static constexpr int G = NT / 8;                 // 8-token groups of a tile
     static constexpr int SKB = 2;                    // 64-column blocks per ring stage
     static constexpr int S = 4;
     static constexpr int kWBytes = SKB * 4096;
     static constexpr int kXBytes = SKB * G * 1024;
-    static constexpr int kStageBytes = kWBytes + kXBytes;
+    static constexpr int kFBytes = SKB * kFoldCap;
+    static constexpr int kStageBytes = kWBytes + kXBytes + kFBytes;
     static constexpr int kAB = 4;                    // TMEM A buffers, one block (32 columns) each
     static constexpr uint32_t kTmemCols = 256;       // D in [0, 128), A buffers in [128, 256)
     static constexpr int kBarOff = S * kStageBytes;
@@ -69,6 +94,55 @@ struct GemmCfg {
     static_assert(NT + kAB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
     static_assert(kTotal <= 227 * 1024, "shared memory");
 };
+
+// Add f16 value `v` to the half `hi` of 32-bit register h[slot / 4][slot % 4] (static indices:
+// the switch keeps the 16 registers out of local memory).
+__device__ __forceinline__ void fold_add(uint32_t (&h)[4][4], int slot, int hi, uint16_t v) {
+    const __half2 add = hi ? __halves2half2(__ushort_as_half(0), __ushort_as_half(v))
+                           : __halves2half2(__ushort_as_half(v), __ushort_as_half(0));
+#define SC_FOLD_CASE(q)                                                                  \
+    case q: {                                                                            \
+        __half2 t = __hadd2(*reinterpret_cast<const __half2*>(&h[(q) / 4][(q) % 4]), add); \
+        h[(q) / 4][(q) % 4] = *reinterpret_cast<const uint32_t*>(&t);                     \
+        break;                                                                           \
+    }
+    switch (slot) {
+        SC_FOLD_CASE(0) SC_FOLD_CASE(1) SC_FOLD_CASE(2) SC_FOLD_CASE(3)
+        SC_FOLD_CASE(4) SC_FOLD_CASE(5) SC_FOLD_CASE(6) SC_FOLD_CASE(7)
+        SC_FOLD_CASE(8) SC_FOLD_CASE(9) SC_FOLD_CASE(10) SC_FOLD_CASE(11)
+        SC_FOLD_CASE(12) SC_FOLD_CASE(13) SC_FOLD_CASE(14) SC_FOLD_CASE(15)
+        default: break;
+    }
+#undef SC_FOLD_CASE
+}
+
+// Token tile tt of a row tile, from the routed count R (read after the dependency wait): tiles
+// [0, ceil(R/128)) hold the routed positions [0, R), the next ones the others from
+// round_up(R, 8); the last tile of the launch may be empty.  identity: perm is the identity
+// (nothing or everything routed) and x is read in token order.
+struct GemmTile {
+    int64_t R, pos0;
+    int ntile;
+    bool routed, fold, identity;
+};
+__device__ __forceinline__ GemmTile gemm_tile(const GemmParams& p, int64_t tt) {
+    constexpr int NT = GemmCfg::NT;
+    GemmTile g;
+    g.R = p.route_all ? p.M : static_cast<int64_t>(*p.nrouted);
+    const int64_t TR = (g.R + NT - 1) / NT, RB = (g.R + 7) & ~static_cast<int64_t>(7);
+    g.identity = g.R == 0 || g.R == p.M;
+    g.routed = tt < TR;
+    if (g.routed) {
+        g.pos0 = tt * NT;
+        g.ntile = static_cast<int>(imin64(NT, g.R - g.pos0));
+    } else {
+        g.pos0 = RB + (tt - TR) * NT;
+        const int64_t left = RB + (p.M - g.R) - g.pos0;
+        g.ntile = static_cast<int>(left <= 0 ? 0 : imin64(NT, left));
+    }
+    g.fold = g.routed && p.foldoff != nullptr;
+    return g;
+}
 
 __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams p) {
     using C = GemmCfg;
@@ -81,13 +155,24 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
     uint64_t* done = a_empty + AB;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
     __shared__ int s_abort;
+    __shared__ int s_last;
+    __shared__ int s_empty;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t rt = blockIdx.x / p.T;
-    const int64_t tok0 = (blockIdx.x - rt * p.T) * NT;
-    const int ntile = static_cast<int>(imin64(NT, p.M - tok0));
-    const int greal = (ntile + 7) >> 3;
-    const int nkb = static_cast<int>(p.KB);
+    // token-tile-major order: the last token tile (empty unless the routed and the other tokens
+    // both leave a partial tile) comes last in the grid
+    const int64_t tile_id = blockIdx.x / p.ks;
+    const int sp = static_cast<int>(blockIdx.x - tile_id * p.ks);
+    const int64_t tt = tile_id / p.RT;
+    const int64_t rt = tile_id - tt * p.RT;
+    if (tt == p.T - 1) {
+        // the only tile that can be empty: look before setting anything up
+        pdl_wait();
+        if (gemm_tile(p, tt).ntile == 0) return;
+    }
+    const int kb_begin = static_cast<int>((p.KB * sp) / p.ks);
+    const int kb_end = static_cast<int>((p.KB * (sp + 1)) / p.ks);
+    const int nkb = kb_end - kb_begin;
 
     pdl_launch_dependents();
     // token groups past the real tokens are never copied: they read as zero in every stage
@@ -102,12 +187,13 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < AB; ++i) {
-            mbar_init(&a_full[i], C::kDqWarps);
+            mbar_init(&a_full[i], C::kDqWarps / 2);  // one set writes a block
             mbar_init(&a_empty[i], 1);
         }
         mbar_init(done, 1);
         fence_mbar_init();
         s_abort = 0;
+        s_empty = 0;
     }
     if (warp == C::kMmaWarp) {
         tmem_alloc(tmem_slot, C::kTmemCols);
@@ -120,22 +206,32 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
 
     int issued = 0;
     const int nst = (nkb + SKB - 1) / SKB;
+    const int pre = nst < S ? nst : S;
     if (warp == C::kProducerWarp) {
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
-            const int64_t Gp = p.Mp >> 3;
-            const int pre = nst < S ? nst : S;
             for (int it = 0; it < pre; ++it, ++issued) {
-                const int kb0 = it * SKB;
-                const int n = nkb - kb0 < SKB ? nkb - kb0 : SKB;
+                const int kb0 = kb_begin + it * SKB;
+                const int n = kb_end - kb0 < SKB ? kb_end - kb0 : SKB;
                 mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
                 bulk_g2s_stream(smem + it * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
                                 static_cast<uint32_t>(n * 4096), &full[it], pol);
             }
             pdl_wait();
-            for (int it = 0; it < nst; ++it) {
-                const int slot = it % S, kb0 = it * SKB;
-                const int n = nkb - kb0 < SKB ? nkb - kb0 : SKB;
+            const GemmTile g = gemm_tile(p, tt);
+            const int64_t pos0 = g.pos0;
+            const int greal = (g.ntile + 7) >> 3;
+            const bool fold = g.fold;
+            const uint16_t* xsrc = g.identity ? p.xk : p.xkp;
+            const int64_t Gp = (g.identity ? p.Mp : p.Mpp) >> 3;
+            if (g.ntile == 0) {
+                // no tokens: complete the prefetched stages' phases (their weights still land)
+                s_empty = 1;
+                for (int it = 0; it < pre; ++it) mbar_arrive_expect_tx(&full[it], 0u);
+            }
+            for (int it = 0; it < nst && g.ntile > 0; ++it) {
+                const int slot = it % S, kb0 = kb_begin + it * SKB;
+                const int n = kb_end - kb0 < SKB ? kb_end - kb0 : SKB;
                 unsigned char* st = smem + slot * C::kStageBytes;
                 if (it >= S) {
                     if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
@@ -147,18 +243,27 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
                                     pol);
                     ++issued;
                 }
-                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * greal * 1024));
-                for (int j = 0; j < n; ++j)
-                    bulk_g2s(st + C::kWBytes + j * G * 1024, p.xk + ((kb0 + j) * Gp + (tok0 >> 3)) * 512,
+                uint32_t fbytes = 0;
+                if (fold) fbytes = p.foldoff[rt * p.KB + kb0 + n] - p.foldoff[rt * p.KB + kb0];
+                mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * greal * 1024) + fbytes);
+                for (int j = 0; j < n; ++j) {
+                    bulk_g2s(st + C::kWBytes + j * G * 1024, xsrc + ((kb0 + j) * Gp + (pos0 >> 3)) * 512,
                              static_cast<uint32_t>(greal * 1024), &full[slot]);
+                    if (fold) {
+                        const uint32_t o0 = p.foldoff[rt * p.KB + kb0 + j], o1 = p.foldoff[rt * p.KB + kb0 + j + 1];
+                        bulk_g2s(st + C::kWBytes + C::kXBytes + j * kFoldCap, p.fold + o0, o1 - o0, &full[slot]);
+                    }
+                }
             }
         }
     } else if (warp == C::kMmaWarp) {
         // warp-uniform loop, one elected lane issues (the same lane every time, so its commits
         // track all of its MMAs)
         const uint32_t idesc = idesc_f16_f32(128, NT);
+        pdl_wait();
         bool ok = true;
-        for (int j = 0; j < nkb && ok; ++j) {
+        const int nmma = gemm_tile(p, tt).ntile > 0 ? nkb : 0;
+        for (int j = 0; j < nmma && ok; ++j) {
             const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
             if (kbl == 0) ok = mbar_wait(&full[slot], (s / S) & 1, p.status);
             if (ok) ok = mbar_wait(&a_full[b], (j / AB) & 1, p.status);
@@ -180,81 +285,108 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         if (elect_one()) tc_commit(done);  // also after an abort, so that the TMEM can be released
         __syncwarp();
     } else {
-        const int sp = warp & 3, q = warp >> 2;
-        const int tile = 2 * sp + q;
-        const uint32_t lane_addr = static_cast<uint32_t>(32 * sp + 16 * q) << 16;
-        for (int j = 0; j < nkb; ++j) {
+        const int sq = warp & 3, q = (warp >> 2) & 1, set = warp >> 3;
+        const int tile = 2 * sq + q;
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * sq + 16 * q) << 16;
+        pdl_wait();
+        const GemmTile g = gemm_tile(p, tt);
+        const int64_t pos0 = g.pos0, R = g.R;
+        const int ntile = g.ntile;
+        const bool fold = g.fold;
+        const int64_t Mx = g.identity ? p.Mp : p.Mpp;  // token rows of the x copy read
+        const uint16_t* xsrc = g.identity ? p.xk : p.xkp;
+        for (int j = set; j < nkb && ntile > 0; j += 2) {
             const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
             bool ok = true;
-            if (kbl == 0 && !mbar_wait(&full[slot], (s / S) & 1, p.status)) ok = false;
+            if (!mbar_wait(&full[slot], (s / S) & 1, p.status)) ok = false;  // each set waits for its own blocks
             if (ok && j >= AB && !mbar_wait(&a_empty[b], ((j / AB) - 1) & 1, p.status)) ok = false;
             if (!ok) {
                 s_abort = 1;
                 break;
             }
             tc_fence_after();
-            const uint4 wv =
-                *reinterpret_cast<const uint4*>(smem + slot * C::kStageBytes + kbl * 4096 + tile * 512 + lane * 16);
+            const unsigned char* stg = smem + slot * C::kStageBytes;
+            const uint4 wv = *reinterpret_cast<const uint4*>(stg + kbl * 4096 + tile * 512 + lane * 16);
             const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+            uint32_t h[4][4];
 #pragma unroll
-            for (int st = 0; st < 4; ++st) {
-                uint32_t h[4];
-                dequant_word(words[st], h);
-                tc_st_16x256b(tmem + lane_addr + NT + b * 32 + st * 8, h[0], h[2], h[1], h[3]);
+            for (int st = 0; st < 4; ++st) dequant_word(words[st], h[st]);
+            if (fold) {
+                // this lane's entries of the block (register slot, half, f16 dW/s)
+                const unsigned char* lst = stg + C::kWBytes + C::kXBytes + kbl * kFoldCap;
+                const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + tile * 33 + lane;
+                const uint32_t* ent = reinterpret_cast<const uint32_t*>(lst + kFoldHdr);
+                const int e1 = offs[1];
+                for (int e = offs[0]; e < e1; ++e) {
+                    const uint32_t w = ent[e];
+                    fold_add(h, static_cast<int>((w >> 5) & 15u), static_cast<int>((w >> 9) & 1u),
+                             static_cast<uint16_t>(w >> 16));
+                }
             }
+#pragma unroll
+            for (int st = 0; st < 4; ++st)
+                tc_st_16x256b(tmem + lane_addr + NT + b * 32 + st * 8, h[st][0], h[st][2], h[st][1], h[st][3]);
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[b]);
         }
-        // epilogue: warp q of sub-partition sp owns rows 32 sp + lane and tokens [64 q, 64 q + 64)
-        if (mbar_wait(done, 0, p.status) && !s_abort) {
+        // epilogue: warp qq = warp / 4 of sub-partition sq owns rows 32 sq + lane and tokens [32 qq, 32 qq + 32)
+        if (ntile > 0 && mbar_wait(done, 0, p.status) && !s_abort) {
             tc_fence_after();
-            pdl_wait();  // y and the routing mask belong to this call's predecessors' stream order
-            const int64_t row = rt * 128 + 32 * sp + lane;
+            const int64_t row = rt * 128 + 32 * sq + lane;
             const bool live = row < p.N;
             const float sc = live ? p.scale[row] : 0.0f;
-            const int64_t e0 = (live && p.nnz > 0) ? p.rowptr[row] : 0, e1 = (live && p.nnz > 0) ? p.rowptr[row + 1] : 0;
-            const uint32_t lane_rows = static_cast<uint32_t>(32 * sp) << 16;
+            // dW entries of this row inside the CTA's columns, for routed tokens not folded
+            int64_t e0 = 0, e1 = 0;
+            if (!fold && live && p.nnz > 0 && g.routed) {
+                const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
+                e0 = p.ks == 1 ? lo : lower_bound_u16(p.col, lo, hi, static_cast<int64_t>(kb_begin) * 64);
+                e1 = p.ks == 1 ? hi : lower_bound_u16(p.col, e0, hi, static_cast<int64_t>(kb_end) * 64);
+            }
+            const uint32_t lane_rows = static_cast<uint32_t>(32 * sq) << 16;
+            float* part = p.partial + ((tile_id * p.ks + sp) * NT) * 128;
+            const int qq = warp >> 2;
 #pragma unroll 1
-            for (int cb = 8 * q; cb < 8 * q + 8; ++cb) {
+            for (int cb = 4 * qq; cb < 4 * qq + 4; ++cb) {
                 const int t0 = cb * 8;
                 if (t0 >= ntile) break;
                 uint32_t d[8];
                 tc_ld8(tmem + lane_rows + t0, d);
                 tc_wait_ld();
-                unsigned rm = 0;
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (t0 + u < ntile && (p.route_all || p.mask[tok0 + t0 + u])) rm |= 1u << u;
                 float corr[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) corr[u] = 0.0f;
-                if (rm) {
+                const int nr = g.routed ? static_cast<int>(imin64(8, ntile - t0)) : 0;  // routed, unfolded
+                if (e1 > e0 && nr > 0) {
                     for (int64_t e = e0; e < e1; ++e) {
                         const int64_t cl = p.col[e];
                         const float v = __fmul_rn(static_cast<float>(p.val[e]), p.ds);
-                        const uint16_t* xg = p.xk + xk_index(cl, static_cast<int>(tok0 + t0), static_cast<int>(p.Mp));
+                        const uint16_t* xg = xsrc + xk_index(cl, static_cast<int>(pos0 + t0), static_cast<int>(Mx));
 #pragma unroll
                         for (int u = 0; u < 8; ++u)
-                            if ((rm >> u) & 1u) corr[u] = __fadd_rn(corr[u], __fmul_rn(h2f(xg[u * 8]), v));
+                            if (u < nr) corr[u] = __fadd_rn(corr[u], __fmul_rn(h2f(xg[u * 8]), v));
                     }
                 }
-                if (live) {
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        if (t0 + u < ntile) {
-                            const float v = __fadd_rn(__fmul_rn(__uint_as_float(d[u]), sc), corr[u]);
-                            const int64_t oi = (tok0 + t0 + u) * p.N + row;
+                for (int u = 0; u < 8; ++u) {
+                    if (t0 + u < ntile) {
+                        const float v = __fadd_rn(__fmul_rn(__uint_as_float(d[u]), sc), corr[u]);
+                        if (p.ks > 1) {
+                            part[(t0 + u) * 128 + 32 * sq + lane] = v;
+                        } else if (live) {
+                            const int64_t oi = static_cast<int64_t>(p.perm[pos0 + t0 + u]) * p.N + row;
                             if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = v;
                             else store_output(p.y, p.y_dtype, oi, v, p.bias, row);
                         }
                     }
                 }
             }
-        } else {
+            if (p.ks > 1) __threadfence();  // the partials, before this CTA's split is counted
+        } else if (ntile > 0) {
             s_abort = 1;
         }
+        (void)R;
         tc_fence_before();
     }
     __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
@@ -265,12 +397,74 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         tc_fence_after();
         tmem_dealloc(tmem, C::kTmemCols);
     }
-    if (s_abort && warp == C::kProducerWarp && lane == 0)
-        for (int it = issued > S ? issued - S : 0; it < issued; ++it)
-            mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+    if (s_abort || s_empty) {
+        if (warp == C::kProducerWarp && lane == 0)
+            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
+                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
+        return;
+    }
+    if (p.ks > 1) {
+        const GemmTile g = gemm_tile(p, tt);
+        const int64_t pos0 = g.pos0;
+        const int ntile = g.ntile;
+        // the last split of the tile to finish adds the partials in split order
+        if (tid == 0) s_last = atomicAdd(&p.tcount[tile_id], 1u) == static_cast<unsigned>(p.ks - 1);
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        const float* base = p.partial + (tile_id * p.ks * NT) * 128;
+        for (int i = tid; i < ntile * 128; i += C::kThreads) {
+            const int t = i >> 7, rl = i & 127;
+            const int64_t r = rt * 128 + rl;
+            if (r >= p.N) continue;
+            float v = 0.0f;
+            for (int k = 0; k < p.ks; ++k) v = __fadd_rn(v, __ldcg(base + (k * NT + t) * 128 + rl));
+            const int64_t oi = static_cast<int64_t>(p.perm[pos0 + t]) * p.N + r;
+            if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = v;
+            else store_output(p.y, p.y_dtype, oi, v, p.bias, r);
+        }
+        if (tid == 0) p.tcount[tile_id] = 0u;
+    }
+}
+
+// xkp[position p] = xk[token perm[p]] for every 16-byte chunk, positions laid out as the GEMM
+// tiles read them (routed [0, R), the others from round_up(R, 8)); other positions are zeroed.
+// One thread per destination chunk, in destination order (coalesced stores).
+__global__ void k_gather_tokens(const uint16_t* __restrict__ xk, uint16_t* __restrict__ xkp,
+                                const int32_t* __restrict__ perm, const int32_t* __restrict__ nrouted, int route_all,
+                                int64_t M, int64_t Mp, int64_t Mpp, int64_t KB) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t R = route_all ? M : *nrouted;
+    if (R == 0 || R == M) return;  // perm is the identity: the GEMM reads xk itself
+    const int64_t RB = (R + 7) & ~static_cast<int64_t>(7);
+    const int64_t total = KB * Mpp * 8;  // chunks
+    const int64_t Gpp = Mpp >> 3;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        // i = ((kb * Mpp/8 + p/8) * 8 + chunk) * 8 + p%8
+        const int64_t pi = i & 7, ch = (i >> 3) & 7, rest = i >> 6;
+        const int64_t kb = rest / Gpp, pg = rest - kb * Gpp;
+        const int64_t pos = pg * 8 + pi;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (pos < R || (pos >= RB && pos < RB + (M - R))) {
+            const int t = perm[pos];
+            v = *reinterpret_cast<const uint4*>(xk + xk_index(kb * 64 + ch * 8, t, static_cast<int>(Mp)));
+        }
+        *reinterpret_cast<uint4*>(xkp + i * 8) = v;
+    }
 }
 
 int64_t gemm_tile_tokens() { return GemmCfg::NT; }
+
+int gemm_ksplit(const Layer& L, int64_t m) {
+    // column splits while the tiles alone leave SMs idle, each split keeping >= 8 blocks (the
+    // launch's extra token tile is usually empty and is not counted)
+    const int64_t tiles = (L.Np / 128) * ((m + GemmCfg::NT - 1) / GemmCfg::NT);
+    int64_t ks = std::max<int64_t>(1, static_cast<int64_t>(L.sms) / std::max<int64_t>(1, tiles));
+    ks = std::min<int64_t>(ks, std::min<int64_t>(16, std::max<int64_t>(1, L.KB / 8)));
+    return static_cast<int>(ks);
+}
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     const Layer& L = *a.L;
@@ -282,31 +476,121 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     p.val = L.val;
     p.ds = L.ds;
     p.nnz = L.nnz;
+    p.fold = L.fold;
+    p.foldoff = L.foldoff;
     p.xk = a.xk;
+    p.xkp = a.xkp;
+    p.perm = a.perm;
+    p.nrouted = a.nrouted;
     p.Mp = a.Mp;
     p.M = a.M;
-    p.mask = a.mask;
+    p.Mpp = a.Mpp;
     p.route_all = a.route_all;
     p.N = L.N;
     p.KB = L.KB;
     p.RT = L.Np / 128;
-    p.T = (a.M + GemmCfg::NT - 1) / GemmCfg::NT;
+    p.T = (a.M + GemmCfg::NT - 1) / GemmCfg::NT + 1;
+    p.ks = a.ks;
+    p.partial = a.partial;
+    p.tcount = a.tcount;
     p.y = a.y;
     p.y_dtype = a.y_dtype;
     p.bias = a.bias;
     p.partial_out = a.partial_out;
     p.status = L.status;
+    const int64_t chunks = L.KB * a.Mpp * 8;
+    const int64_t gblocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(L.sms) * 16);
+    cudaError_t e = launch_pdl(k_gather_tokens, dim3(static_cast<unsigned>(gblocks)), dim3(256), 0, s,
+                               a.xk, a.xkp, a.perm, a.nrouted, a.route_all, a.M, a.Mp, a.Mpp, L.KB);
+    if (e != cudaSuccess) return e;
     static std::atomic<uint64_t> flags{0};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (!(flags.load() & bit)) {
-        cudaError_t e = cudaFuncSetAttribute(k_ctarq_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg::kTotal);
+        e = cudaFuncSetAttribute(k_ctarq_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg::kTotal);
         if (e != cudaSuccess) return e;
         flags.fetch_or(bit);
     }
-    return launch_pdl(k_ctarq_gemm, dim3(static_cast<unsigned>(p.RT * p.T)), dim3(GemmCfg::kThreads), GemmCfg::kTotal,
-                      s, p);
+    return launch_pdl(k_ctarq_gemm, dim3(static_cast<unsigned>(p.RT * p.T * p.ks)), dim3(GemmCfg::kThreads),
+                      GemmCfg::kTotal, s, p);
+}
+
+// Fold lists from the host CSR (columns ascending per row) and the f32 row scales: for every
+// (row tile, block), a header of u16 entry offsets [16-row tile][lane 0..32] (kFoldHdr bytes;
+// entry o[t][l] .. o[t][l+1] belong to lane l of tile t), then one u32 per entry, grouped by
+// (tile, lane): bits 0-4 the lane (4 g + c) holding the weight in the dequantised fragment, 5-8
+// the register slot (step * 4 + register), 9 the half, 16-31 the f16 of dW/s.  Left empty (no
+// fold: the GEMM adds dW in its epilogue) when a list exceeds its shared-memory slot or a value
+// is not representable.
+cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol, const int8_t* sval,
+                             const float* scale) {
+    L.fold = nullptr;
+    L.foldoff = nullptr;
+    if (L.nnz == 0) return cudaSuccess;
+    const int64_t RT = L.Np / 128, KB = L.KB;
+    std::vector<uint32_t> off(RT * KB + 1, 0);
+    std::vector<uint8_t> blob;
+    std::vector<std::vector<uint32_t>> per(KB * 8 * 32);  // [kb][tile16][lane] entries of one row tile
+    for (int64_t rt = 0; rt < RT; ++rt) {
+        for (auto& v : per) v.clear();
+        for (int r = 0; r < 128; ++r) {
+            const int64_t row = rt * 128 + r;
+            if (row >= L.N) break;
+            for (uint32_t q = srp[row]; q < srp[row + 1]; ++q) {
+                const double dw = static_cast<double>(static_cast<float>(sval[q]) * L.ds);
+                if (dw == 0.0) continue;
+                const double sc = static_cast<double>(scale[row]);
+                if (!(sc > 0.0)) return cudaSuccess;
+                const __half hv = __float2half_rn(static_cast<float>(dw / sc));
+                if (!std::isfinite(__half2float(hv))) return cudaSuccess;
+                const int cl = scol[q] % 64, kb = scol[q] / 64;
+                const int rl = r % 16, g = rl & 7, upper = rl >> 3;
+                const int stp = cl >> 4, cc = cl & 15, c = cc >> 2, k = cc & 3;
+                const uint32_t lane = static_cast<uint32_t>(g * 4 + c);
+                const uint32_t slot = static_cast<uint32_t>(stp * 4 + upper + (k >= 2 ? 2 : 0));
+                const uint32_t half = static_cast<uint32_t>(k & 1);
+                per[(kb * 8 + r / 16) * 32 + lane].push_back(lane | (slot << 5) | (half << 9) |
+                                                             (static_cast<uint32_t>(__half_as_ushort(hv)) << 16));
+            }
+        }
+        for (int64_t kb = 0; kb < KB; ++kb) {
+            size_t n = 0;
+            for (int t = 0; t < 8 * 32; ++t) n += per[kb * 256 + t].size();
+            const size_t bytes = ((kFoldHdr + 4 * n) + 15) / 16 * 16;
+            if (bytes > static_cast<size_t>(kFoldCap)) return cudaSuccess;
+            const size_t at = blob.size();
+            blob.resize(at + bytes, 0);
+            uint16_t hdr[kFoldHdr / 2] = {};
+            uint32_t acc = 0;
+            for (int t = 0; t < 8; ++t) {
+                for (int l = 0; l < 32; ++l) {
+                    const auto& v = per[kb * 256 + t * 32 + l];
+                    hdr[t * 33 + l] = static_cast<uint16_t>(acc);
+                    std::memcpy(&blob[at + kFoldHdr + 4 * acc], v.data(), 4 * v.size());
+                    acc += static_cast<uint32_t>(v.size());
+                }
+                hdr[t * 33 + 32] = static_cast<uint16_t>(acc);
+            }
+            std::memcpy(&blob[at], hdr, sizeof(hdr));
+            off[rt * KB + kb + 1] = static_cast<uint32_t>(blob.size());
+        }
+    }
+    uint8_t* dblob = nullptr;
+    uint32_t* doff = nullptr;
+    cudaError_t e = cudaMalloc(&dblob, blob.size());
+    if (e == cudaSuccess) e = cudaMalloc(&doff, off.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(dblob, blob.data(), blob.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(doff, off.data(), off.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dblob);
+        cudaFree(doff);
+        return e;
+    }
+    L.fold = dblob;
+    L.foldoff = doff;
+    L.device_bytes += static_cast<int64_t>(blob.size() + off.size() * 4);
+    return cudaSuccess;
 }
 
 }  // namespace sc

@@ -48,6 +48,10 @@ struct Layer {
     int ks_fused = 0;            // column splits (= cluster size) of the fused kernel; 0: not usable
     uint8_t* dwblk = nullptr;
     uint32_t* dwoff = nullptr;   // byte offset of block (rt * ks_fused + split); [RT*ks_fused + 1]
+    // dW over the row scale, per (128-row tile, 64-column block), for the prefill GEMM: routed
+    // tokens' tiles fold it into the dequantised weights ((q - 8) + dW/s, see sc_gemm.cu).
+    uint8_t* fold = nullptr;     // lists, each [9 u16 offsets per 16-row tile | pad to 32 B | u32 entries]
+    uint32_t* foldoff = nullptr; // byte offset of list (rt * KB + kb); [RT*KB + 1]; null: no fold
 };
 
 // Shared-memory budget of one dW block in the fused decode kernel.
@@ -74,6 +78,8 @@ struct WsLayout {
     int64_t Mp = 0;              // tokens padded to 8
     size_t xk = 0, mask = 0, scores = 0, ridx = 0, nrouted = 0, counter = 0;
     size_t partial = 0, rtcount = 0;
+    size_t xkp = 0, perm = 0;    // prefill GEMM: x in routed-first order and that order
+    int gemm_ks = 0;             // prefill GEMM column splits (0: the GEMM does not serve the call)
     size_t total = 0;
     int ksplit = 1;
     int chunk_tokens = 0;        // tokens per decode launch
@@ -121,6 +127,7 @@ struct RouterArgs {
     float* scores;
     int32_t* ridx;
     int32_t* nrouted;
+    int32_t* perm;          // nullable: routed-first token order for the GEMM
     uint32_t* counter;
     uint32_t* status;
 };
@@ -146,13 +153,20 @@ struct DecodeArgs {
 };
 cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s);
 
-// Many tokens (prefill): tcgen05 GEMM over 128-token tiles of the router's staged x.
+// Many tokens (prefill): tcgen05 GEMM over 128-token tiles of the router's staged x, taken in
+// routed-first order (perm) so that routed tokens share tiles.
 struct GemmArgs {
     const Layer* L;
-    const uint16_t* xk;     // staged x (xk_index layout), Mp token rows
-    int64_t Mp, M;
-    const uint8_t* mask;
+    const uint16_t* xk;     // staged x (xk_index layout) in token order, Mp token rows
+    uint16_t* xkp;          // the same in perm order (written by launch_gemm's gather)
+    const int32_t* perm;    // staged position -> token: routed at [0, R), the others from round_up(R, 8)
+    const int32_t* nrouted; // routed tokens R (device)
+    int64_t Mp, M;          // xk token rows, tokens
+    int64_t Mpp;            // xkp / perm positions (Mp + 16)
     int route_all;
+    int ks;                 // column splits (>= 1)
+    float* partial;         // split partials [tiles][ks][128 tokens][128 rows] (ks > 1)
+    uint32_t* tcount;       // per-tile split counters (ks > 1), zero between calls
     void* y;                // [M, N]; f32 partial when partial_out
     int y_dtype;
     const float* bias;
@@ -160,6 +174,9 @@ struct GemmArgs {
 };
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 int64_t gemm_tile_tokens();
+int gemm_ksplit(const Layer& L, int64_t m);  // column splits of the prefill GEMM for m tokens
+cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol, const int8_t* sval,
+                             const float* scale);
 #ifndef SC_GEMM_MIN_TOKENS
 #define SC_GEMM_MIN_TOKENS 9  // calls of at least this many tokens (not decoded fused) run the GEMM
 #endif

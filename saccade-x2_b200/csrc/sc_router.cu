@@ -40,6 +40,7 @@ struct RouterKernelArgs {
     float* scores;
     int32_t* ridx;
     int32_t* nrouted;
+    int32_t* perm;          // nullable: staged order, routed tokens (ascending) then the others
     uint32_t* counter;
     uint32_t* status;
 };
@@ -160,6 +161,28 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
         base += tot;
         __syncthreads();
     }
+    if (a.perm) {
+        // the GEMM's token order: perm[0, R) = the routed tokens, then from round_up(R, 8) (a
+        // whole 8-token group) the others
+        for (int64_t i = tid; i < base; i += kThreads) a.perm[i] = a.ridx[i];
+        int ub = (base + 7) & ~7;
+        for (int64_t t0 = 0; t0 < a.M; t0 += kThreads) {
+            const int64_t tt = t0 + tid;
+            const int v = (tt < a.M) ? (reinterpret_cast<volatile uint8_t*>(a.mask)[tt] == 0) : 0;
+            const unsigned bal = __ballot_sync(0xffffffffu, v);
+            if (lane == 0) s_wsum[warp] = __popc(bal);
+            __syncthreads();
+            int pre = 0, tot = 0;
+            for (int w = 0; w < kWarps; ++w) {
+                if (w < warp) pre += s_wsum[w];
+                tot += s_wsum[w];
+            }
+            pre += __popc(bal & ((1u << lane) - 1u));
+            if (v) a.perm[ub + pre] = static_cast<int32_t>(tt);
+            ub += tot;
+            __syncthreads();
+        }
+    }
     if (tid == 0) {
         *a.nrouted = base;
         *a.counter = 0u;
@@ -186,6 +209,7 @@ cudaError_t launch_router(const RouterArgs& r, cudaStream_t s) {
     a.scores = r.scores;
     a.ridx = r.ridx;
     a.nrouted = r.nrouted;
+    a.perm = r.perm;
     a.counter = r.counter;
     a.status = r.status;
     return launch_pdl(k_router<256>, dim3(static_cast<unsigned>(r.Mp)), dim3(256), 0, s, a);

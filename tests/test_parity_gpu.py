@@ -249,6 +249,32 @@ def test_qwen2_7b_shapes(sc, n, k, m, mode):
 
 # ------------------------------------------------------------------ tensor-parallel slices
 
+# ------------------------------------------------------------------ prefill GEMM (9+ tokens)
+
+@pytest.mark.parametrize("n,k,m,nroute,fill", [
+    (300, 3584, 300, 300, 0.02),   # every tile routed (dW folded into the weights), column splits
+    (300, 3584, 300, 200, 0.02),   # a folded tile, a mixed tile (dW in the epilogue), an unrouted tile
+    (4864, 896, 257, 100, 0.01),   # many row tiles, no column split, ragged last tile
+    (1000, 520, 40, 40, 0.04),     # one tile, all routed, K not a multiple of 64
+    (130, 200, 9, 0, 0.02),        # the smallest GEMM call, nothing routed
+    (96, 128, 20, 20, 1.0),        # dense dW: lists too long to fold, dW in the epilogue
+])
+def test_prefill_gemm_routing(sc, n, k, m, nroute, fill):
+    rng = np.random.default_rng(n + m + nroute)
+    boost = sorted(rng.choice(m, size=nroute, replace=False).tolist()) if nroute else []
+    case = make_case(n, k, m, fill, seed=n + k + m, boost=boost, thresholds=(8.0, 3e38))
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    assert int(rr.sum()) == nroute
+    for mode in FAST_MODES:
+        op = to_op(sc, case, mode=mode)
+        y, mask, ridx = run_gpu(op, case.x_bits)
+        assert np.array_equal(mask, rr)
+        assert np.array_equal(ridx, np.nonzero(rr)[0])
+        assert_fast_close(y_bits(y), yr, f"gemm {n}x{k} m={m} routed={nroute} {mode}")
+        acc = op.forward_partial(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0")).cpu().numpy()
+        assert_acc_close(acc, acc_ref, f"gemm {n}x{k} m={m} routed={nroute} {mode} acc")
+
+
 @pytest.mark.parametrize("count", [2, 3])
 def test_column_shards_concatenate(sc, count):
     case = make_case(520, 256, 6, 0.02, seed=31)
