@@ -64,10 +64,10 @@ def parse():
 
 def launches_per_call(args):
     """Kernels one forward call launches: the router-fused decode kernel for <= 8 tokens in the
-    fast modes; the router kernel plus one decode launch per 32-token chunk otherwise."""
+    fast modes; otherwise the router, then the exact kernel or the token gather and the GEMM."""
     if args.mode != "exact" and args.tokens <= 8:
         return 1
-    return 1 + (1 if args.mode == "exact" else -(-args.tokens // 32))
+    return 2 if args.mode == "exact" else 3
 
 
 def launches_per_step(args, units):
@@ -82,7 +82,7 @@ def launch_kind(args):
                 if args.tokens == 1 else "k_ctarq_fused_mma (router-fused decode, f16 mma.sync)")
         return {"fast_tc": "k_ctarq_fused_tc<f16> (router-fused decode, tcgen05)",
                 "fast_tc8": "k_ctarq_fused_tc<fp8> (router-fused decode, tcgen05 e4m3)"}.get(args.mode, fast)
-    return "k_decode_exact (+ k_router)" if args.mode == "exact" else "k_ctarq_tc / k_ctarq_mma (+ k_router)"
+    return "k_decode_exact (+ k_router)" if args.mode == "exact" else "k_ctarq_gemm (+ k_router, k_gather_tokens)"
 
 
 def call_bytes(n, k, m, nnz, routed):

@@ -1,25 +1,23 @@
-// sc_decode.cu -- C-TARQ kernels for a few tokens per call (decode).
+// sc_decode.cu -- C-TARQ kernels for a few tokens per call (decode, M <= 8) and the exact mode.
 //
-// Both fast kernels stream the 4-bit base through a shared-memory ring filled by one
-// producer lane with non-multicast bulk copies (cp.async.bulk + mbarrier complete_tx, L2
-// evict-first on weights).  A CTA owns one 128-row tile and a contiguous range of 64-column
-// blocks (split-K across CTAs when a layer has few rows).  Under programmatic dependent
-// launch the producer requests its first weight stages before griddepcontrol.wait, so they
-// overlap the previous kernel's tail; activations are read only after the wait.
+// The fast kernels stream the 4-bit base through a shared-memory ring filled by one producer
+// lane with non-multicast bulk copies (cp.async.bulk + mbarrier complete_tx, L2 evict-first on
+// weights).  A CTA owns one 128-row tile and a contiguous range of 64-column blocks (split-K
+// across CTAs when a layer has few rows).  Under programmatic dependent launch the producer
+// requests its first weight stages before griddepcontrol.wait, so they overlap the previous
+// kernel's tail; activations are read only after the wait.
 //
-//   k_ctarq_mma  (<= 8 tokens): eight MMA warps, one 16-row tile each.  Per 64 columns a lane
-//                reads 16 bytes of packed nibbles, converts each word into an mma.m16n8k16 A
-//                fragment of exact integers q-8 in registers (dequant_word) and multiplies it
-//                with the activations, f32 accumulation.  At decode sizes the kernel is
-//                bound by HBM and by this conversion, not by the tensor pipe.
-//   k_ctarq_tc   (9..32 tokens): the same words are stored to TMEM with tcgen05.st.16x256b and
-//                one thread issues tcgen05.mma.kind::f16 (A from TMEM, activations from shared
-//                memory as K-major core matrices, f32 accumulators in TMEM): the 5th-gen tensor
-//                core covers 16-32 tokens per instruction where mma.sync would need 2-4.
-//   dW warps (both kernels): one output row per lane; they walk the row's CSR dW entries in
-//                the CTA's column range for the routed tokens (op.rs:152-170) meanwhile.
-// Epilogue: y = f16(acc * s + dW) (+ bias after the rounding); with split-K the last CTA of a
-// row tile sums the partials in split order (deterministic).
+//   k_ctarq_fused_mma / k_ctarq_fused_tc (below): the router folded in, one launch per call or
+//                group of calls; the production decode path.
+//   k_ctarq_mma  (<= 8 tokens, a layer too wide for the fused kernel's x copy, after k_router):
+//                eight MMA warps, one 16-row tile each.  Per 64 columns a lane reads 16 bytes of
+//                packed nibbles, converts each word into an mma.m16n8k16 A fragment of exact
+//                integers q-8 in registers (dequant_word) and multiplies it with the activations,
+//                f32 accumulation.  dW warps: one output row per lane; they walk the row's CSR dW
+//                entries in the CTA's column range for the routed tokens (op.rs:152-170).
+//                Epilogue: y = f16(acc * s + dW) (+ bias after the rounding); with split-K the
+//                last CTA of a row tile sums the partials in split order (deterministic).
+// More tokens go to the prefill GEMM (sc_gemm.cu).
 //
 // k_decode_exact: SC_MODE_EXACT.  One thread per row pair replays op.rs exactly: four f32
 // accumulators fed in the reference's order with single-rounding f16 x f16 -> f32 FMAs
@@ -308,185 +306,6 @@ __global__ void __launch_bounds__(MmaCfg::kThreads, 1) k_ctarq_mma(TCParams p) {
     }
     pdl_wait();
     epilogue_tile<C::NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
-}
-
-// ---------------------------------------------------------------- k_ctarq_tc (9..32 tokens)
-
-template <int NT>
-struct TcCfg {
-    static constexpr int kDqWarps = 8;               // two per TMEM sub-partition, one 16-row tile each
-    static constexpr int kProducerWarp = 8;
-    static constexpr int kMmaWarp = 9;
-    static constexpr int kDeltaWarp0 = 10;
-    static constexpr int kThreads = 14 * 32;
-    static constexpr int G = NT / 8;
-    static constexpr int SKB = 4;
-    static constexpr int kWBytes = SKB * 4096;
-    static constexpr int kXBytes = SKB * G * 1024;
-    static constexpr int kStageBytes = kWBytes + kXBytes;
-    static constexpr int S = NT == 16 ? 7 : 5;
-    static constexpr int kAB = 4;                    // TMEM A buffers, one 64-column block (32 cols) each
-    static constexpr int kLd = NT + 1;
-    static constexpr int kAccOff = S * kStageBytes;
-    static constexpr int kCorrOff = kAccOff + 128 * kLd * 4;
-    static constexpr int kBarOff = kCorrOff + 128 * kLd * 4;
-    static constexpr int kNumBars = 2 * S + 2 * kAB + 1;
-    static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
-    static constexpr int kTotal = kTmemSlotOff + 16;
-    static constexpr uint32_t kTmemCols = 256;       // D in [0, 32), A buffers in [32, 160)
-    static_assert(NT == 16 || NT == 32, "token tile");
-    static_assert(kTotal <= 227 * 1024, "shared memory");
-};
-
-template <int NT>
-__global__ void __launch_bounds__(TcCfg<NT>::kThreads, 1) k_ctarq_tc(TCParams p) {
-    using C = TcCfg<NT>;
-    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB;
-    extern __shared__ __align__(1024) unsigned char smem[];
-    float* accbuf = reinterpret_cast<float*>(smem + C::kAccOff);
-    float* corrbuf = reinterpret_cast<float*>(smem + C::kCorrOff);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-    uint64_t* empty = full + S;
-    uint64_t* a_full = empty + S;
-    uint64_t* a_empty = a_full + AB;
-    uint64_t* done = a_empty + AB;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
-    __shared__ int s_last;
-    __shared__ int s_abort;
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t rt = blockIdx.x / p.ksplit;
-    const int split = static_cast<int>(blockIdx.x - rt * p.ksplit);
-    const int64_t kb_begin = (p.KB * split) / p.ksplit;
-    const int64_t kb_end = (p.KB * (split + 1)) / p.ksplit;
-    const int nkb = static_cast<int>(kb_end - kb_begin);
-    const int greal = (p.ntok + 7) >> 3;
-
-    pdl_launch_dependents();
-    // Padding token groups of the N tile must read as zero: clear the activation part of every
-    // stage once (bulk copies only write the real groups), plus the accumulator and dW tiles.
-    for (int i = tid; i < S * (C::kXBytes / 16); i += C::kThreads) {
-        const int st = i / (C::kXBytes / 16), off = i - st * (C::kXBytes / 16);
-        reinterpret_cast<uint4*>(smem + st * C::kStageBytes + C::kWBytes)[off] = make_uint4(0, 0, 0, 0);
-    }
-    for (int i = tid; i < 2 * 128 * C::kLd; i += C::kThreads) accbuf[i] = 0.0f;
-    fence_proxy_async_smem();
-    if (tid == 0) {
-        for (int i = 0; i < S; ++i) {
-            mbar_init(&full[i], 2);
-            mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < AB; ++i) {
-            mbar_init(&a_full[i], C::kDqWarps);
-            mbar_init(&a_empty[i], 1);
-        }
-        mbar_init(done, 1);
-        fence_mbar_init();
-        s_abort = 0;
-    }
-    if (warp == C::kMmaWarp) {
-        tmem_alloc(tmem_slot, C::kTmemCols);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    int issued = 0;
-    if (warp == C::kProducerWarp) {
-        if (lane == 0)
-            issued = producer_run<SKB, S, C::G, C::kWBytes, C::kStageBytes>(p, smem, full, empty, rt, kb_begin, kb_end,
-                                                                           greal, &s_abort);
-    } else if (warp == C::kMmaWarp) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(128, NT);
-            for (int j = 0; j < nkb; ++j) {
-                const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
-                if (kbl == 0 && !mbar_wait(&full[slot], (s / S) & 1, p.status)) {
-                    s_abort = 1;
-                    break;
-                }
-                if (!mbar_wait(&a_full[b], (j / AB) & 1, p.status)) {
-                    s_abort = 1;
-                    break;
-                }
-                tc_fence_after();
-                const unsigned char* xs = smem + slot * C::kStageBytes + C::kWBytes + kbl * C::G * 1024;
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    tc_mma_ts(tmem, tmem + 32 + b * 32 + i * 8, desc_kmajor(xs + 2 * i * 128, 128, 1024), idesc,
-                              (j | i) ? 1u : 0u);
-                tc_commit(&a_empty[b]);
-                if (kbl == SKB - 1 || j == nkb - 1) tc_commit(&empty[slot]);
-            }
-            tc_commit(done);  // also after an abort, so that the TMEM can be released
-        }
-    } else if (warp < C::kDqWarps) {
-        const int sp = warp & 3, q = warp >> 2;
-        const int tile = 2 * sp + q;
-        const uint32_t lane_addr = static_cast<uint32_t>(32 * sp + 16 * q) << 16;
-        for (int j = 0; j < nkb; ++j) {
-            const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
-            bool ok = true;
-            if (kbl == 0 && !mbar_wait(&full[slot], (s / S) & 1, p.status)) ok = false;
-            if (ok && j >= AB && !mbar_wait(&a_empty[b], ((j / AB) - 1) & 1, p.status)) ok = false;
-            if (!ok) {
-                s_abort = 1;
-                break;
-            }
-            tc_fence_after();
-            const uint4 wv =
-                *reinterpret_cast<const uint4*>(smem + slot * C::kStageBytes + kbl * 4096 + tile * 512 + lane * 16);
-            const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-            for (int st = 0; st < 4; ++st) {
-                uint32_t h[4];
-                dequant_word(words[st], h);
-                tc_st_16x256b(tmem + lane_addr + 32 + b * 32 + st * 8, h[0], h[2], h[1], h[3]);
-            }
-            tc_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[b]);
-        }
-        // accumulators -> shared tile: warp q of sub-partition sp reads token columns q*8.., q*8+16..
-        if (mbar_wait(done, 0, p.status)) {
-            tc_fence_after();
-            const uint32_t lane_rows = static_cast<uint32_t>(32 * sp) << 16;
-            const int rl = 32 * sp + lane;
-#pragma unroll
-            for (int cb = q; cb < NT / 8; cb += 2) {
-                uint32_t d[8];
-                tc_ld8(tmem + lane_rows + cb * 8, d);
-                tc_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 8; ++i) accbuf[rl * C::kLd + cb * 8 + i] = __uint_as_float(d[i]);
-            }
-        } else {
-            s_abort = 1;
-        }
-        tc_fence_before();
-    } else {
-        pdl_wait();
-        delta_rows<NT, C::kLd>(p, corrbuf, (warp - C::kDeltaWarp0) * 32 + lane, rt, kb_begin, kb_end);
-    }
-    __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
-    __syncthreads();
-    if (warp == C::kMmaWarp) {
-        // every tcgen05 operation of this CTA has completed (done observed, loads waited)
-        if (s_abort) mbar_wait(done, 0, nullptr, kDrainNs);
-        tc_fence_after();
-        tmem_dealloc(tmem, C::kTmemCols);
-    }
-    if (s_abort) {
-        if (warp == C::kProducerWarp && lane == 0)
-            for (int it = issued > S ? issued - S : 0; it < issued; ++it)
-                mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
-        return;
-    }
-    pdl_wait();
-    epilogue_tile<NT, C::kLd, C::kThreads>(p, accbuf, corrbuf, rt, split, &s_last);
 }
 
 // ---------------------------------------------------------------- router-fused decode (<= 8 tokens)
@@ -1541,18 +1360,6 @@ cudaError_t launch_decode_tc(const DecodeArgs& a, cudaStream_t s) {
         cudaError_t e = set_smem_once(k_ctarq_mma, MmaCfg::kTotal, f);
         if (e != cudaSuccess) return e;
         return launch_pdl(k_ctarq_mma, grid, dim3(MmaCfg::kThreads), MmaCfg::kTotal, s, p);
-    }
-    if (a.ntok <= 16) {
-        static std::atomic<uint64_t> f{0};
-        cudaError_t e = set_smem_once(k_ctarq_tc<16>, TcCfg<16>::kTotal, f);
-        if (e != cudaSuccess) return e;
-        return launch_pdl(k_ctarq_tc<16>, grid, dim3(TcCfg<16>::kThreads), TcCfg<16>::kTotal, s, p);
-    }
-    if (a.ntok <= 32) {
-        static std::atomic<uint64_t> f{0};
-        cudaError_t e = set_smem_once(k_ctarq_tc<32>, TcCfg<32>::kTotal, f);
-        if (e != cudaSuccess) return e;
-        return launch_pdl(k_ctarq_tc<32>, grid, dim3(TcCfg<32>::kThreads), TcCfg<32>::kTotal, s, p);
     }
     return cudaErrorInvalidValue;
 }

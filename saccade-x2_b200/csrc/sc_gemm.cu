@@ -295,22 +295,16 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         const bool fold = g.fold;
         const int64_t Mx = g.identity ? p.Mp : p.Mpp;  // token rows of the x copy read
         const uint16_t* xsrc = g.identity ? p.xk : p.xkp;
-        for (int j = set; j < nkb && ntile > 0; j += 2) {
-            const int s = j / SKB, kbl = j - s * SKB, slot = s % S, b = j % AB;
-            bool ok = true;
-            if (!mbar_wait(&full[slot], (s / S) & 1, p.status)) ok = false;  // each set waits for its own blocks
-            if (ok && j >= AB && !mbar_wait(&a_empty[b], ((j / AB) - 1) & 1, p.status)) ok = false;
-            if (!ok) {
-                s_abort = 1;
-                break;
-            }
-            tc_fence_after();
+        // Software-pipelined: the next block of this set is read and dequantised while the
+        // current block's tensor-memory stores drain.
+        auto load_block = [&](int jj, uint32_t (&hh)[4][4]) -> bool {
+            const int s = jj / SKB, kbl = jj - s * SKB, slot = s % S;
+            if (!mbar_wait(&full[slot], (s / S) & 1, p.status)) return false;
             const unsigned char* stg = smem + slot * C::kStageBytes;
             const uint4 wv = *reinterpret_cast<const uint4*>(stg + kbl * 4096 + tile * 512 + lane * 16);
             const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-            uint32_t h[4][4];
 #pragma unroll
-            for (int st = 0; st < 4; ++st) dequant_word(words[st], h[st]);
+            for (int st = 0; st < 4; ++st) dequant_word(words[st], hh[st]);
             if (fold) {
                 // this lane's entries of the block (register slot, half, f16 dW/s)
                 const unsigned char* lst = stg + C::kWBytes + C::kXBytes + kbl * kFoldCap;
@@ -319,17 +313,46 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
                 const int e1 = offs[1];
                 for (int e = offs[0]; e < e1; ++e) {
                     const uint32_t w = ent[e];
-                    fold_add(h, static_cast<int>((w >> 5) & 15u), static_cast<int>((w >> 9) & 1u),
+                    fold_add(hh, static_cast<int>((w >> 5) & 15u), static_cast<int>((w >> 9) & 1u),
                              static_cast<uint16_t>(w >> 16));
                 }
             }
+            return true;
+        };
+        uint32_t h[4][4];
+        int j = set;
+        bool have = ntile > 0 && j < nkb;
+        if (have && !load_block(j, h)) {
+            s_abort = 1;
+            have = false;
+        }
+        while (have) {
+            const int b = j % AB;
+            if (j >= AB && !mbar_wait(&a_empty[b], ((j / AB) - 1) & 1, p.status)) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
 #pragma unroll
             for (int st = 0; st < 4; ++st)
                 tc_st_16x256b(tmem + lane_addr + NT + b * 32 + st * 8, h[st][0], h[st][2], h[st][1], h[st][3]);
+            const int jn = j + 2;
+            uint32_t hn[4][4];
+            bool next = jn < nkb;
+            if (next && !load_block(jn, hn)) {
+                s_abort = 1;
+                next = false;
+            }
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[b]);
+            if (!next) break;
+#pragma unroll
+            for (int st = 0; st < 4; ++st)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) h[st][r] = hn[st][r];
+            j = jn;
         }
         // epilogue: warp qq = warp / 4 of sub-partition sq owns rows 32 sq + lane and tokens [32 qq, 32 qq + 32)
         if (ntile > 0 && mbar_wait(done, 0, p.status) && !s_abort) {
