@@ -11,6 +11,7 @@ Effective bytes per call (the metric's numerator, independent of the device layo
 value = bytes of all calls of all ranks / max-over-ranks device time (CUDA events).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M] [--impl reference]
+  python bench.py --sweep OUT.md      # single calls: 4 shapes x M 1..4096 x routed 0/25/100 %
 
 --impl reference times the reference's CPU algorithm (the oracle restatement of
 saccade-core's op.rs; the Rust reference cannot be built here) on the host cores.

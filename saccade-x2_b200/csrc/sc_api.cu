@@ -181,7 +181,7 @@ WsLayout plan_workspace(const Layer& L, int64_t m) {
         w.xkp = take(static_cast<size_t>(L.KB * 64 * (w.Mp + 16) * 2));
         w.perm = take(static_cast<size_t>(4 * (w.Mp + 16)));
         const int64_t tiles = RT * ((m + gemm_tile_tokens() - 1) / gemm_tile_tokens() + 1);
-        w.partial = take(static_cast<size_t>(w.gemm_ks > 1 ? tiles * w.gemm_ks * gemm_tile_tokens() * 128 * 4 : 16));
+        w.partial = take(static_cast<size_t>(w.gemm_ks > 1 ? tiles * w.gemm_ks * gemm_tile_tokens() * 256 * 4 : 16));
     } else {
         w.ksplit = static_cast<int>(ks);
         w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));

@@ -1,7 +1,7 @@
 // sc_gemm.cu -- C-TARQ linear for many tokens (prefill): a tcgen05 GEMM over 128-token tiles.
 //
-// One CTA computes a 128-row x 128-token tile of Y over a range of K (op.rs:99-178 for those
-// rows and tokens).  The router (sc_router.cu) has decided every token, staged x as K-major
+// One CTA computes one or two 128-row x 128-token tiles of Y (two share every x block, when the
+// grid of pairs still fills the GPU) over a range of K (op.rs:99-178 for those rows and tokens).  The router (sc_router.cu) has decided every token, staged x as K-major
 // core matrices (xk_index) and listed the tokens routed first (perm); k_gather_tokens copies
 // the staged x into that order, so the routed tokens fill whole tiles.  For one 64-column
 // block the 8-token groups of a tile are 1 KB each and contiguous, so a tile's activations
@@ -9,15 +9,17 @@
 // between 8-column chunks, SBO 1 KB between token groups).
 //
 // Roles (18 warps, one CTA per SM):
-//   producer lane   weights (4 KB per block, contiguous per row tile), the tile's x blocks and,
-//                   for a tile of routed tokens, the blocks' dW lists, through a ring of S
-//                   stages; the first stages' weights are requested before the dependency wait;
-//   16 dequantising warps, one 16-row tile each, in two sets taking alternate blocks (two
-//                   independent store pipelines): W4U words -> f16 (q - 8) with dequant_word; in a
+//   producer lane   weights (4 KB per block and row tile, contiguous per row tile), the tile's x
+//                   blocks and, for a tile of routed tokens, the blocks' dW lists, through a ring
+//                   of S stages; the first stages' weights are requested before the dependency wait;
+//   16 dequantising warps, one 16-row tile each, in two sets of 8: one set per row tile, or with
+//                   one row tile alternate blocks (the next block is read while the current one's
+//                   stores drain): W4U words -> f16 (q - 8) with dequant_word; in a
 //                   tile of routed tokens the row's dW is folded in as (q - 8) + dW/s (s the row
 //                   scale), one f16 per weight; then into tensor memory with tcgen05.st.16x256b;
 //   MMA warp        one elected lane issues tcgen05.mma.kind::f16 M=128 N=128 K=16 (A from tensor
-//                   memory, B from shared memory, f32 D in tensor memory), 4 per block;
+//                   memory, B from shared memory, f32 D in tensor memory), 4 per block and row tile,
+//                   both row tiles on the same B (x) block: half the x traffic per MMA;
 //   epilogue        the dequantising warps read D (tcgen05.ld, 32 rows x 8 tokens) and write
 //                   y = f16(acc * s [+ dW]) (+ bias after rounding) for the tile's tokens.  A tile
 //                   holding both routed and other tokens (at most one per row tile), or a layer
@@ -62,6 +64,8 @@ struct GemmParams {
     int64_t Mp, M, Mpp;     // xk token rows, tokens, xkp positions
     int route_all;
     int64_t N, KB, RT, T;   // rows, column blocks, row tiles, token tiles (one more than ceil(M/128))
+    int rpc;                // row tiles per CTA: 2 when the grid still fills the GPU, else 1
+    int64_t RTP;            // CTAs per token tile and split: ceil(RT / rpc)
     int ks;
     float* partial;
     uint32_t* tcount;
@@ -72,26 +76,33 @@ struct GemmParams {
     uint32_t* status;
 };
 
+// RPC: 128-row tiles per CTA (1, or 2 sharing every x block); the ring, the tensor memory and
+// every index are compile-time for each.
+template <int RPC>
 struct GemmCfg {
     static constexpr int NT = 128;                   // tokens per tile (MMA N)
-    static constexpr int kDqWarps = 16;              // 2 sets (even / odd blocks) x 8 tiles of 16 rows
+    static constexpr int kRowTiles = RPC;
+    static constexpr int kDqWarps = 16;              // two sets of 8 (16-row tiles): per row tile, or alternate blocks
     static constexpr int kProducerWarp = 16;
     static constexpr int kMmaWarp = 17;
     static constexpr int kThreads = 18 * 32;
     static constexpr int G = NT / 8;                 // 8-token groups of a tile
     static constexpr int SKB = 2;                    // 64-column blocks per ring stage
-    static constexpr int S = 4;
-    static constexpr int kWBytes = SKB * 4096;
+    static constexpr int S = RPC == 1 ? 4 : 3;       // ring stages
+    // A stage holds [row tile][block] 4 KB weights, the blocks' x (16 KB each), then [row tile]
+    // [block] dW lists: 44 KB with one row tile, 56 KB with two.
+    static constexpr int kWBytes = RPC * SKB * 4096;
     static constexpr int kXBytes = SKB * G * 1024;
-    static constexpr int kFBytes = SKB * kFoldCap;
+    static constexpr int kFBytes = RPC * SKB * kFoldCap;
     static constexpr int kStageBytes = kWBytes + kXBytes + kFBytes;
-    static constexpr int kAB = 4;                    // TMEM A buffers, one block (32 columns) each
-    static constexpr uint32_t kTmemCols = 256;       // D in [0, 128), A buffers in [128, 256)
+    static constexpr int kAB = 4;                    // TMEM A buffers per row tile, one block (32 columns) each
+    static constexpr uint32_t kTmemCols = RPC == 1 ? 256 : 512;  // D of row tile t at t*128, A after the D's
     static constexpr int kBarOff = S * kStageBytes;
     static constexpr int kNumBars = 2 * S + 2 * kAB + 1;
     static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
     static constexpr int kTotal = kTmemSlotOff + 16;
-    static_assert(NT + kAB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
+    static_assert(RPC == 1 || RPC == 2, "row tiles per CTA");
+    static_assert(RPC * NT + RPC * kAB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
     static_assert(kTotal <= 227 * 1024, "shared memory");
 };
 
@@ -126,7 +137,7 @@ struct GemmTile {
     bool routed, fold, identity;
 };
 __device__ __forceinline__ GemmTile gemm_tile(const GemmParams& p, int64_t tt) {
-    constexpr int NT = GemmCfg::NT;
+    constexpr int NT = GemmCfg<1>::NT;
     GemmTile g;
     g.R = p.route_all ? p.M : static_cast<int64_t>(*p.nrouted);
     const int64_t TR = (g.R + NT - 1) / NT, RB = (g.R + 7) & ~static_cast<int64_t>(7);
@@ -144,13 +155,14 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmParams& p, int64_t tt) {
     return g;
 }
 
-__global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams p) {
-    using C = GemmCfg;
-    constexpr int SKB = C::SKB, S = C::S, AB = C::kAB, NT = C::NT, G = C::G;
+template <int RPC>
+__global__ void __launch_bounds__(GemmCfg<RPC>::kThreads, 1) k_ctarq_gemm(GemmParams p) {
+    using C = GemmCfg<RPC>;
+    constexpr int SKB = C::SKB, AB = C::kAB, NT = C::NT, G = C::G, S = C::S;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-    uint64_t* empty = full + S;
-    uint64_t* a_full = empty + S;
+    uint64_t* empty = full + C::S;
+    uint64_t* a_full = empty + C::S;
     uint64_t* a_empty = a_full + AB;
     uint64_t* done = a_empty + AB;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kTmemSlotOff);
@@ -163,8 +175,12 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
     // both leave a partial tile) comes last in the grid
     const int64_t tile_id = blockIdx.x / p.ks;
     const int sp = static_cast<int>(blockIdx.x - tile_id * p.ks);
-    const int64_t tt = tile_id / p.RT;
-    const int64_t rt = tile_id - tt * p.RT;
+    const int64_t tt = tile_id / p.RTP;
+    const int64_t rt0 = (tile_id - tt * p.RTP) * RPC;          // first row tile of the CTA
+    const int nrt = static_cast<int>(imin64(RPC, p.RT - rt0));     // row tiles present
+    constexpr int kStage = C::kStageBytes;
+    constexpr int kW = C::kWBytes;                                 // offset of x in a stage
+    constexpr int kF = C::kWBytes + C::kXBytes;                    // offset of the dW lists
     if (tt == p.T - 1) {
         // the only tile that can be empty: look before setting anything up
         pdl_wait();
@@ -178,7 +194,7 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
     // token groups past the real tokens are never copied: they read as zero in every stage
     for (int i = tid; i < S * (C::kXBytes / 16); i += C::kThreads) {
         const int st = i / (C::kXBytes / 16), off = i - st * (C::kXBytes / 16);
-        reinterpret_cast<uint4*>(smem + st * C::kStageBytes + C::kWBytes)[off] = make_uint4(0, 0, 0, 0);
+        reinterpret_cast<uint4*>(smem + st * kStage + kW)[off] = make_uint4(0, 0, 0, 0);
     }
     fence_proxy_async_smem();
     if (tid == 0) {
@@ -187,7 +203,7 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < AB; ++i) {
-            mbar_init(&a_full[i], C::kDqWarps / 2);  // one set writes a block
+            mbar_init(&a_full[i], 8 * nrt);  // every present row tile's set writes its block
             mbar_init(&a_empty[i], 1);
         }
         mbar_init(done, 1);
@@ -213,9 +229,10 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             for (int it = 0; it < pre; ++it, ++issued) {
                 const int kb0 = kb_begin + it * SKB;
                 const int n = kb_end - kb0 < SKB ? kb_end - kb0 : SKB;
-                mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
-                bulk_g2s_stream(smem + it * C::kStageBytes, p.wq + (rt * p.KB + kb0) * 1024,
-                                static_cast<uint32_t>(n * 4096), &full[it], pol);
+                mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(nrt * n * 4096));
+                for (int r = 0; r < nrt; ++r)
+                    bulk_g2s_stream(smem + it * kStage + r * SKB * 4096, p.wq + ((rt0 + r) * p.KB + kb0) * 1024,
+                                    static_cast<uint32_t>(n * 4096), &full[it], pol);
             }
             pdl_wait();
             const GemmTile g = gemm_tile(p, tt);
@@ -232,26 +249,33 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             for (int it = 0; it < nst && g.ntile > 0; ++it) {
                 const int slot = it % S, kb0 = kb_begin + it * SKB;
                 const int n = kb_end - kb0 < SKB ? kb_end - kb0 : SKB;
-                unsigned char* st = smem + slot * C::kStageBytes;
+                unsigned char* st = smem + slot * kStage;
                 if (it >= S) {
                     if (!mbar_wait(&empty[slot], ((it / S) - 1) & 1, p.status)) {
                         s_abort = 1;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * 4096));
-                    bulk_g2s_stream(st, p.wq + (rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096), &full[slot],
-                                    pol);
+                    mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nrt * n * 4096));
+                    for (int r = 0; r < nrt; ++r)
+                        bulk_g2s_stream(st + r * SKB * 4096, p.wq + ((rt0 + r) * p.KB + kb0) * 1024,
+                                        static_cast<uint32_t>(n * 4096), &full[slot], pol);
                     ++issued;
                 }
                 uint32_t fbytes = 0;
-                if (fold) fbytes = p.foldoff[rt * p.KB + kb0 + n] - p.foldoff[rt * p.KB + kb0];
+                if (fold)
+                    for (int r = 0; r < nrt; ++r)
+                        fbytes += p.foldoff[(rt0 + r) * p.KB + kb0 + n] - p.foldoff[(rt0 + r) * p.KB + kb0];
                 mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(n * greal * 1024) + fbytes);
                 for (int j = 0; j < n; ++j) {
-                    bulk_g2s(st + C::kWBytes + j * G * 1024, xsrc + ((kb0 + j) * Gp + (pos0 >> 3)) * 512,
+                    bulk_g2s(st + kW + j * G * 1024, xsrc + ((kb0 + j) * Gp + (pos0 >> 3)) * 512,
                              static_cast<uint32_t>(greal * 1024), &full[slot]);
                     if (fold) {
-                        const uint32_t o0 = p.foldoff[rt * p.KB + kb0 + j], o1 = p.foldoff[rt * p.KB + kb0 + j + 1];
-                        bulk_g2s(st + C::kWBytes + C::kXBytes + j * kFoldCap, p.fold + o0, o1 - o0, &full[slot]);
+                        for (int r = 0; r < nrt; ++r) {
+                            const int64_t li = (rt0 + r) * p.KB + kb0 + j;
+                            const uint32_t o0 = p.foldoff[li], o1 = p.foldoff[li + 1];
+                            bulk_g2s(st + kF + (r * SKB + j) * kFoldCap, p.fold + o0, o1 - o0,
+                                     &full[slot]);
+                        }
                     }
                 }
             }
@@ -270,12 +294,15 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             ok = __all_sync(0xffffffffu, ok);  // the elected lane below needs the whole warp
             if (!ok) break;
             tc_fence_after();
-            const unsigned char* xs = smem + slot * C::kStageBytes + C::kWBytes + kbl * G * 1024;
+            const unsigned char* xs = smem + slot * kStage + kW + kbl * G * 1024;
             if (elect_one()) {
+                // every row tile against the same x block: D of tile r in columns [r*128, r*128+128)
+                for (int r = 0; r < nrt; ++r) {
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    tc_mma_ts(tmem, tmem + NT + b * 32 + i * 8, desc_kmajor(xs + 2 * i * 128, 128, 1024), idesc,
-                              (j | i) ? 1u : 0u);
+                    for (int i = 0; i < 4; ++i)
+                        tc_mma_ts(tmem + r * NT, tmem + C::kRowTiles * NT + (r * AB + b) * 32 + i * 8,
+                                  desc_kmajor(xs + 2 * i * 128, 128, 1024), idesc, (j | i) ? 1u : 0u);
+                }
                 tc_commit(&a_empty[b]);
                 if (kbl == SKB - 1 || j == nkb - 1) tc_commit(&empty[slot]);
             }
@@ -285,9 +312,14 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         if (elect_one()) tc_commit(done);  // also after an abort, so that the TMEM can be released
         __syncwarp();
     } else {
+        // two row tiles: set s takes row tile s, every block; one row tile: the sets take
+        // alternate blocks of it (two independent store pipelines)
         const int sq = warp & 3, q = (warp >> 2) & 1, set = warp >> 3;
         const int tile = 2 * sq + q;
         const uint32_t lane_addr = static_cast<uint32_t>(32 * sq + 16 * q) << 16;
+        const int r = nrt == 1 ? 0 : set;          // row tile of this warp
+        const int jstep = nrt == 1 ? 2 : 1;
+        const int64_t rt = rt0 + r;
         pdl_wait();
         const GemmTile g = gemm_tile(p, tt);
         const int64_t pos0 = g.pos0, R = g.R;
@@ -300,14 +332,15 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         auto load_block = [&](int jj, uint32_t (&hh)[4][4]) -> bool {
             const int s = jj / SKB, kbl = jj - s * SKB, slot = s % S;
             if (!mbar_wait(&full[slot], (s / S) & 1, p.status)) return false;
-            const unsigned char* stg = smem + slot * C::kStageBytes;
-            const uint4 wv = *reinterpret_cast<const uint4*>(stg + kbl * 4096 + tile * 512 + lane * 16);
+            const unsigned char* stg = smem + slot * kStage;
+            const uint4 wv =
+                *reinterpret_cast<const uint4*>(stg + (r * SKB + kbl) * 4096 + tile * 512 + lane * 16);
             const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
             for (int st = 0; st < 4; ++st) dequant_word(words[st], hh[st]);
             if (fold) {
                 // this lane's entries of the block (register slot, half, f16 dW/s)
-                const unsigned char* lst = stg + C::kWBytes + C::kXBytes + kbl * kFoldCap;
+                const unsigned char* lst = stg + kF + (r * SKB + kbl) * kFoldCap;
                 const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + tile * 33 + lane;
                 const uint32_t* ent = reinterpret_cast<const uint32_t*>(lst + kFoldHdr);
                 const int e1 = offs[1];
@@ -320,7 +353,7 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             return true;
         };
         uint32_t h[4][4];
-        int j = set;
+        int j = nrt == 1 ? set : 0;
         bool have = ntile > 0 && j < nkb;
         if (have && !load_block(j, h)) {
             s_abort = 1;
@@ -335,8 +368,9 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
             tc_fence_after();
 #pragma unroll
             for (int st = 0; st < 4; ++st)
-                tc_st_16x256b(tmem + lane_addr + NT + b * 32 + st * 8, h[st][0], h[st][2], h[st][1], h[st][3]);
-            const int jn = j + 2;
+                tc_st_16x256b(tmem + lane_addr + C::kRowTiles * NT + (r * AB + b) * 32 + st * 8, h[st][0], h[st][2],
+                              h[st][1], h[st][3]);
+            const int jn = j + jstep;
             uint32_t hn[4][4];
             bool next = jn < nkb;
             if (next && !load_block(jn, hn)) {
@@ -354,7 +388,8 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
                 for (int r = 0; r < 4; ++r) h[st][r] = hn[st][r];
             j = jn;
         }
-        // epilogue: warp qq = warp / 4 of sub-partition sq owns rows 32 sq + lane and tokens [32 qq, 32 qq + 32)
+        // epilogue: rows 32 sq + lane of row tile r; tokens [64 q, +64) with two row tiles, else
+        // [32 (2 set + q), +32)
         if (ntile > 0 && mbar_wait(done, 0, p.status) && !s_abort) {
             tc_fence_after();
             const int64_t row = rt * 128 + 32 * sq + lane;
@@ -368,14 +403,14 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
                 e1 = p.ks == 1 ? hi : lower_bound_u16(p.col, e0, hi, static_cast<int64_t>(kb_end) * 64);
             }
             const uint32_t lane_rows = static_cast<uint32_t>(32 * sq) << 16;
-            float* part = p.partial + ((tile_id * p.ks + sp) * NT) * 128;
-            const int qq = warp >> 2;
+            float* part = p.partial + ((tile_id * p.ks + sp) * NT) * 256;
+            const int nch = nrt == 1 ? 4 : 8, cq = nrt == 1 ? 2 * set + q : q;
 #pragma unroll 1
-            for (int cb = 4 * qq; cb < 4 * qq + 4; ++cb) {
+            for (int cb = nch * cq; cb < nch * cq + nch; ++cb) {
                 const int t0 = cb * 8;
                 if (t0 >= ntile) break;
                 uint32_t d[8];
-                tc_ld8(tmem + lane_rows + t0, d);
+                tc_ld8(tmem + lane_rows + r * NT + t0, d);
                 tc_wait_ld();
                 float corr[8];
 #pragma unroll
@@ -396,7 +431,7 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
                     if (t0 + u < ntile) {
                         const float v = __fadd_rn(__fmul_rn(__uint_as_float(d[u]), sc), corr[u]);
                         if (p.ks > 1) {
-                            part[(t0 + u) * 128 + 32 * sq + lane] = v;
+                            part[(t0 + u) * 256 + r * 128 + 32 * sq + lane] = v;
                         } else if (live) {
                             const int64_t oi = static_cast<int64_t>(p.perm[pos0 + t0 + u]) * p.N + row;
                             if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = v;
@@ -435,13 +470,14 @@ __global__ void __launch_bounds__(GemmCfg::kThreads, 1) k_ctarq_gemm(GemmParams 
         __syncthreads();
         if (!s_last) return;
         __threadfence();
-        const float* base = p.partial + (tile_id * p.ks * NT) * 128;
-        for (int i = tid; i < ntile * 128; i += C::kThreads) {
-            const int t = i >> 7, rl = i & 127;
-            const int64_t r = rt * 128 + rl;
+        const float* base = p.partial + (tile_id * p.ks * NT) * 256;
+        const int rows = 128 * nrt;  // this CTA's rows (its row tiles only)
+        for (int i = tid; i < ntile * rows; i += C::kThreads) {
+            const int t = i / rows, rl = i - t * rows;
+            const int64_t r = rt0 * 128 + rl;
             if (r >= p.N) continue;
             float v = 0.0f;
-            for (int k = 0; k < p.ks; ++k) v = __fadd_rn(v, __ldcg(base + (k * NT + t) * 128 + rl));
+            for (int k = 0; k < p.ks; ++k) v = __fadd_rn(v, __ldcg(base + (k * NT + t) * 256 + rl));
             const int64_t oi = static_cast<int64_t>(p.perm[pos0 + t]) * p.N + r;
             if (p.partial_out) reinterpret_cast<float*>(p.y)[oi] = v;
             else store_output(p.y, p.y_dtype, oi, v, p.bias, r);
@@ -478,12 +514,20 @@ __global__ void k_gather_tokens(const uint16_t* __restrict__ xk, uint16_t* __res
     }
 }
 
-int64_t gemm_tile_tokens() { return GemmCfg::NT; }
+int64_t gemm_tile_tokens() { return GemmCfg<1>::NT; }
+
+// Row tiles per CTA: two (sharing every x block, half the x traffic per MMA) while the grid of
+// pairs still fills every SM once, else one (more CTAs, a deeper ring).
+static int gemm_rows_per_cta(const Layer& L, int64_t m) {
+    const int64_t pairs = (L.Np / 128 + 1) / 2 * ((m + GemmCfg<1>::NT - 1) / GemmCfg<1>::NT);
+    return pairs >= L.sms ? 2 : 1;
+}
 
 int gemm_ksplit(const Layer& L, int64_t m) {
     // column splits while the tiles alone leave SMs idle, each split keeping >= 8 blocks (the
     // launch's extra token tile is usually empty and is not counted)
-    const int64_t tiles = (L.Np / 128) * ((m + GemmCfg::NT - 1) / GemmCfg::NT);
+    const int rpc = gemm_rows_per_cta(L, m);
+    const int64_t tiles = (L.Np / 128 + rpc - 1) / rpc * ((m + GemmCfg<1>::NT - 1) / GemmCfg<1>::NT);
     int64_t ks = std::max<int64_t>(1, static_cast<int64_t>(L.sms) / std::max<int64_t>(1, tiles));
     ks = std::min<int64_t>(ks, std::min<int64_t>(16, std::max<int64_t>(1, L.KB / 8)));
     return static_cast<int>(ks);
@@ -512,7 +556,9 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     p.N = L.N;
     p.KB = L.KB;
     p.RT = L.Np / 128;
-    p.T = (a.M + GemmCfg::NT - 1) / GemmCfg::NT + 1;
+    p.rpc = gemm_rows_per_cta(L, a.M);
+    p.RTP = (p.RT + p.rpc - 1) / p.rpc;
+    p.T = (a.M + GemmCfg<1>::NT - 1) / GemmCfg<1>::NT + 1;
     p.ks = a.ks;
     p.partial = a.partial;
     p.tcount = a.tcount;
@@ -526,17 +572,18 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     cudaError_t e = launch_pdl(k_gather_tokens, dim3(static_cast<unsigned>(gblocks)), dim3(256), 0, s,
                                a.xk, a.xkp, a.perm, a.nrouted, a.route_all, a.M, a.Mp, a.Mpp, L.KB);
     if (e != cudaSuccess) return e;
-    static std::atomic<uint64_t> flags{0};
+    static std::atomic<uint64_t> flags[2] = {{0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    if (!(flags.load() & bit)) {
-        e = cudaFuncSetAttribute(k_ctarq_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg::kTotal);
+    auto kern = p.rpc == 2 ? k_ctarq_gemm<2> : k_ctarq_gemm<1>;
+    const int smem = p.rpc == 2 ? GemmCfg<2>::kTotal : GemmCfg<1>::kTotal;
+    if (!(flags[p.rpc - 1].load() & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        flags.fetch_or(bit);
+        flags[p.rpc - 1].fetch_or(bit);
     }
-    return launch_pdl(k_ctarq_gemm, dim3(static_cast<unsigned>(p.RT * p.T * p.ks)), dim3(GemmCfg::kThreads),
-                      GemmCfg::kTotal, s, p);
+    return launch_pdl(kern, dim3(static_cast<unsigned>(p.RTP * p.T * p.ks)), dim3(GemmCfg<1>::kThreads), smem, s, p);
 }
 
 // Fold lists from the host CSR (columns ascending per row) and the f32 row scales: for every

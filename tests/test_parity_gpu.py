@@ -258,6 +258,8 @@ def test_qwen2_7b_shapes(sc, n, k, m, mode):
     (1000, 520, 40, 40, 0.04),     # one tile, all routed, K not a multiple of 64
     (130, 200, 9, 0, 0.02),        # the smallest GEMM call, nothing routed
     (96, 128, 20, 20, 1.0),        # dense dW: lists too long to fold, dW in the epilogue
+    (4864, 896, 1100, 300, 0.01),  # enough tiles for two row tiles per CTA
+    (4736, 512, 1100, 400, 0.02),  # two row tiles per CTA, the last CTA holding one
 ])
 def test_prefill_gemm_routing(sc, n, k, m, nroute, fill):
     rng = np.random.default_rng(n + m + nroute)
