@@ -64,7 +64,7 @@ static int sm_count(int dev) {
 int choose_ksplit(int64_t rt, int64_t kb) {
     const int64_t min_ks = (kb + fused_max_kb(1) - 1) / fused_max_kb(1);
     if (min_ks > kMaxFusedCluster) return 0;
-    const bool small = rt * kb * 4096 <= fused_prefetch_bytes();
+    const bool small = rt * kb * 4096 * 100 <= fused_prefetch_bytes() * SC_FUSED_SMALL_PCT;
     int best = 0;
     for (int ks = 1; ks <= kMaxFusedCluster; ++ks) {
         if (ks < min_ks || (ks > 1 && kb / ks < 2)) continue;

@@ -59,6 +59,9 @@ constexpr int64_t kDwBlockMax = 16 * 1024;
 #ifndef SC_FUSED_MAX_CLUSTER
 #define SC_FUSED_MAX_CLUSTER 16
 #endif
+#ifndef SC_FUSED_SMALL_PCT
+#define SC_FUSED_SMALL_PCT 100  // a launch is small (one CTA per SM) up to this % of the one-CTA-per-SM rings
+#endif
 #ifndef SC_FUSED_INT8
 #define SC_FUSED_INT8 1  // one-token decode in SC_MODE_FAST runs the s8 integer variant
 #endif
