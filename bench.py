@@ -11,7 +11,9 @@ Effective bytes per call (the metric's numerator, independent of the device layo
 value = bytes of all calls of all ranks / max-over-ranks device time (CUDA events).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M] [--impl reference]
-  python bench.py --sweep OUT.md      # single calls: 4 shapes x M 1..4096 x routed 0/25/100 %
+  python bench.py --sweep OUT.md [--sweep-fills 0.005,0.01,0.04]
+                                      # single calls: 4 shapes x M 1..4096 x routed 0/10/25/100 %
+                                      # x dW densities
 
 --impl reference times the reference's CPU algorithm (the oracle restatement of
 saccade-core's op.rs; the Rust reference cannot be built here) on the host cores.
@@ -60,6 +62,8 @@ def parse():
     ap.add_argument("--sweep", metavar="PATH",
                     help="instead of the step: time single calls over a grid of shapes x tokens x routed "
                          "fractions (one GPU) and write a markdown table to PATH")
+    ap.add_argument("--sweep-fills", default=None, metavar="LIST",
+                    help="comma-separated dW densities for --sweep (default: --fill)")
     return ap.parse_args()
 
 
@@ -491,12 +495,12 @@ def run_ours(args, rank, world):
 
 SWEEP_SHAPES = [("q/o", 3584, 3584), ("k/v", 512, 3584), ("gate/up", 18944, 3584), ("down", 3584, 18944)]
 SWEEP_TOKENS = [1, 4, 16, 64, 256, 1024, 4096]
-SWEEP_ROUTED = [0.0, 0.25, 1.0]
+SWEEP_ROUTED = [0.0, 0.10, 0.25, 1.0]
 SWEEP_POOL_BYTES = 512 * 2 ** 20  # round-robin over >= 4x L2 of distinct layers
 
 
 def run_sweep(args):
-    """Single-call times over shapes x tokens x routed fractions (1 % dW): every point replays a
+    """Single-call times over dW densities x shapes x tokens x routed fractions: every point replays a
     CUDA graph of one call on each layer of a pool of distinct copies of the layer (>= 512 MB of
     weights, so each call reads its weights from HBM), and reports the algorithmic bytes and
     flops per call against the measured HBM and bf16 peaks."""
@@ -514,11 +518,12 @@ def run_sweep(args):
         tc = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["bf16_tflops"])
     except (OSError, ValueError, KeyError):
         pass
+    fills = [float(v) for v in args.sweep_fills.split(",")] if args.sweep_fills else [args.fill]
     rows = []
-    for label, n, k in SWEEP_SHAPES:
+    for fill, (label, n, k) in [(f, sh) for f in fills for sh in SWEEP_SHAPES]:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
         scale = ((0.02 * (3.0 + torch.rand(n, device=dev, generator=gen))) / 7.0).to(torch.float16)
-        nnz = int(round(n * k * args.fill))
+        nnz = int(round(n * k * fill))
         flat = torch.unique(torch.randint(0, n * k, (int(nnz * 1.02) + 16,), device=dev, generator=gen))[:nnz]
         rr, cc = flat // k, flat % k
         rp = torch.zeros(n + 1, dtype=torch.int64, device=dev)
@@ -567,7 +572,7 @@ def run_sweep(args):
                 b = call_bytes(n, k, m, real_nnz, r > 0)
                 fl = 2.0 * m * n * k + 2.0 * real_nnz * r
                 t_hbm, t_tc = b / (hbm * 1e3), fl / (tc * 1e6)  # microseconds
-                rows.append((label, n, k, m, frac, us, b / us / 1e3, fl / us / 1e6,
+                rows.append((fill, label, n, k, m, frac, us, b / us / 1e3, fl / us / 1e6,
                              "hbm" if t_hbm >= t_tc else "tensor", max(t_hbm, t_tc) / us, pool))
                 del g
             del y
@@ -575,18 +580,19 @@ def run_sweep(args):
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
     with open(args.sweep, "w") as f:
-        f.write(f"# C-TARQ linear: single-call sweep ({args.mode} mode, {args.fill:.0%} dW, f16 x)\n\n")
+        f.write(f"# C-TARQ linear: single-call sweep ({args.mode} mode, f16 x)\n\n")
         f.write("Command: `python bench.py --sweep " + args.sweep + (f" --mode {args.mode}" if args.mode != "fast" else "")
-                + "`\n\n")
+                + (f" --sweep-fills {args.sweep_fills}" if args.sweep_fills else "")
+                + (f" --fill {args.fill}" if not args.sweep_fills and args.fill != 0.01 else "") + "`\n\n")
         f.write(f"Peaks: HBM {hbm} GB/s, bf16 dense {tc} TFLOP/s (MEASURED_PEAKS.json). `bound` is the larger of "
                 "bytes/HBM and flops/tensor; `frac` = that bound time / measured time. Routed = fraction of "
                 "the tokens boosted x8 (their variance clears t4 = 8). Each point replays one call on every "
                 "layer of a pool of distinct copies (>= 512 MB of weights).\n\n")
-        f.write("| shape | N x K | M | routed | us / call | GB/s | TFLOP/s | bound | frac | pool |\n")
-        f.write("|---|---|---|---|---|---|---|---|---|---|\n")
-        for (label, n, k, m, frac, us, gbs, tfl, bound, fr, pool) in rows:
-            f.write(f"| {label} | {n}x{k} | {m} | {frac:.0%} | {us:.2f} | {gbs:.0f} | {tfl:.1f} | {bound} | "
-                    f"{fr:.3f} | {pool} |\n")
+        f.write("| dW | shape | N x K | M | routed | us / call | GB/s | TFLOP/s | bound | frac | pool |\n")
+        f.write("|---|---|---|---|---|---|---|---|---|---|---|\n")
+        for (fill, label, n, k, m, frac, us, gbs, tfl, bound, fr, pool) in rows:
+            f.write(f"| {fill:.1%} | {label} | {n}x{k} | {m} | {frac:.0%} | {us:.2f} | {gbs:.0f} | {tfl:.1f} | "
+                    f"{bound} | {fr:.3f} | {pool} |\n")
     print(json.dumps({"sweep": args.sweep, "points": len(rows)}), flush=True)
 
 

@@ -86,12 +86,14 @@ bool use_fused(const Layer& L, int64_t m) { return use_fused_ks(L, m, L.ks_fused
 // dW blocks of the router-fused decode for `ks` column splits, from the host CSR (columns local
 // to the layer, ascending per row): for every (row tile, split), 129 u16 row offsets (272 B), the
 // u16 columns relative to the split, then the i8 values, each padded to 16 B; off[rt * ks + sp]
-// is the byte offset of a block.  Left empty (the kernel then reads the CSR) when a block would
-// exceed the kernel's shared-memory copy.
+// is the byte offset of a block.  When a block would exceed the kernel's shared-memory copy,
+// every CTA of the layer reads its block from global memory instead (`global`).  Left empty (the
+// kernel then reads the CSR) when a block holds more entries than u16 offsets describe.
 struct DwBlocks {
     uint8_t* blk = nullptr;
     uint32_t* off = nullptr;
     int64_t bytes = 0;
+    int global = 0;
 };
 
 static cudaError_t build_dw_blocks(const Layer& L, int ks, const uint32_t* srp, const uint16_t* scol,
@@ -103,6 +105,7 @@ static cudaError_t build_dw_blocks(const Layer& L, int ks, const uint32_t* srp, 
     std::vector<uint8_t> blob;
     std::vector<uint16_t> roff(129), cols;
     std::vector<int8_t> vals;
+    int global = 0;
     for (int64_t rt = 0; rt < RT; ++rt) {
         for (int64_t sp = 0; sp < ks; ++sp) {
             const int64_t bc0 = (L.KB * sp / ks) * 64, bc1 = (L.KB * (sp + 1) / ks) * 64;
@@ -124,7 +127,8 @@ static cudaError_t build_dw_blocks(const Layer& L, int ks, const uint32_t* srp, 
             if (n > 65535) return cudaSuccess;  // u16 row offsets cannot describe the block
             roff[128] = static_cast<uint16_t>(n);
             const size_t bytes = 272 + ((n * 2 + 15) / 16) * 16 + ((n + 15) / 16) * 16;
-            if (static_cast<int64_t>(bytes) > kDwBlockMax) return cudaSuccess;
+            if (static_cast<int64_t>(bytes) > kDwBlockMax) global = 1;
+            if (blob.size() + bytes > 0xFFFFFFFFull) return cudaSuccess;  // u32 block offsets
             const size_t at = blob.size();
             blob.resize(at + bytes, 0);
             std::memcpy(&blob[at], roff.data(), 129 * 2);
@@ -146,6 +150,7 @@ static cudaError_t build_dw_blocks(const Layer& L, int ks, const uint32_t* srp, 
         return e;
     }
     out->bytes = static_cast<int64_t>(blob.size() + off.size() * 4);
+    out->global = global;
     return cudaSuccess;
 }
 
@@ -276,6 +281,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         f.ksplit = w.ksplit;
         f.dwblk = L.dwblk;
         f.dwoff = L.dwoff;
+        f.dw_global = L.dw_global;
         cudaError_t e = launch_decode_fused(&f, 1, stream);
         if (e != cudaSuccess) return cuda_fail(e, "fused decode launch");
         return SC_OK;
@@ -667,6 +673,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
         e = build_dw_blocks(L, L.ks_fused, srp.data(), scol.data(), sval.data(), &b);
         L.dwblk = b.blk;
         L.dwoff = b.off;
+        L.dw_global = b.global;
         L.device_bytes += b.bytes;
     }
     if (e == cudaSuccess && L.nnz > 0) {
@@ -943,6 +950,7 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
             const bool layers_fit = group->ksplit == L.ks_fused;
             a.dwblk = own ? group->own[i].blk : layers_fit ? L.dwblk : nullptr;
             a.dwoff = own ? group->own[i].off : layers_fit ? L.dwoff : nullptr;
+            a.dw_global = own ? group->own[i].global : layers_fit ? L.dw_global : 0;
         }
         const cudaError_t e = launch_decode_fused(f, n, s);
         if (e != cudaSuccess) return cuda_fail(e, "grouped decode launch");

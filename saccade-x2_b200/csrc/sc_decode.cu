@@ -340,6 +340,7 @@ struct FusedParams {
     int32_t* nrouted_out;
     const uint8_t* dwblk;   // blocked dW (null: read the CSR)
     const uint32_t* dwoff;
+    int dw_global;          // 1: each CTA reads its block from global memory (no shared-memory copy)
     int ntp;                // staged token rows: 1, 2, 4 or 8
     int full_row;           // one token whose whole row fits the staging region: one bulk copy of
                             // it, and the one-token kernels route on their own sums (no exchange)
@@ -422,7 +423,8 @@ struct FusedCtx {
     int64_t rt, kb_begin, kb_end;
     int bid;  // CTA index within this layer's part of the grid
     int split, ks, nkb, ntok, cs, rb, nr;
-    bool use_blk;
+    bool use_blk;   // dW in the blocked layout
+    bool blk_copy;  // ... bulk-copied to shared memory (else read in place from global memory)
     bool local;  // route on this CTA's own sums of the staged whole token (one-token kernels)
 };
 
@@ -460,6 +462,7 @@ __device__ __forceinline__ FusedCtx fused_ctx(const FusedParams& fp, int bid, un
     c.rb = (128 * c.split) / c.ks;
     c.nr = (128 * (c.split + 1)) / c.ks - c.rb;
     c.use_blk = fp.dwblk != nullptr && p.nnz > 0;
+    c.blk_copy = c.use_blk && !fp.dw_global;
     c.local = one_token && fp.full_row;
     if (c.local) c.xs = c.xrow + (fp.x_col0 + c.kb_begin * 64) * 2;
     c.split8 = nullptr;
@@ -494,7 +497,7 @@ __device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* r
     const uint64_t pol = policy_evict_first();
     const int pre = nst < S ? nst : S;
     int issued = 0;
-    if (c.use_blk) {
+    if (c.blk_copy) {
         const uint32_t o0 = c.fp->dwoff[c.bid], o1 = c.fp->dwoff[c.bid + 1];
         mbar_arrive_expect_tx(c.dw_ready, o1 - o0);
         bulk_g2s(const_cast<unsigned char*>(c.dws), c.fp->dwblk + o0, o1 - o0, c.dw_ready);
@@ -799,7 +802,7 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
             if ((mask >> t) & 1u)
                 corr[t] = __fadd_rn(corr[t], __fmul_rn(h2f(*reinterpret_cast<const uint16_t*>(xp + t * 16)), v));
     };
-    if (c.use_blk) {
+    if (c.blk_copy) {
         if (!mbar_wait(c.dw_ready, 0, p.status)) {
             *c.s_abort = 1;
             return;
@@ -809,6 +812,26 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
         const uint16_t* bcol = reinterpret_cast<const uint16_t*>(c.dws + 272);
         const int8_t* bval = reinterpret_cast<const int8_t*>(c.dws + 272 + ((n * 2 + 15) / 16) * 16);
         for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
+    } else if (c.use_blk) {
+        // the same block read in place: 8 entries loaded before they are added (same order)
+        const unsigned char* blk = fp.dwblk + fp.dwoff[c.bid];
+        const uint16_t* roff = reinterpret_cast<const uint16_t*>(blk);
+        const int n = roff[128];
+        const uint16_t* bcol = reinterpret_cast<const uint16_t*>(blk + 272);
+        const int8_t* bval = reinterpret_cast<const int8_t*>(blk + 272 + ((n * 2 + 15) / 16) * 16);
+        const int e1 = roff[at + 1];
+        for (int e = roff[at]; e < e1; e += 8) {
+            const int cnt = e1 - e < 8 ? e1 - e : 8;
+            int cc[8], vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                cc[u] = u < cnt ? static_cast<int>(__ldg(bcol + e + u)) : 0;
+                vv[u] = u < cnt ? static_cast<int>(__ldg(bval + e + u)) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (u < cnt) add_entry(cc[u], static_cast<int8_t>(vv[u]));
+        }
     } else {
         const int64_t lo = p.rowptr[row], hi = p.rowptr[row + 1];
         const int64_t e0 = (ks == 1) ? lo : lower_bound_u16(p.col, lo, hi, c.kb_begin * 64);
@@ -1098,7 +1121,7 @@ __global__ void __launch_bounds__(FusedTcCfg<F8>::kThreads, 2) k_ctarq_fused_tc(
     if (s_abort && warp == C::kProducerWarp && lane == 0) {
         for (int it = issued > S ? issued - S : 0; it < issued; ++it)
             mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
-        if (c.use_blk) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
+        if (c.blk_copy) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
     }
     if (warp >= C::kAuxWarp0) fused_aux_finish<TK>(c, at, v);
 }
@@ -1291,7 +1314,7 @@ __global__ void __launch_bounds__(FusedMmaCfg::kThreads, 2) k_ctarq_fused_mma(Fu
     if (s_abort && warp == C::kProducerWarp && lane == 0) {
         for (int it = issued > S ? issued - S : 0; it < issued; ++it)
             mbar_wait(&full[it % S], (it / S) & 1, nullptr, kDrainNs);
-        if (c.use_blk) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
+        if (c.blk_copy) mbar_wait(c.dw_ready, 0, nullptr, kDrainNs);
     }
     if (warp < C::kAuxWarp0) return;
     const int64_t row = c.rt * 128 + at;
@@ -1564,6 +1587,7 @@ static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     fp.nrouted_out = f.nrouted_out;
     fp.dwblk = f.dwblk;
     fp.dwoff = f.dwoff;
+    fp.dw_global = f.dw_global;
     fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
     fp.rc = route_consts(fp.Kfull);
     // each auxiliary thread adds at most T values sequentially in f32 (both passes), then five

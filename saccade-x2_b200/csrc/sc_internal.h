@@ -48,6 +48,8 @@ struct Layer {
     int ks_fused = 0;            // column splits (= cluster size) of the fused kernel; 0: not usable
     uint8_t* dwblk = nullptr;
     uint32_t* dwoff = nullptr;   // byte offset of block (rt * ks_fused + split); [RT*ks_fused + 1]
+    int dw_global = 0;           // 1: some block exceeds the kernel's shared-memory copy, so every
+                                 // CTA reads its block from global memory
     // dW over the row scale, per (128-row tile, 64-column block), for the prefill GEMM: routed
     // tokens' tiles fold it into the dequantised weights ((q - 8) + dW/s, see sc_gemm.cu).
     uint8_t* fold = nullptr;     // lists, each [9 u16 offsets per 16-row tile | pad to 32 B | u32 entries]
@@ -207,6 +209,7 @@ struct FusedArgs {
     int ksplit;
     const uint8_t* dwblk;   // dW blocks built for this ksplit (null: the kernel reads the CSR)
     const uint32_t* dwoff;
+    int dw_global;          // 1: the blocks are read from global memory (too large to copy)
 };
 // One launch for n (<= SC_GROUP_MAX) layers that read the same x, all with the same ksplit and mode.
 cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s);

@@ -97,6 +97,27 @@ def test_fast_mode_within_tolerance(sc, n, k, m, fill, mode):
     assert_acc_close(acc, acc_ref, f"fast acc {n}x{k} m={m}")
 
 
+@pytest.mark.parametrize("mode", FAST_MODES)
+@pytest.mark.parametrize("n,k,m", [(256, 3584, 1), (256, 3584, 4), (384, 3584, 8)])
+def test_fused_decode_dw_blocks_in_global_memory(sc, n, k, m, mode):
+    # 25 % dW: with at most 16 column splits a CTA covers >= 224 columns, so its dW block
+    # (~3 B per entry, 128 rows) is > 16 KB and is read in place instead of being copied.
+    assert 128 * (k // 16) * 0.25 * 3 > 16 * 1024
+    case = make_case(n, k, m, 0.25, seed=n + k + 7 * m)
+    op = to_op(sc, case, mode=mode)
+    y, mask, ridx = run_gpu(op, case.x_bits)
+    yr, rr, acc_ref = case.oracle().forward(case.x_bits)
+    assert rr.any(), "the case routes at least one token"
+    assert np.array_equal(mask, rr)
+    assert np.array_equal(ridx, np.nonzero(rr)[0])
+    assert_fast_close(y_bits(y), yr, f"fast {n}x{k} m={m} 25% dW")
+    grp = sc.SaccadeLinearGroup([op, to_op(sc, make_case(128, k, m, 0.25, seed=5), mode=mode)])
+    ys = grp.forward(torch.from_numpy(case.x_bits.view(np.float16)).to("cuda:0"))
+    torch.cuda.synchronize()
+    op.check_device()
+    assert_fast_close(y_bits(ys[0]), yr, f"group {n}x{k} m={m} 25% dW")
+
+
 def test_threshold_token_exactly_on_t4(sc):
     # calibrate() puts t4 exactly on one token's score; the router must reproduce the
     # reference's f32 decision for it (score >= t4 -> routed).
