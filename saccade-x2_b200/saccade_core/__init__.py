@@ -5,6 +5,9 @@ include/saccade_ctarq.h); this package is the host-side mirror of the reference'
 names (saccade-core/src/lib.rs:9-12).
 """
 from ._lib import CTarqError, LIB_PATH
+from .checkpoint import (SaccadeMlp, build_saccade_op, compile_mlp_checkpoint, extract_scalar_f32,
+                         load_mlp, load_saccade_checkpoint, read_safetensors, saccade_blocks,
+                         write_safetensors)
 from .graph import CapturedStep
 from .compress import (ProfileRunner, compress_tensor_to_saccade, compute_percentile_threshold,
                        saccade_op_from_compressed)
@@ -12,7 +15,9 @@ from .op import (SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDelta
                  is_c_tarq_bypassed, set_bypass_c_tarq, variance_heuristic)
 
 __all__ = [
-    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearGroup", "SaccadeLinearOp", "SparseDeltaMatrix",
-    "compress_tensor_to_saccade", "compute_percentile_threshold", "finalize", "is_c_tarq_bypassed",
-    "saccade_op_from_compressed", "set_bypass_c_tarq", "variance_heuristic",
+    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearGroup", "SaccadeLinearOp",
+    "SaccadeMlp", "SparseDeltaMatrix", "build_saccade_op", "compile_mlp_checkpoint", "compress_tensor_to_saccade",
+    "compute_percentile_threshold", "extract_scalar_f32", "finalize", "is_c_tarq_bypassed", "load_mlp",
+    "load_saccade_checkpoint", "read_safetensors", "saccade_blocks", "saccade_op_from_compressed",
+    "set_bypass_c_tarq", "variance_heuristic", "write_safetensors",
 ]

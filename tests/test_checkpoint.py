@@ -1,0 +1,272 @@
+"""Compiled checkpoints: the safetensors container, the reference's saccade_* key schema
+(compress.rs:113-127, compile.rs:158-205, model.rs:437-495) and the loader built on it.
+
+CPU tests cover the container (round trips, a file assembled byte by byte from the format,
+malformed headers), the schema reader and the compile step with a host stand-in for the GPU
+packer; the `gpu` tests build the ops from a checkpoint file and compare them with the oracle.
+"""
+import json
+import struct
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from saccade_core import checkpoint as ck
+
+
+def _oracle_blocks(w, fill):
+    """compress_tensor_to_saccade's key set from the oracle's compress (host tensors)."""
+    c = O.compress(w, O.percentile_threshold(w, fill))
+    b = {"packed_base": torch.from_numpy(c.packed_base.copy()),
+         "scale_base": torch.from_numpy(c.scale_base.view(np.float16).copy())}
+    if c.nnz:
+        b["delta_row_ptrs"] = torch.from_numpy(c.delta_row_ptrs.copy())
+        b["delta_col_indices"] = torch.from_numpy(c.delta_col_indices.copy())
+        b["delta_values"] = torch.from_numpy(c.delta_values.copy())
+        b["delta_scale"] = torch.tensor([c.delta_scale], dtype=torch.int16).view(torch.float16)
+    return c, b
+
+
+def _tiny_model(rng, layers=3, hidden=64, inter=96):
+    """A Qwen2-shaped tensor map (random weights) with dense MLP projections."""
+    t = {"model.embed_tokens.weight": torch.from_numpy(rng.standard_normal((50, hidden)).astype(np.float32)),
+         "model.norm.weight": torch.ones(hidden, dtype=torch.bfloat16)}
+    for i in range(layers):
+        p = f"model.layers.{i}"
+        t[f"{p}.input_layernorm.weight"] = torch.ones(hidden)
+        t[f"{p}.self_attn.q_proj.weight"] = torch.from_numpy((rng.standard_normal((hidden, hidden)) * 0.02).astype(np.float32))
+        t[f"{p}.self_attn.q_proj.bias"] = torch.zeros(hidden)
+        for name, (n, k) in (("gate_proj", (inter, hidden)), ("up_proj", (inter, hidden)), ("down_proj", (hidden, inter))):
+            t[f"{p}.mlp.{name}.weight"] = torch.from_numpy((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    return t
+
+
+# ------------------------------------------------------------------ container
+
+def test_round_trip_every_dtype(tmp_path):
+    rng = np.random.default_rng(0)
+    ts = {
+        "f32": torch.from_numpy(rng.standard_normal((3, 5)).astype(np.float32)),
+        "f64": torch.from_numpy(rng.standard_normal(4)),
+        "f16": torch.from_numpy(rng.standard_normal((2, 3)).astype(np.float16)),
+        "bf16": torch.from_numpy(rng.standard_normal(7).astype(np.float32)).to(torch.bfloat16),
+        "u32": torch.from_numpy(rng.integers(0, 2 ** 32, (4, 2), dtype=np.uint32)),
+        "u8": torch.from_numpy(rng.integers(0, 256, 9, dtype=np.uint8)),
+        "i8": torch.from_numpy(rng.integers(-128, 128, 3, dtype=np.int8)),
+        "i32": torch.from_numpy(rng.integers(-2 ** 31, 2 ** 31, 5, dtype=np.int32)),
+        "i64": torch.from_numpy(rng.integers(-2 ** 62, 2 ** 62, 2, dtype=np.int64)),
+        "u16": torch.from_numpy(rng.integers(0, 2 ** 16, 3, dtype=np.uint16)),
+        "bool": torch.tensor([True, False, True]),
+        "scalar": torch.tensor(3.5, dtype=torch.float32),
+        "empty": torch.zeros((0, 4), dtype=torch.float16),
+    }
+    path = tmp_path / "all.safetensors"
+    ck.write_safetensors(str(path), ts, metadata={"format": "pt", "n": 13})
+    back, meta = ck.read_safetensors(str(path))
+    assert meta == {"format": "pt", "n": "13"}
+    assert set(back) == set(ts)
+    for k, v in ts.items():
+        assert back[k].dtype == v.dtype and tuple(back[k].shape) == tuple(v.shape), k
+        a = back[k].view(torch.uint16) if v.dtype == torch.bfloat16 else back[k]
+        b = v.view(torch.uint16) if v.dtype == torch.bfloat16 else v
+        assert torch.equal(a, b), k
+    # every tensor starts on a multiple of its element size
+    raw = path.read_bytes()
+    (hlen,) = struct.unpack("<Q", raw[:8])
+    assert hlen % 8 == 0
+    header = json.loads(raw[8:8 + hlen])
+    for k, ent in header.items():
+        if k != "__metadata__":
+            assert ent["data_offsets"][0] % ts[k].element_size() == 0, k
+
+
+def test_reads_a_file_assembled_from_the_format(tmp_path):
+    # built by hand: header length (u64 LE), JSON header, little-endian data; unaligned
+    # offsets, an unsorted header and no padding are all legal and must read back
+    u8 = bytes([1, 2, 3])
+    f32 = struct.pack("<3f", 1.5, -2.0, 0.25)
+    u32 = struct.pack("<2I", 7, 0xFFFFFFFF)
+    f16 = np.array([0.5, -1.0], dtype="<f2").tobytes()
+    data = u8 + f32 + u32 + f16
+    header = {"b": {"dtype": "F32", "shape": [3], "data_offsets": [3, 15]},
+              "a": {"dtype": "U8", "shape": [1, 3], "data_offsets": [0, 3]},
+              "d": {"dtype": "F16", "shape": [2], "data_offsets": [23, 27]},
+              "c": {"dtype": "U32", "shape": [2], "data_offsets": [15, 23]},
+              "__metadata__": {"k": "v"}}
+    hb = json.dumps(header).encode()
+    path = tmp_path / "hand.safetensors"
+    path.write_bytes(struct.pack("<Q", len(hb)) + hb + data)
+    t, meta = ck.read_safetensors(str(path))
+    assert meta == {"k": "v"}
+    assert t["a"].tolist() == [[1, 2, 3]]
+    assert t["b"].tolist() == [1.5, -2.0, 0.25]
+    assert t["c"].dtype == torch.uint32 and t["c"].view(torch.int32).tolist() == [7, -1]
+    assert t["d"].tolist() == [0.5, -1.0]
+
+
+@pytest.mark.parametrize("case", ["short", "header_past_end", "not_json", "bad_dtype", "size_mismatch",
+                                  "out_of_range", "overlap", "extra_key"])
+def test_malformed_files_raise(tmp_path, case):
+    good = {"x": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]},
+            "y": {"dtype": "U8", "shape": [4], "data_offsets": [8, 12]}}
+    data = bytes(12)
+    hdr = json.dumps(good).encode()
+    blob = struct.pack("<Q", len(hdr)) + hdr + data
+    if case == "short":
+        blob = b"\x01\x02"
+    elif case == "header_past_end":
+        blob = struct.pack("<Q", 10 ** 6) + hdr
+    elif case == "not_json":
+        bad = b"{not json"
+        blob = struct.pack("<Q", len(bad)) + bad + data
+    else:
+        h = json.loads(hdr)
+        if case == "bad_dtype":
+            h["x"]["dtype"] = "F8_E9"
+        elif case == "size_mismatch":
+            h["x"]["shape"] = [3]
+        elif case == "out_of_range":
+            h["y"]["data_offsets"] = [8, 13]
+            h["y"]["shape"] = [5]
+        elif case == "overlap":
+            h["y"]["data_offsets"] = [4, 8]
+        elif case == "extra_key":
+            h["x"]["offsets"] = 0
+        hb = json.dumps(h).encode()
+        blob = struct.pack("<Q", len(hb)) + hb + data
+    path = tmp_path / f"{case}.safetensors"
+    path.write_bytes(blob)
+    with pytest.raises(ValueError):
+        ck.read_safetensors(str(path))
+
+
+# ------------------------------------------------------------------ key schema
+
+def test_schema_blocks_thresholds_and_detection(tmp_path):
+    rng = np.random.default_rng(1)
+    w_g = (rng.standard_normal((96, 64)) * 0.02).astype(np.float32)
+    c, blocks = _oracle_blocks(w_g, 0.05)
+    ts = {f"model.layers.0.mlp.gate_proj.saccade_{k}": v for k, v in blocks.items()}
+    ts["model.layers.0.mlp.down_proj.saccade_packed_base"] = blocks["packed_base"]
+    ts["model.layers.0.saccade_t4"] = torch.tensor([2.5], dtype=torch.float32)
+    ts["model.layers.0.saccade_t8"] = torch.tensor([[7.0, 1.0]], dtype=torch.float16)  # flattened, first value
+    ts["model.layers.1.mlp.down_proj.weight"] = torch.zeros(4, 8)
+    path = tmp_path / "s.safetensors"
+    ck.write_safetensors(str(path), ts)
+    t, _ = ck.read_safetensors(str(path))
+    assert ck.is_compressed_layer(t, 0) and not ck.is_compressed_layer(t, 1)
+    assert ck.extract_scalar_f32(t["model.layers.0.saccade_t4"]) == 2.5
+    assert ck.extract_scalar_f32(t["model.layers.0.saccade_t8"]) == 7.0
+    with pytest.raises(KeyError, match="Missing threshold tensor"):
+        ck.extract_scalar_f32(t.get("model.layers.1.saccade_t4"))
+    with pytest.raises(ValueError, match="Empty threshold tensor"):
+        ck.extract_scalar_f32(torch.zeros(0))
+    b, n, k = ck.saccade_blocks(t, "model.layers.0.mlp.gate_proj")
+    assert (n, k) == (96, 64) and set(b) == set(ck.BLOCK_SUFFIXES)
+    assert np.array_equal(b["packed_base"].numpy(), c.packed_base)
+    assert np.array_equal(b["scale_base"].view(torch.int16).numpy().view(np.uint16), c.scale_base)
+    assert np.array_equal(b["delta_row_ptrs"].numpy(), c.delta_row_ptrs)
+    assert np.array_equal(b["delta_col_indices"].numpy(), c.delta_col_indices)
+    assert np.array_equal(b["delta_values"].numpy(), c.delta_values)
+    assert int(b["delta_scale"].view(torch.int16).item()) & 0xFFFF == c.delta_scale
+    with pytest.raises(KeyError, match=r"Missing model.layers.0.mlp.up_proj.saccade_packed_base"):
+        ck.saccade_blocks(t, "model.layers.0.mlp.up_proj")
+    # delta_* read only when delta_row_ptrs exists; then all four are required
+    t2 = {k: v for k, v in t.items() if "gate_proj.saccade_delta" not in k}
+    b2, _, _ = ck.saccade_blocks(t2, "model.layers.0.mlp.gate_proj")
+    assert set(b2) == {"packed_base", "scale_base"}
+    t3 = {k: v for k, v in t.items() if not k.endswith("gate_proj.saccade_delta_values")}
+    with pytest.raises(KeyError, match="saccade_delta_values"):
+        ck.saccade_blocks(t3, "model.layers.0.mlp.gate_proj")
+
+
+def test_compile_follows_the_reference_phase(monkeypatch):
+    # the GPU packer is replaced by the oracle's (bit-identical on the GPU, checked by the
+    # packer parity tests) so that the key handling runs on the CPU
+    from saccade_core import compress as cp
+
+    monkeypatch.setattr(cp, "compute_percentile_threshold", lambda w, f: O.percentile_threshold(w.numpy(), f))
+    monkeypatch.setattr(cp, "compress_tensor_to_saccade", lambda w, thr: _oracle_blocks_thr(w.numpy(), thr))
+    rng = np.random.default_rng(2)
+    model = _tiny_model(rng)
+    model["model.layers.1.mlp.up_proj.weight"] = torch.zeros(96, 60)      # K % 8 != 0: kept as is
+    del model["model.layers.2.mlp.gate_proj.weight"]                       # missing: skipped
+    model["model.layers.3.mlp.down_proj.weight"] = torch.zeros(8, 8)       # beyond num_layers: dropped
+    msgs = []
+    out = ck.compile_mlp_checkpoint(model, 3, 8.0, 64.0, 0.01, log=msgs.append)
+    assert any("missing model.layers.2.mlp.gate_proj.weight" in m for m in msgs)
+    assert any("model.layers.1.mlp.up_proj.weight has incompatible shape [96, 60]" in m for m in msgs)
+    for k in ("model.embed_tokens.weight", "model.norm.weight", "model.layers.0.self_attn.q_proj.bias"):
+        assert out[k] is model[k]
+    assert "model.layers.3.mlp.down_proj.weight" not in out
+    assert out["model.layers.1.mlp.up_proj.weight"] is model["model.layers.1.mlp.up_proj.weight"]
+    for i in range(3):
+        assert out[f"model.layers.{i}.saccade_t4"].dtype == torch.float32
+        assert out[f"model.layers.{i}.saccade_t4"].tolist() == [8.0]
+        assert out[f"model.layers.{i}.saccade_t8"].tolist() == [64.0]
+    assert "model.layers.0.mlp.gate_proj.weight" not in out
+    w = model["model.layers.0.mlp.down_proj.weight"].numpy()
+    c, _ = _oracle_blocks(w, 0.01)
+    assert np.array_equal(out["model.layers.0.mlp.down_proj.saccade_packed_base"].numpy(), c.packed_base)
+    assert np.array_equal(out["model.layers.0.mlp.down_proj.saccade_delta_values"].numpy(), c.delta_values)
+    assert "model.layers.2.mlp.gate_proj.saccade_packed_base" not in out
+    assert "model.layers.2.mlp.up_proj.saccade_packed_base" in out
+
+
+def _oracle_blocks_thr(w, thr):
+    c = O.compress(w, thr)
+    b = {"packed_base": torch.from_numpy(c.packed_base.copy()),
+         "scale_base": torch.from_numpy(c.scale_base.view(np.float16).copy())}
+    if c.nnz:
+        b["delta_row_ptrs"] = torch.from_numpy(c.delta_row_ptrs.copy())
+        b["delta_col_indices"] = torch.from_numpy(c.delta_col_indices.copy())
+        b["delta_values"] = torch.from_numpy(c.delta_values.copy())
+        b["delta_scale"] = torch.tensor([c.delta_scale], dtype=torch.int16).view(torch.float16)
+    return b
+
+
+# ------------------------------------------------------------------ loader on the GPU
+
+@pytest.mark.gpu
+def test_checkpoint_ops_match_the_oracle(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import saccade_core as sc
+
+    rng = np.random.default_rng(3)
+    hidden, inter = 256, 384
+    model = _tiny_model(rng, layers=2, hidden=hidden, inter=inter)
+    # compiled on the GPU packer, then written and read back as a file
+    compiled = sc.compile_mlp_checkpoint(model, 1, 8.0, 1e30, 0.02, device="cuda:0")
+    # compile drops the MLP weights of layers past num_layers; put layer 1 back dense
+    compiled.update({k: v for k, v in model.items() if k.startswith("model.layers.1.mlp.")})
+    path = tmp_path / "m.safetensors"
+    sc.write_safetensors(str(path), compiled)
+    mlps, rest = sc.load_saccade_checkpoint(str(path), 2, device="cuda:0", mode="exact")
+    assert mlps[1] is None and "model.layers.1.mlp.gate_proj.weight" in rest  # layer 1 stays dense
+    assert "model.layers.0.mlp.gate_proj.saccade_packed_base" not in rest
+    m = 5
+    x = rng.standard_normal((m, hidden)).astype(np.float32)
+    x[2] *= 8.0  # one token above t4
+    xb = x.astype(np.float16).view(np.uint16)
+    xg = torch.from_numpy(xb.view(np.float16)).to("cuda:0")
+    mlp = mlps[0]
+    for name, op in (("gate_proj", mlp.gate_proj), ("up_proj", mlp.up_proj)):
+        w = model[f"model.layers.0.mlp.{name}.weight"].numpy()
+        c = O.compress(w, O.percentile_threshold(w, 0.02))
+        ref = O.OracleLinear(c, 8.0, 1e30)
+        yr, rr, _ = ref.forward(xb)
+        y = op.forward(xg)
+        torch.cuda.synchronize()
+        assert np.array_equal(y.cpu().numpy().view(np.uint16), yr), name
+        assert rr.tolist() == [False, False, True, False, False]
+    # the MLP composes the three ops (gate and up as one grouped launch)
+    g = mlp.gate_proj.forward(xg).float()
+    u = mlp.up_proj.forward(xg).float()
+    h = (torch.nn.functional.silu(g) * u).to(torch.float16)  # f32 between the ops, as the f32 model
+    want = mlp.down_proj.forward(h)
+    got = mlp.forward(xg)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
