@@ -64,6 +64,8 @@ def parse():
                          "fractions (one GPU) and write a markdown table to PATH")
     ap.add_argument("--sweep-fills", default=None, metavar="LIST",
                     help="comma-separated dW densities for --sweep (default: --fill)")
+    ap.add_argument("--sweep-tokens", default=None, metavar="LIST",
+                    help="comma-separated token counts for --sweep (default: 1,4,16,64,256,1024,4096)")
     return ap.parse_args()
 
 
@@ -519,6 +521,7 @@ def run_sweep(args):
     except (OSError, ValueError, KeyError):
         pass
     fills = [float(v) for v in args.sweep_fills.split(",")] if args.sweep_fills else [args.fill]
+    tokens = [int(v) for v in args.sweep_tokens.split(",")] if args.sweep_tokens else SWEEP_TOKENS
     rows = []
     for fill, (label, n, k) in [(f, sh) for f in fills for sh in SWEEP_SHAPES]:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
@@ -537,7 +540,7 @@ def run_sweep(args):
                                   mode=args.mode) for _ in range(pool)]
         real_nnz = ops[0].delta_nnz
         del packed, scale, flat, rr, cc, rp, vals, sp
-        for m in SWEEP_TOKENS:
+        for m in tokens:
             y = torch.empty((m, n), dtype=torch.float16, device=dev)
             for frac in SWEEP_ROUTED:
                 r = int(round(frac * m))
@@ -583,6 +586,7 @@ def run_sweep(args):
         f.write(f"# C-TARQ linear: single-call sweep ({args.mode} mode, f16 x)\n\n")
         f.write("Command: `python bench.py --sweep " + args.sweep + (f" --mode {args.mode}" if args.mode != "fast" else "")
                 + (f" --sweep-fills {args.sweep_fills}" if args.sweep_fills else "")
+                + (f" --sweep-tokens {args.sweep_tokens}" if args.sweep_tokens else "")
                 + (f" --fill {args.fill}" if not args.sweep_fills and args.fill != 0.01 else "") + "`\n\n")
         f.write(f"Peaks: HBM {hbm} GB/s, bf16 dense {tc} TFLOP/s (MEASURED_PEAKS.json). `bound` is the larger of "
                 "bytes/HBM and flops/tensor; `frac` = that bound time / measured time. Routed = fraction of "

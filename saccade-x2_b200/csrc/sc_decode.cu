@@ -813,23 +813,27 @@ __device__ __forceinline__ void fused_aux_front(const FusedCtx& c, int at, float
         const int8_t* bval = reinterpret_cast<const int8_t*>(c.dws + 272 + ((n * 2 + 15) / 16) * 16);
         for (int e = roff[at]; e < roff[at + 1]; ++e) add_entry(bcol[e], bval[e]);
     } else if (c.use_blk) {
-        // the same block read in place: 8 entries loaded before they are added (same order)
-        const unsigned char* blk = fp.dwblk + fp.dwoff[c.bid];
+        // the same block read in place (same order), pulled into L2 in one bulk prefetch now that
+        // a token is routed; B entries loaded before they are added
+        constexpr int B = 8;
+        const uint32_t o0 = fp.dwoff[c.bid];
+        const unsigned char* blk = fp.dwblk + o0;
+        if (at == 0) bulk_prefetch_l2(blk, fp.dwoff[c.bid + 1] - o0);
         const uint16_t* roff = reinterpret_cast<const uint16_t*>(blk);
         const int n = roff[128];
         const uint16_t* bcol = reinterpret_cast<const uint16_t*>(blk + 272);
         const int8_t* bval = reinterpret_cast<const int8_t*>(blk + 272 + ((n * 2 + 15) / 16) * 16);
         const int e1 = roff[at + 1];
-        for (int e = roff[at]; e < e1; e += 8) {
-            const int cnt = e1 - e < 8 ? e1 - e : 8;
-            int cc[8], vv[8];
+        for (int e = roff[at]; e < e1; e += B) {
+            const int cnt = e1 - e < B ? e1 - e : B;
+            int cc[B], vv[B];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < B; ++u) {
                 cc[u] = u < cnt ? static_cast<int>(__ldg(bcol + e + u)) : 0;
                 vv[u] = u < cnt ? static_cast<int>(__ldg(bval + e + u)) : 0;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < B; ++u)
                 if (u < cnt) add_entry(cc[u], static_cast<int8_t>(vv[u]));
         }
     } else {

@@ -163,6 +163,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 
 // Non-multicast bulk copy global -> this CTA's shared memory, completing on `bar`.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
+// [gsrc, gsrc + bytes) into L2 (address 16-byte aligned, bytes a multiple of 16); no completion.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gsrc), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
