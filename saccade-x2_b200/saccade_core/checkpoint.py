@@ -95,10 +95,13 @@ def read_safetensors(path: str) -> Tuple[Dict[str, torch.Tensor], Dict[str, str]
         tag = ent["dtype"]
         if tag not in _DTYPES:
             raise ValueError(f"{path}: {name}: unsupported dtype {tag!r}")
-        shape = ent["shape"]
-        b, e = ent["data_offsets"]
-        if not all(isinstance(d, int) and d >= 0 for d in shape) or not (0 <= b <= e <= nbytes):
-            raise ValueError(f"{path}: {name}: bad shape {shape} or offsets [{b}, {e}) (data is {nbytes} B)")
+        shape, offs = ent["shape"], ent["data_offsets"]
+        if (not isinstance(shape, list) or not all(isinstance(d, int) and d >= 0 for d in shape)
+                or not isinstance(offs, list) or len(offs) != 2 or not all(isinstance(o, int) for o in offs)):
+            raise ValueError(f"{path}: {name}: shape {shape!r} or data_offsets {offs!r} malformed")
+        b, e = offs
+        if not 0 <= b <= e <= nbytes:
+            raise ValueError(f"{path}: {name}: offsets [{b}, {e}) outside the {nbytes} B of data")
         itemsize = np.dtype(_DTYPES[tag][0]).itemsize
         if int(np.prod(shape, dtype=np.int64)) * itemsize != e - b:
             raise ValueError(f"{path}: {name}: shape {shape} x {itemsize} B != {e - b} B of data")
@@ -253,7 +256,8 @@ def load_saccade_checkpoint(source, num_layers: Optional[int] = None, *, device=
     else:
         tensors = dict(source)
     if num_layers is None:
-        idx = {int(k.split(".")[2]) for k in tensors if k.startswith("model.layers.") and k.split(".")[2].isdigit()}
+        parts = (k.split(".") for k in tensors if k.startswith("model.layers."))
+        idx = {int(p[2]) for p in parts if len(p) > 2 and p[2].isdigit()}
         num_layers = max(idx) + 1 if idx else 0
     mlps, used = [], set()
     for i in range(num_layers):

@@ -107,7 +107,7 @@ def test_reads_a_file_assembled_from_the_format(tmp_path):
 
 
 @pytest.mark.parametrize("case", ["short", "header_past_end", "not_json", "bad_dtype", "size_mismatch",
-                                  "out_of_range", "overlap", "extra_key"])
+                                  "out_of_range", "overlap", "extra_key", "shape_not_list", "offsets_short"])
 def test_malformed_files_raise(tmp_path, case):
     good = {"x": {"dtype": "F32", "shape": [2], "data_offsets": [0, 8]},
             "y": {"dtype": "U8", "shape": [4], "data_offsets": [8, 12]}}
@@ -134,6 +134,10 @@ def test_malformed_files_raise(tmp_path, case):
             h["y"]["data_offsets"] = [4, 8]
         elif case == "extra_key":
             h["x"]["offsets"] = 0
+        elif case == "shape_not_list":
+            h["x"]["shape"] = 2
+        elif case == "offsets_short":
+            h["x"]["data_offsets"] = [0]
         hb = json.dumps(h).encode()
         blob = struct.pack("<Q", len(hb)) + hb + data
     path = tmp_path / f"{case}.safetensors"
@@ -180,6 +184,20 @@ def test_schema_blocks_thresholds_and_detection(tmp_path):
     t3 = {k: v for k, v in t.items() if not k.endswith("gate_proj.saccade_delta_values")}
     with pytest.raises(KeyError, match="saccade_delta_values"):
         ck.saccade_blocks(t3, "model.layers.0.mlp.gate_proj")
+
+
+def test_loader_on_a_dense_checkpoint(tmp_path):
+    # no saccade_* keys: every layer stays dense and every tensor is handed back
+    rng = np.random.default_rng(4)
+    model = _tiny_model(rng, layers=2)
+    model["model.layers"] = torch.zeros(1)  # a key without a layer index is not a layer
+    path = tmp_path / "dense.safetensors"
+    ck.write_safetensors(str(path), model)
+    mlps, rest = ck.load_saccade_checkpoint(str(path))
+    assert mlps == [None, None]
+    assert set(rest) == set(model)
+    mlps, _ = ck.load_saccade_checkpoint(model, 4)
+    assert mlps == [None] * 4
 
 
 def test_compile_follows_the_reference_phase(monkeypatch):
