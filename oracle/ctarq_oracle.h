@@ -2,8 +2,8 @@
  * ctarq_oracle.h -- CPU oracle for the C-TARQ linear path (TEST INFRASTRUCTURE).
  *
  * This is a plain-C restatement of saccade-core's CPU implementation of the
- * C-TARQ linear operator.  It is the checker for the CUDA library, never the
- * thing that ships: only tests/, __graft_entry__.smoke() and the CPU-baseline
+ * C-TARQ linear operator.  Tests compare the CUDA library against it; it is never
+ * the thing that ships: only tests/, __graft_entry__.smoke() and the CPU-baseline
  * leg of bench.py may load it.
  *
  * Parity status: UNPINNED.  The reference is Rust-only, its Candle substrate
