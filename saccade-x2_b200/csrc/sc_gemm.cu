@@ -44,7 +44,10 @@
 
 namespace sc {
 
-constexpr int kFoldCap = 4096;  // bytes of one block's dW list in a ring stage (~10 % dW on average)
+// Bytes of one block's dW list slot in a ring stage: 4 KB (~10 % dW on average) in every
+// variant, 8 KB (~23 %) in a one-row-tile variant for layers whose lists need it.
+constexpr int kFoldCap = 4096;
+constexpr int kFoldCapWide = 8192;
 constexpr int kFoldHdr = 528;   // its header: u16 entry offsets [8 tiles of 16 rows][33 lanes + end]
 
 struct GemmParams {
@@ -76,9 +79,9 @@ struct GemmParams {
     uint32_t* status;
 };
 
-// RPC: 128-row tiles per CTA (1, or 2 sharing every x block); the ring, the tensor memory and
-// every index are compile-time for each.
-template <int RPC>
+// RPC: 128-row tiles per CTA (1, or 2 sharing every x block); FC: bytes of a dW list slot.  The
+// ring, the tensor memory and every index are compile-time for each.
+template <int RPC, int FC = kFoldCap>
 struct GemmCfg {
     static constexpr int NT = 128;                   // tokens per tile (MMA N)
     static constexpr int kRowTiles = RPC;
@@ -90,10 +93,11 @@ struct GemmCfg {
     static constexpr int SKB = 2;                    // 64-column blocks per ring stage
     static constexpr int S = RPC == 1 ? 4 : 3;       // ring stages
     // A stage holds [row tile][block] 4 KB weights, the blocks' x (16 KB each), then [row tile]
-    // [block] dW lists: 48 KB with one row tile, 64 KB with two.
+    // [block] dW lists: 48 KB with one row tile, 64 KB with two (56 KB with one and 8 KB slots).
+    static constexpr int kFold = FC;
     static constexpr int kWBytes = RPC * SKB * 4096;
     static constexpr int kXBytes = SKB * G * 1024;
-    static constexpr int kFBytes = RPC * SKB * kFoldCap;
+    static constexpr int kFBytes = RPC * SKB * kFold;
     static constexpr int kStageBytes = kWBytes + kXBytes + kFBytes;
     static constexpr int kAB = 4;                    // TMEM A buffers per row tile, one block (32 columns) each
     static constexpr uint32_t kTmemCols = RPC == 1 ? 256 : 512;  // D of row tile t at t*128, A after the D's
@@ -102,6 +106,7 @@ struct GemmCfg {
     static constexpr int kTmemSlotOff = kBarOff + kNumBars * 8;
     static constexpr int kTotal = kTmemSlotOff + 16;
     static_assert(RPC == 1 || RPC == 2, "row tiles per CTA");
+    static_assert(FC % 16 == 0 && (kStageBytes % 1024) == 0, "list slots keep the x tiles 1 KB aligned");
     static_assert(RPC * NT + RPC * kAB * 32 <= static_cast<int>(kTmemCols), "tensor memory");
     static_assert(kTotal <= 227 * 1024, "shared memory");
 };
@@ -155,9 +160,9 @@ __device__ __forceinline__ GemmTile gemm_tile(const GemmParams& p, int64_t tt) {
     return g;
 }
 
-template <int RPC>
-__global__ void __launch_bounds__(GemmCfg<RPC>::kThreads, 1) k_ctarq_gemm(GemmParams p) {
-    using C = GemmCfg<RPC>;
+template <int RPC, int FC>
+__global__ void __launch_bounds__(GemmCfg<RPC, FC>::kThreads, 1) k_ctarq_gemm(GemmParams p) {
+    using C = GemmCfg<RPC, FC>;
     constexpr int SKB = C::SKB, AB = C::kAB, NT = C::NT, G = C::G, S = C::S;
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
@@ -273,7 +278,7 @@ __global__ void __launch_bounds__(GemmCfg<RPC>::kThreads, 1) k_ctarq_gemm(GemmPa
                         for (int r = 0; r < nrt; ++r) {
                             const int64_t li = (rt0 + r) * p.KB + kb0 + j;
                             const uint32_t o0 = p.foldoff[li], o1 = p.foldoff[li + 1];
-                            bulk_g2s(st + kF + (r * SKB + j) * kFoldCap, p.fold + o0, o1 - o0,
+                            bulk_g2s(st + kF + (r * SKB + j) * C::kFold, p.fold + o0, o1 - o0,
                                      &full[slot]);
                         }
                     }
@@ -340,7 +345,7 @@ __global__ void __launch_bounds__(GemmCfg<RPC>::kThreads, 1) k_ctarq_gemm(GemmPa
             for (int st = 0; st < 4; ++st) dequant_word(words[st], hh[st]);
             if (fold) {
                 // this lane's entries of the block (register slot, half, f16 dW/s)
-                const unsigned char* lst = stg + kF + (r * SKB + kbl) * kFoldCap;
+                const unsigned char* lst = stg + kF + (r * SKB + kbl) * C::kFold;
                 const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + tile * 33 + lane;
                 const uint32_t* ent = reinterpret_cast<const uint32_t*>(lst + kFoldHdr);
                 const int e1 = offs[1];
@@ -517,8 +522,10 @@ __global__ void k_gather_tokens(const uint16_t* __restrict__ xk, uint16_t* __res
 int64_t gemm_tile_tokens() { return GemmCfg<1>::NT; }
 
 // Row tiles per CTA: two (sharing every x block, half the x traffic per MMA) while the grid of
-// pairs still fills every SM once, else one (more CTAs, a deeper ring).
+// pairs still fills every SM once, else one (more CTAs, a deeper ring).  Layers whose dW lists
+// need the 8 KB slots take one (two row tiles would not fit the shared memory).
 static int gemm_rows_per_cta(const Layer& L, int64_t m) {
+    if (L.fold != nullptr && L.fold_cap > kFoldCap) return 1;
     const int64_t pairs = (L.Np / 128 + 1) / 2 * ((m + GemmCfg<1>::NT - 1) / GemmCfg<1>::NT);
     return pairs >= L.sms ? 2 : 1;
 }
@@ -572,16 +579,17 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     cudaError_t e = launch_pdl(k_gather_tokens, dim3(static_cast<unsigned>(gblocks)), dim3(256), 0, s,
                                a.xk, a.xkp, a.perm, a.nrouted, a.route_all, a.M, a.Mp, a.Mpp, L.KB);
     if (e != cudaSuccess) return e;
-    static std::atomic<uint64_t> flags[2] = {{0}, {0}};
+    static std::atomic<uint64_t> flags[3] = {{0}, {0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
-    auto kern = p.rpc == 2 ? k_ctarq_gemm<2> : k_ctarq_gemm<1>;
-    const int smem = p.rpc == 2 ? GemmCfg<2>::kTotal : GemmCfg<1>::kTotal;
-    if (!(flags[p.rpc - 1].load() & bit)) {
+    const int var = p.rpc == 2 ? 1 : (L.fold != nullptr && L.fold_cap > kFoldCap) ? 2 : 0;
+    auto kern = var == 1 ? k_ctarq_gemm<2, kFoldCap> : var == 2 ? k_ctarq_gemm<1, kFoldCapWide> : k_ctarq_gemm<1, kFoldCap>;
+    const int smem = var == 1 ? GemmCfg<2>::kTotal : var == 2 ? GemmCfg<1, kFoldCapWide>::kTotal : GemmCfg<1>::kTotal;
+    if (!(flags[var].load() & bit)) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        flags[p.rpc - 1].fetch_or(bit);
+        flags[var].fetch_or(bit);
     }
     return launch_pdl(kern, dim3(static_cast<unsigned>(p.RTP * p.T * p.ks)), dim3(GemmCfg<1>::kThreads), smem, s, p);
 }
@@ -590,14 +598,16 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
 // (row tile, block), a header of u16 entry offsets [16-row tile][lane 0..32] (kFoldHdr bytes;
 // entry o[t][l] .. o[t][l+1] belong to lane l of tile t), then one u32 per entry, grouped by
 // (tile, lane): bits 0-4 the lane (4 g + c) holding the weight in the dequantised fragment, 5-8
-// the register slot (step * 4 + register), 9 the half, 16-31 the f16 of dW/s.  Left empty (no
-// fold: the GEMM adds dW in its epilogue) when a list exceeds its shared-memory slot or a value
-// is not representable.
+// the register slot (step * 4 + register), 9 the half, 16-31 the f16 of dW/s.  The slot size
+// (L.fold_cap) is the smaller of 4 KB and 8 KB that holds every list.  Left empty (no fold: the
+// GEMM adds dW in its epilogue) when a list exceeds 8 KB or a value is not representable.
 cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol, const int8_t* sval,
                              const float* scale) {
     L.fold = nullptr;
     L.foldoff = nullptr;
+    L.fold_cap = 0;
     if (L.nnz == 0) return cudaSuccess;
+    size_t max_bytes = 0;
     const int64_t RT = L.Np / 128, KB = L.KB;
     std::vector<uint32_t> off(RT * KB + 1, 0);
     std::vector<uint8_t> blob;
@@ -628,7 +638,8 @@ cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol
             size_t n = 0;
             for (int t = 0; t < 8 * 32; ++t) n += per[kb * 256 + t].size();
             const size_t bytes = ((kFoldHdr + 4 * n) + 15) / 16 * 16;
-            if (bytes > static_cast<size_t>(kFoldCap)) return cudaSuccess;
+            if (bytes > static_cast<size_t>(kFoldCapWide)) return cudaSuccess;
+            max_bytes = std::max(max_bytes, bytes);
             const size_t at = blob.size();
             blob.resize(at + bytes, 0);
             uint16_t hdr[kFoldHdr / 2] = {};
@@ -659,6 +670,7 @@ cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol
     }
     L.fold = dblob;
     L.foldoff = doff;
+    L.fold_cap = max_bytes <= static_cast<size_t>(kFoldCap) ? kFoldCap : kFoldCapWide;
     L.device_bytes += static_cast<int64_t>(blob.size() + off.size() * 4);
     return cudaSuccess;
 }

@@ -54,6 +54,7 @@ struct Layer {
     // tokens' tiles fold it into the dequantised weights ((q - 8) + dW/s, see sc_gemm.cu).
     uint8_t* fold = nullptr;     // lists, each [9 u16 offsets per 16-row tile | pad to 32 B | u32 entries]
     uint32_t* foldoff = nullptr; // byte offset of list (rt * KB + kb); [RT*KB + 1]; null: no fold
+    int fold_cap = 0;            // shared-memory slot of one list: 4096 or 8192 bytes
 };
 
 // Shared-memory budget of one dW block in the fused decode kernel.

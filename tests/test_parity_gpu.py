@@ -281,6 +281,8 @@ def test_qwen2_7b_shapes(sc, n, k, m, mode):
     (96, 128, 20, 20, 1.0),        # dense dW: lists too long to fold, dW in the epilogue
     (4864, 896, 1100, 300, 0.01),  # enough tiles for two row tiles per CTA
     (4736, 512, 1100, 400, 0.02),  # two row tiles per CTA, the last CTA holding one
+    (300, 3584, 300, 300, 0.15),   # 15 % dW (the compile default): ~5.4 KB lists, the 8 KB-slot variant
+    (300, 3584, 300, 200, 0.15),   # the same with a mixed and an unrouted tile
 ])
 def test_prefill_gemm_routing(sc, n, k, m, nroute, fill):
     rng = np.random.default_rng(n + m + nroute)
