@@ -44,7 +44,7 @@ T8_NEVER = float(np.finfo(np.float32).max)
 METRIC = "C-TARQ linear effective HBM GB/s"
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -66,7 +66,7 @@ def parse():
                     help="comma-separated dW densities for --sweep (default: --fill)")
     ap.add_argument("--sweep-tokens", default=None, metavar="LIST",
                     help="comma-separated token counts for --sweep (default: 1,4,16,64,256,1024,4096)")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def launches_per_call(args):
@@ -115,6 +115,14 @@ def stack_spec(layers, m, route_frac, seed):
                 boosted_of[inp] = [t for t in range(m) if rng.random() < route_frac]
             calls.append((li, name, n, k, boosted_of[inp]))
     return calls
+
+
+def workload_config(args, calls, step_bytes):
+    """The workload keys both arms report: the same stack of calls, sizes and routing."""
+    return {"workload": "qwen2-7b decoder linear stack, decode", "tokens": args.tokens, "layers": args.layers,
+            "calls_per_step": len(calls), "routed_calls_per_step": sum(1 for c in calls if c[4]),
+            "dw_fill": args.fill, "route_frac": args.route_frac, "bytes_per_step": step_bytes,
+            "weights": "int4 base + i8 dW, f32 accumulation"}
 
 
 def synth_compressed_np(n, k, fill, rng):
@@ -266,6 +274,7 @@ def run_reference(args, rank):
     calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234)
     items = build_oracle_stack(calls, args.fill, 99, args.tokens)
     step_bytes = sum(b for _, _, b in items)
+    config = workload_config(args, calls, step_bytes)
     # one step is bounded: if the whole stack takes too long on this host, time a prefix of it
     _, dt1 = time_oracle(items[: 7], 1, native)
     per_step_est = dt1 * len(items) / 7
@@ -286,8 +295,7 @@ def run_reference(args, rank):
     out = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-           "config": {"workload": "qwen2-7b decoder linear stack, decode", "tokens": args.tokens,
-                      "layers": args.layers, "dw_fill": args.fill, "route_frac": args.route_frac},
+           "config": config,
            "impl": "reference",
            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
                             "sample": sample},
@@ -309,7 +317,6 @@ def run_ours(args, rank, world):
     gen.manual_seed(1000 + rank)
     calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234 + rank)
     ops, xs, step_bytes, big = [], [], 0, []
-    routed_calls = 0
     x_of = {}  # (layer, input) -> activations shared by the calls that read them
     for li, name, n, k, boosted in calls:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
@@ -334,7 +341,6 @@ def run_ours(args, rank, world):
             x_of[key] = x.to(torch.float16)
         x = x_of[key]
         b = call_bytes(n, k, args.tokens, op.delta_nnz, len(boosted) > 0)
-        routed_calls += len(boosted) > 0
         ops.append(op)
         xs.append(x)
         step_bytes += b
@@ -469,10 +475,8 @@ def run_ours(args, rank, world):
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "qwen2-7b decoder linear stack, decode", "tokens": args.tokens,
-                   "layers": args.layers, "calls_per_step": len(ops), "routed_calls_per_step": routed_calls,
-                   "dw_fill": args.fill, "mode": args.mode, "bytes_per_step": step_bytes,
-                   "weights": "int4 base + i8 dW, f32 accumulation", "l2": "inputs > L2 (3.3 GB of weights)",
+        "config": {**workload_config(args, calls, step_bytes), "mode": args.mode,
+                   "l2": "inputs > L2 (3.3 GB of weights)",
                    "parallelism": f"replicas{world}", "graph": "one CUDA graph per step",
                    "launch_units": "q,k,v and gate,up grouped (sc_forward_group)" if not args.no_group
                    else "one launch per projection", "launches_per_step": launches_per_step(args, units)},
