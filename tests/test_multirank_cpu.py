@@ -92,3 +92,112 @@ def test_row_shards_all_reduce_two_ranks():
         for m in masks:
             assert np.array_equal(m, rr)
     assert np.array_equal(results[0][1], results[1][1]), "every rank holds the same reduced sum"
+
+
+# ------------------------------------------------------------------ tensor-parallel MLP, two ranks
+
+def row_slice(c, r0, r1):
+    """The layer restricted to output rows [r0, r1) (what a COLUMNS shard keeps: rows move with
+    their scales and their dW)."""
+    from oracle import oracle as O
+    lo, hi = int(c.delta_row_ptrs[r0]), int(c.delta_row_ptrs[r1])
+    rp = (c.delta_row_ptrs[r0:r1 + 1] - lo).astype(np.uint32)
+    return O.Compressed(np.ascontiguousarray(c.packed_base[r0:r1]), np.ascontiguousarray(c.scale_base[r0:r1]), rp,
+                        np.ascontiguousarray(c.delta_col_indices[lo:hi]), np.ascontiguousarray(c.delta_values[lo:hi]),
+                        c.delta_scale, r1 - r0, c.in_features)
+
+
+def _silu_mul(g_bits, u_bits):
+    """f16(silu(g) * u) in f32: the MLP's step between gate/up and down."""
+    g = g_bits.view(np.float16).astype(np.float32)
+    u = u_bits.view(np.float16).astype(np.float32)
+    return ((g / (np.float32(1.0) + np.exp(-g))) * u).astype(np.float16).view(np.uint16)
+
+
+def _mlp_layers():
+    from oracle import oracle as O
+    rng = np.random.default_rng(91)
+
+    def comp(n, k):
+        w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+        return O.compress(w, O.percentile_threshold(w, 0.03))
+
+    gate, up, down = comp(384, 256), comp(384, 256), comp(256, 384)
+    x = rng.standard_normal((5, 256)).astype(np.float32)
+    x[3] *= 8.0
+    return gate, up, down, x.astype(np.float16).view(np.uint16)
+
+
+def _down_route(h_bits):
+    """Threshold between the unboosted and the boosted token's variance of h, and the mask."""
+    from oracle import oracle as O
+    s = np.array([O.variance(h_bits[t]) for t in range(h_bits.shape[0])])
+    t4 = float(np.sqrt(np.max(np.delete(s, 3)) * s[3]))
+    return t4, (s >= t4).astype(np.uint8)
+
+
+def _mlp_rank(rank, world, port, q):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.dirname(here))
+    from oracle import oracle as O
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gate, up, down, xb = _mlp_layers()
+        inter = gate.out_features
+        r0, r1 = inter * rank // world, inter * (rank + 1) // world
+        # column-parallel gate and up: this rank's rows, x replicated, no exchange
+        g, _, _ = O.OracleLinear(row_slice(gate, r0, r1), 8.0, 3e38).forward(xb)
+        u, _, _ = O.OracleLinear(row_slice(up, r0, r1), 8.0, 3e38).forward(xb)
+        h_part = _silu_mul(g, u)
+        # down routes on the whole token: gather h (the router needs all of K); the f16 bit
+        # patterns travel as int32 (gloo has no 16-bit integer type)
+        parts = [torch.zeros(h_part.shape, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(h_part.astype(np.int32)))
+        h = np.concatenate([p.numpy().astype(np.uint16) for p in parts], axis=1)
+        t4, routed = _down_route(h)
+        # row-parallel down over this rank's K slice, then the sum over ranks
+        _, _, acc = O.OracleLinear(column_slice(down, r0, r1), t4, 3e38).forward(
+            np.ascontiguousarray(h[:, r0:r1]), force_route=routed)
+        t = torch.from_numpy(acc.copy())
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        q.put((rank, g, u, h, routed, t.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_mlp_two_ranks():
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    from oracle import oracle as O
+    from ctarq_cases import assert_acc_close, assert_fast_close
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_mlp_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    gate, up, down, xb = _mlp_layers()
+    g, rg, _ = O.OracleLinear(gate, 8.0, 3e38).forward(xb)
+    u, _, _ = O.OracleLinear(up, 8.0, 3e38).forward(xb)
+    assert rg.tolist() == [0, 0, 0, 1, 0]
+    h = _silu_mul(g, u)
+    t4, routed = _down_route(h)
+    y, rd, acc_ref = O.OracleLinear(down, t4, 3e38).forward(h)
+    assert rd.tolist() == [0, 0, 0, 1, 0]
+    inter = gate.out_features
+    for rank, g_r, u_r, h_r, routed_r, acc in results:
+        r0, r1 = inter * rank // world, inter * (rank + 1) // world
+        assert np.array_equal(g_r, g[:, r0:r1]) and np.array_equal(u_r, u[:, r0:r1]), "rows are independent"
+        assert np.array_equal(h_r, h) and np.array_equal(routed_r, rd)
+        assert_acc_close(acc, acc_ref, f"tp mlp rank {rank}")
+        assert_fast_close(acc.astype(np.float16).view(np.uint16), y, f"tp mlp rank {rank} y")
+    assert np.array_equal(results[0][5], results[1][5]), "every rank holds the same reduced sum"
