@@ -457,7 +457,13 @@ def run_ours(args, rank, world):
     for op in ops[:7]:
         op.check_device()
 
-    value = step_bytes * world / (ms / 1e3) / 1e9
+    # bytes of one step over all ranks (their routed tokens, hence their dW bytes, differ)
+    total_bytes = float(step_bytes)
+    if world > 1:
+        tb = torch.tensor([total_bytes], device=dev, dtype=torch.float64)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        total_bytes = float(tb.item())
+    value = total_bytes / (ms / 1e3) / 1e9
     big_bytes = sum(b for _, b in big)
     achieved = big_bytes / (ms_big / 1e3) / 1e9
     peak, peak_kind = measured_peak()
@@ -487,10 +493,10 @@ def run_ours(args, rank, world):
                      "kernel": launch_kind(args) + f" on the gate/up/down calls ({len(big_units)} launches per step)",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
-        "e2e": {"value": round(step_bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
+        "e2e": {"value": round(total_bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": "one pinned host->device copy of all inputs, the 196 calls, one device->host copy of "
-                       "all outputs; captured step, host sync each step"},
+                "how": f"one pinned host->device copy of all inputs, the {len(ops)} calls, one device->host copy "
+                       "of all outputs; captured step, host sync each step"},
         "gpu_launches": launches_per_step(args, units) * args.steps,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
