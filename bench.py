@@ -317,6 +317,7 @@ def run_ours(args, rank, world):
     gen.manual_seed(1000 + rank)
     calls = stack_spec(args.layers, args.tokens, args.route_frac, seed=1234 + rank)
     ops, xs, step_bytes, big = [], [], 0, []
+    check_src = []
     x_of = {}  # (layer, input) -> activations shared by the calls that read them
     for li, name, n, k, boosted in calls:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
@@ -332,6 +333,9 @@ def run_ours(args, rank, world):
                                   torch.tensor([0.006 / 127.0], dtype=torch.float16))
         op = sc.SaccadeLinearOp(packed, scale, sp, sc.SaccadeConfig(T4_BOOSTED, T8_NEVER), n, k, device=dev,
                                 mode=args.mode)
+        if li == 0 and rank == 0:  # reference-format buffers of the first layer, for the parity check
+            check_src.append((len(ops), packed.cpu(), scale.cpu(), rp.to(torch.int32).cpu(), cols.to(torch.int32).cpu(),
+                              vals.cpu()))
         del packed, scale, flat, rows, cols, rp, vals
         key = (li, INPUT_OF[name])
         if key not in x_of:
@@ -453,9 +457,11 @@ def run_ours(args, rank, world):
     ms_big = timed(g_big, args.steps)
     ms_e2e = timed(g_e2e, args.steps, sync_each=True)
 
-    # correctness guard on the timed configuration: no device-side error recorded
+    # correctness guard on the timed configuration: no device-side error recorded, and the first
+    # layer's seven outputs of the last timed step equal the oracle's on a sample of rows
     for op in ops[:7]:
         op.check_device()
+    parity = check_against_oracle(check_src, ops, xs, ys, calls) if rank == 0 else None
 
     # bytes of one step over all ranks (their routed tokens, hence their dW bytes, differ)
     total_bytes = float(step_bytes)
@@ -498,11 +504,47 @@ def run_ours(args, rank, world):
                 "how": f"one pinned host->device copy of all inputs, the {len(ops)} calls, one device->host copy "
                        "of all outputs; captured step, host sync each step"},
         "gpu_launches": launches_per_step(args, units) * args.steps,
+        "parity_check": parity,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args)
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+def check_against_oracle(check_src, ops, xs, ys, calls, rows_per_call=96):
+    """Compares sampled output rows of the given calls with the oracle on the same inputs (fast-mode
+    tolerance: 1e-3 * RMS + one f16 ulp, router masks identical).  Raises on a mismatch."""
+    import torch
+
+    from oracle import oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    worst = 0.0
+    for idx, packed, scale, rp, cols, vals in check_src:
+        n, k = ops[idx].out_features, ops[idx].in_features
+        rng = np.random.default_rng(idx)
+        rows = np.sort(rng.choice(n, size=min(rows_per_call, n), replace=False))
+        rpn = rp.numpy().astype(np.int64)
+        sel = [np.arange(rpn[r], rpn[r + 1]) for r in rows]
+        ent = np.concatenate(sel) if sel else np.zeros(0, np.int64)
+        ptrs = np.concatenate([[0], np.cumsum([len(e) for e in sel])]).astype(np.uint32)
+        c = O.Compressed(np.ascontiguousarray(packed.numpy().view(np.uint32)[rows]),
+                         np.ascontiguousarray(scale.numpy().view(np.uint16)[rows]), ptrs,
+                         cols.numpy().view(np.uint32)[ent].copy(), vals.numpy()[ent].copy(),
+                         int(np.array([0.006 / 127.0], dtype=np.float16).view(np.uint16)[0]), len(rows), k)
+        xb = xs[idx].cpu().numpy().view(np.uint16)
+        yr, _, _ = O.OracleLinear(c, T4_BOOSTED, T8_NEVER).forward(xb)
+        yg = ys[idx].cpu().numpy().view(np.uint16)[:, rows]
+        a, b = yg.view(np.float16).astype(np.float32), yr.view(np.float16).astype(np.float32)
+        rms = float(np.sqrt(np.mean(b.astype(np.float64) ** 2)))
+        tol = 1e-3 * rms + np.spacing(np.abs(b).astype(np.float16)).astype(np.float32)
+        ratio = float(np.max(np.abs(a - b) / tol))
+        worst = max(worst, ratio)
+        if ratio > 1.0:
+            raise AssertionError(f"bench parity: call {calls[idx][:4]} differs from the oracle "
+                                 f"(max error / tolerance {ratio:.3f})")
+    return {"calls": len(check_src), "rows_per_call": rows_per_call, "max_err_over_tol": round(worst, 4),
+            "tolerance": "1e-3 * RMS(ref) + 1 f16 ulp", "ok": True}
 
 
 SWEEP_SHAPES = [("q/o", 3584, 3584), ("k/v", 512, 3584), ("gate/up", 18944, 3584), ("down", 3584, 18944)]

@@ -127,6 +127,14 @@ SC_API sc_status sc_layer_check(sc_layer* layer, void* stream);
 SC_API void sc_set_bypass_c_tarq(int on);
 SC_API int sc_is_c_tarq_bypassed(void);
 
+/* Test hook for the bounded device waits; no counterpart in the reference.  While on, every
+ * router-fused decode launch of SC_MODE_FAST (one to eight tokens; the mma.sync engines, which
+ * hold no tensor memory) leaves the first weight stage of its first CTA unissued, so the base-product warps' wait on that stage runs out after its bound (2 s):
+ * the kernel records SC_ETIMEOUT in the layer's status word (read by sc_layer_check) and returns
+ * without writing that CTA's outputs.  Nothing faults and the context stays usable.  Leave it
+ * off (0) outside tests. */
+SC_API void sc_test_drop_weight_copy(int on);
+
 /* Workspace bytes sc_forward_ws needs for m tokens on this layer. */
 SC_API size_t sc_workspace_size(const sc_layer* layer, int64_t m);
 
@@ -184,8 +192,9 @@ SC_API sc_status sc_forward_group(const sc_group* group, const void* x, int x_dt
  *  - Each call first zero-fills the array's 64 KiB counter region on the stream.
  *  - One array per device is shared by every call on that device: calls that overlap on the
  *    GPU (several streams or host threads) race and corrupt each other's results.
- *  - The first call on each device looks the array up (cudaGetSymbolAddress, which may load
- *    the module); make that first call before any stream capture begins. */
+ *  - sc_layer_create looks the array up on its device (cudaGetSymbolAddress, which may load
+ *    the module), so sc_forward_static itself loads nothing; the address is kept for the life
+ *    of the process, so a cudaDeviceReset invalidates it (create the layers again after one). */
 #define SC_STATIC_SCRATCH_BYTES (8u * 1024u * 1024u)
 SC_API sc_status sc_forward_static(const sc_layer* layer, const void* x, int x_dtype, int64_t m,
                             void* y, int y_dtype, const float* bias,

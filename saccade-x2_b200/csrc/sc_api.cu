@@ -440,6 +440,8 @@ size_t sc_last_error(char* buf, size_t len) {
 }
 
 void sc_set_bypass_c_tarq(int on) { g_bypass.store(on ? 1 : 0); }
+
+void sc_test_drop_weight_copy(int on) { set_drop_weight_copy(on); }
 int sc_is_c_tarq_bypassed(void) { return g_bypass.load(); }
 
 static void free_layer(Layer& L) {
@@ -688,6 +690,16 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     if (e != cudaSuccess) {
         free_layer(L);
         return cuda_fail(e, "sc_layer_create: device layout");
+    }
+    {
+        // look up sc_forward_static's scratch array now, so that its first call on this device
+        // neither loads the module (which places the array) nor takes the lookup's lock
+        void* scratch = nullptr;
+        const sc_status st = static_scratch(L.device, &scratch);
+        if (st != SC_OK) {
+            free_layer(L);
+            return st;
+        }
     }
     sc_layer* layer = new sc_layer;
     layer->L = L;

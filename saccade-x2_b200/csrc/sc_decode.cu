@@ -346,6 +346,8 @@ struct FusedParams {
                             // it, and the one-token kernels route on their own sums (no exchange)
     RouteConsts rc;         // of Kfull
     double gT;              // bound factor of this kernel's own f32 sums (gamma of their depth, doubled)
+    int drop_copy;          // test hook (sc_test_drop_weight_copy): CTA 0 never issues its first weight
+                            // stage, so the base-product warps' bounded wait on it runs out
 };
 
 // Up to kGroupMax layers reading the same x in one launch: layer i owns the CTAs
@@ -505,6 +507,7 @@ __device__ __forceinline__ int fused_produce(const FusedCtx& c, unsigned char* r
     for (int it = 0; it < pre; ++it, ++issued) {
         const int64_t kb0 = c.kb_begin + static_cast<int64_t>(it) * SKB;
         const int n = static_cast<int>(imin64(SKB, c.kb_end - kb0));
+        if (it == 0 && c.bid == 0 && c.fp->drop_copy) continue;  // nothing ever completes this stage
         mbar_arrive_expect_tx(&full[it], static_cast<uint32_t>(n * 4096));
         bulk_g2s_stream(ring + it * kStage, p.wq + (c.rt * p.KB + kb0) * 1024, static_cast<uint32_t>(n * 4096),
                         &full[it], pol);
@@ -1552,6 +1555,10 @@ __global__ void __launch_bounds__(128) k_decode_exact(ExactParams p) {
     }
 }
 
+// Test hook behind sc_test_drop_weight_copy (0: off).
+static std::atomic<int> g_drop_copy{0};
+void set_drop_weight_copy(int on) { g_drop_copy.store(on ? 1 : 0); }
+
 static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     const Layer& L = *f.L;
     TCParams& p = fp.t;
@@ -1594,6 +1601,7 @@ static void fill_fused_params(const FusedArgs& f, FusedParams& fp) {
     fp.dw_global = f.dw_global;
     fp.ntp = f.m <= 1 ? 1 : f.m <= 2 ? 2 : f.m <= 4 ? 4 : 8;
     fp.rc = route_consts(fp.Kfull);
+    fp.drop_copy = g_drop_copy.load();
     // each auxiliary thread adds at most T values sequentially in f32 (both passes), then five
     // shuffle levels add partial sums; the bound uses the depth, doubled for safety
     const int64_t ks = p.ksplit;
@@ -1633,6 +1641,8 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s) {
     bool i8 = SC_FUSED_INT8 && f[0].L->mode == SC_MODE_FAST && f[0].m == 1;
     for (int i = 0; i < n && i8; ++i) i8 = (f[i].L->KB + ksplit - 1) / ksplit <= FusedRegions::kMaxKbI8;
     const int which = f8 ? 2 : tc ? 1 : i8 ? 3 : 0;
+    if (tc || f8)  // the test hook only reaches the mma.sync engines, which hold no tensor memory
+        for (int i = 0; i < n; ++i) g.p[i].drop_copy = 0;
     auto kern = f8 ? k_ctarq_fused_tc<true> : tc ? k_ctarq_fused_tc<false> : i8 ? k_ctarq_fused_mma<true> : k_ctarq_fused_mma<false>;
     const int threads = f8 ? FusedTcCfg<true>::kThreads : tc ? FusedTcCfg<false>::kThreads : FusedMmaCfg::kThreads;
     const int smem = f8 ? FusedTcCfg<true>::kTotal : tc ? FusedTcCfg<false>::kTotal : FusedMmaCfg::kTotal;

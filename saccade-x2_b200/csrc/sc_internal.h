@@ -220,6 +220,9 @@ int fused_max_active_clusters(int ks);
 int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
 int64_t fused_prefetch_bytes();  // weight bytes the fused kernel prefetches with one CTA on every SM
 
+// Test hook: the next router-fused decode launches leave CTA 0's first weight stage unissued.
+void set_drop_weight_copy(int on);
+
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                             cudaStream_t s);
 

@@ -87,6 +87,7 @@ SIGNATURES = {
     "sc_layer_check": (_int, [_vp, _vp]),
     "sc_set_bypass_c_tarq": (None, [_int]),
     "sc_is_c_tarq_bypassed": (_int, []),
+    "sc_test_drop_weight_copy": (None, [_int]),
     "sc_workspace_size": (ctypes.c_size_t, [_vp, _i64]),
     "sc_forward": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "sc_forward_ws": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),

@@ -76,3 +76,21 @@ def assert_acc_close(acc_gpu: np.ndarray, acc_ref: np.ndarray, what: str = "") -
     rms = float(np.sqrt(np.mean(acc_ref.astype(np.float64) ** 2))) if acc_ref.size else 0.0
     err = float(np.max(np.abs(acc_gpu - acc_ref))) if acc_ref.size else 0.0
     assert err <= TOL_REL_RMS * rms, f"{what}: max err {err:.3e} > {TOL_REL_RMS} * rms {rms:.3e}"
+
+
+def sample_rows(c: O.Compressed, rows: np.ndarray) -> O.Compressed:
+    """The layer restricted to output rows `rows` (ascending): its packed words, row scales and
+    CSR rows.  The dW scale is the whole matrix's, so each sampled row computes exactly what it
+    computes in the full layer (routing depends on the tokens only)."""
+    rows = np.asarray(rows, dtype=np.int64)
+    rp = c.delta_row_ptrs.astype(np.int64)
+    cols, vals, ptrs = [], [], [0]
+    for r in rows:
+        lo, hi = rp[r], rp[r + 1]
+        cols.append(c.delta_col_indices[lo:hi])
+        vals.append(c.delta_values[lo:hi])
+        ptrs.append(ptrs[-1] + int(hi - lo))
+    ci = np.concatenate(cols).astype(np.uint32) if cols else np.zeros(0, np.uint32)
+    cv = np.concatenate(vals).astype(np.uint8) if vals else np.zeros(0, np.uint8)
+    return O.Compressed(np.ascontiguousarray(c.packed_base[rows]), np.ascontiguousarray(c.scale_base[rows]),
+                        np.asarray(ptrs, dtype=np.uint32), ci, cv, c.delta_scale, int(rows.size), c.in_features)

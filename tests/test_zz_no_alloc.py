@@ -89,9 +89,9 @@ def test_static_matches_workspace_entry(sc, n, k, m, mode):
     assert want[2].size > 0, "the case should route at least one token"
 
     got = [outputs(m, n) for _ in range(2)]
-    call_static(sc, op, x, *got[0])            # first call: looks the scratch array up
     torch.cuda.synchronize()
-    free0 = torch.cuda.mem_get_info(0)[0]
+    free0 = torch.cuda.mem_get_info(0)[0]      # sc_layer_create has already looked the array up
+    call_static(sc, op, x, *got[0])
     call_static(sc, op, x, *got[1])
     call_static(sc, op, x, *got[0])
     torch.cuda.synchronize()
