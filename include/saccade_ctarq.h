@@ -172,6 +172,10 @@ SC_API sc_status sc_forward_ws(const sc_layer* layer, const void* x, int x_dtype
  * launch (different split or engine, more than 8 tokens) run one after another on the stream. */
 typedef struct sc_group sc_group;
 SC_API sc_status sc_group_create(sc_layer* const* layers, int count, sc_group** out);
+/* Workspace bytes sc_forward_group needs for m tokens: the largest sc_workspace_size of its layers,
+ * or more when the group's layers share one launch of the 9..64-token path.  A smaller workspace
+ * (at least every layer's own size) makes the group run its layers one after another. */
+SC_API size_t sc_group_workspace_size(const sc_group* group, int64_t m);
 SC_API void sc_group_destroy(sc_group* group);
 SC_API sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, int64_t m,
                                   void* const* y, int y_dtype, const float* const* bias,

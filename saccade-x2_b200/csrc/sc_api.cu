@@ -83,6 +83,10 @@ bool use_fused_ks(const Layer& L, int64_t m, int ks) {
 
 bool use_fused(const Layer& L, int64_t m) { return use_fused_ks(L, m, L.ks_fused); }
 
+bool use_mid(const Layer& L, int64_t m) {
+    return L.mode != SC_MODE_EXACT && m >= kMidMinTokens && m <= kMidMaxTokens && !use_fused(L, m);
+}
+
 // dW blocks of the router-fused decode for `ks` column splits, from the host CSR (columns local
 // to the layer, ascending per row): for every (row tile, split), 129 u16 row offsets (272 B), the
 // u16 columns relative to the split, then the i8 values, each padded to 16 B; off[rt * ks + sp]
@@ -180,6 +184,12 @@ WsLayout plan_workspace(const Layer& L, int64_t m) {
     if (use_fused(L, m)) {
         w.ksplit = L.ks_fused;  // reduced inside the cluster: no partial buffer
         w.partial = take(16);
+    } else if (use_mid(L, m)) {
+        // 9..64-token GEMM: split partials, an f16 copy of bf16 (or unaligned) tokens
+        const int64_t kfull = L.shard_kind == SC_SHARD_ROWS ? L.fullK : L.K;
+        w.mid_ks = mid_ksplit(RT, L.KB, L.sms, m);
+        w.partial = take(static_cast<size_t>(w.mid_ks > 1 ? RT * w.mid_ks * m * 128 * 4 : 16));
+        w.xconv = take(static_cast<size_t>(m * kfull * 2));
     } else if (L.mode != SC_MODE_EXACT && m >= kGemmMinTokens) {
         // prefill GEMM: x again in routed-first order, that order, split partials
         w.gemm_ks = gemm_ksplit(L, m);
@@ -284,6 +294,33 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         f.dw_global = L.dw_global;
         cudaError_t e = launch_decode_fused(&f, 1, stream);
         if (e != cudaSuccess) return cuda_fail(e, "fused decode launch");
+        return SC_OK;
+    }
+    if (w.mid_ks > 0) {
+        // the 9..64-token tcgen05 GEMM, router and dW in the same launch
+        MidArgs a = {};
+        a.n = 1;
+        a.layer[0] = &L;
+        a.x = x;
+        a.x_dtype = x_dtype;
+        a.x_stride = L.shard_kind == SC_SHARD_ROWS ? L.fullK : L.K;
+        a.x_col0 = L.shard_kind == SC_SHARD_ROWS ? L.col_begin : 0;
+        a.m = m;
+        a.route_all = bypass_now ? 1 : 0;
+        a.ks = w.mid_ks;
+        a.xconv = reinterpret_cast<uint16_t*>(base + w.xconv);
+        a.counter = reinterpret_cast<uint32_t*>(base + w.counter);
+        a.mask[0] = mask_out ? mask_out : reinterpret_cast<uint8_t*>(base + w.mask);
+        a.ridx[0] = ridx_out ? ridx_out : reinterpret_cast<int32_t*>(base + w.ridx);
+        a.nrouted[0] = nrouted_out ? nrouted_out : reinterpret_cast<int32_t*>(base + w.nrouted);
+        a.y[0] = y;
+        a.y_dtype = partial ? SC_F32 : y_dtype;
+        a.bias[0] = partial ? nullptr : bias;
+        a.partial_out = partial ? 1 : 0;
+        a.partial = reinterpret_cast<float*>(base + w.partial);
+        a.rtcount = reinterpret_cast<uint32_t*>(base + w.rtcount);
+        cudaError_t e = launch_mid(a, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "9..64-token GEMM launch");
         return SC_OK;
     }
     uint16_t* xk = reinterpret_cast<uint16_t*>(base + w.xk);
@@ -455,6 +492,10 @@ static void free_layer(Layer& L) {
     cudaFree(L.dwoff);
     cudaFree(L.fold);
     cudaFree(L.foldoff);
+    cudaFree(L.dseg);
+    cudaFree(L.dsegoff);
+    L.dseg = nullptr;
+    L.dsegoff = nullptr;
     L.dwblk = nullptr;
     L.dwoff = nullptr;
     L.fold = nullptr;
@@ -683,6 +724,7 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
         std::vector<float> hs(static_cast<size_t>(L.Np));
         e = cudaMemcpy(hs.data(), L.scale, L.Np * 4, cudaMemcpyDeviceToHost);
         if (e == cudaSuccess) e = build_fold_lists(L, srp.data(), scol.data(), sval.data(), hs.data());
+        if (e == cudaSuccess) e = build_dw_segments(L, srp.data(), scol.data(), sval.data());
     }
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     cudaFree(tmp_packed);
@@ -900,6 +942,54 @@ sc_status sc_group_create(sc_layer* const* layers, int count, sc_group** out) {
 
 void sc_group_destroy(sc_group* group) { delete group; }
 
+}  // extern "C"
+
+// One launch pair of the integer GEMM for every layer of a group (2..64 tokens): the workspace
+// carve-up (offsets from the base) and its total.
+struct MidGroupPlan {
+    bool use = false;
+    int ks = 0;
+    int64_t rt = 0;
+    size_t xconv = 0, mask = 0, ridx = 0, nrouted = 0, partial = 0, total = 0;
+};
+
+static MidGroupPlan plan_mid_group(const sc_group* g, int64_t m) {
+    MidGroupPlan p;
+    const int n = static_cast<int>(g->layers.size());
+    const Layer& L0 = g->layers[0]->L;
+    bool ok = n > 1;
+    for (int i = 0; i < n && ok; ++i) ok = use_mid(g->layers[i]->L, m);
+    if (!ok) return p;
+    for (int i = 0; i < n; ++i) p.rt += g->layers[i]->L.Np / 128;
+    if (p.rt > kMaxRowTiles) return p;
+    p.ks = mid_ksplit(p.rt, L0.KB, L0.sms, m);
+    size_t off = kCounterBytes;
+    auto take = [&](size_t bytes) {
+        size_t o = off;
+        off = static_cast<size_t>(ceil_to(static_cast<int64_t>(off + bytes), 256));
+        return o;
+    };
+    p.xconv = take(static_cast<size_t>(m * L0.K * 2));
+    p.mask = take(static_cast<size_t>(SC_GROUP_MAX * ceil_to(m, 16)));
+    p.ridx = take(static_cast<size_t>(SC_GROUP_MAX * 4 * m));
+    p.nrouted = take(static_cast<size_t>(SC_GROUP_MAX * 16));
+    p.partial = take(static_cast<size_t>(p.ks > 1 ? p.rt * p.ks * m * 128 * 4 : 16));
+    p.total = off;
+    p.use = true;
+    return p;
+}
+
+extern "C" {
+
+size_t sc_group_workspace_size(const sc_group* group, int64_t m) {
+    if (!group || m < 0) return 0;
+    size_t need = 0;
+    for (const sc_layer* l : group->layers) need = std::max(need, plan_workspace(l->L, m).total);
+    const MidGroupPlan p = plan_mid_group(group, m);
+    if (p.use) need = std::max(need, p.total);
+    return need;
+}
+
 sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, int64_t m, void* const* y, int y_dtype,
                            const float* const* bias, uint8_t* const* mask_out, int32_t* const* routed_idx_out,
                            int32_t* const* n_routed_out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -966,6 +1056,47 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
         }
         const cudaError_t e = launch_decode_fused(f, n, s);
         if (e != cudaSuccess) return cuda_fail(e, "grouped decode launch");
+        return SC_OK;
+    }
+    const MidGroupPlan mp = plan_mid_group(group, m);
+    if (mp.use && workspace && workspace_bytes >= mp.total && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0) {
+        if ((x_dtype != SC_F16 && x_dtype != SC_BF16) || !x ||
+            (y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32)) {
+            set_error("sc_forward_group: bad x / y dtype or null x");
+            return SC_EINVAL;
+        }
+        unsigned char* base = static_cast<unsigned char*>(workspace);
+        MidArgs a = {};
+        a.n = n;
+        for (int i = 0; i < n; ++i) {
+            if (!y[i]) {
+                set_error("sc_forward_group: null output " + std::to_string(i));
+                return SC_EINVAL;
+            }
+            a.layer[i] = &group->layers[i]->L;
+            a.mask[i] = (mask_out && mask_out[i]) ? mask_out[i] : base + mp.mask + i * ceil_to(m, 16);
+            a.ridx[i] = (routed_idx_out && routed_idx_out[i]) ? routed_idx_out[i]
+                                                              : reinterpret_cast<int32_t*>(base + mp.ridx) + i * m;
+            a.nrouted[i] = (n_routed_out && n_routed_out[i]) ? n_routed_out[i]
+                                                             : reinterpret_cast<int32_t*>(base + mp.nrouted) + i * 4;
+            a.y[i] = y[i];
+            a.bias[i] = bias ? bias[i] : nullptr;
+        }
+        a.x = x;
+        a.x_dtype = x_dtype;
+        a.x_stride = L0.K;
+        a.x_col0 = 0;
+        a.m = m;
+        a.route_all = g_bypass.load() != 0 ? 1 : 0;
+        a.ks = mp.ks;
+        a.xconv = reinterpret_cast<uint16_t*>(base + mp.xconv);
+        a.y_dtype = y_dtype;
+        a.partial_out = 0;
+        a.partial = reinterpret_cast<float*>(base + mp.partial);
+        a.counter = reinterpret_cast<uint32_t*>(base);
+        a.rtcount = reinterpret_cast<uint32_t*>(base + 256);
+        const cudaError_t e = launch_mid(a, s);
+        if (e != cudaSuccess) return cuda_fail(e, "grouped 9..64-token GEMM launch");
         return SC_OK;
     }
     for (int i = 0; i < n; ++i) {

@@ -535,20 +535,6 @@ __device__ __forceinline__ uint4 load_x8(const void* x, int x_dtype, bool vec, i
     return *reinterpret_cast<const uint4*>(h);
 }
 
-__device__ __forceinline__ void sum_x8(uint4 v, float& a1, float& a2, float& a3) {
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const float lo = h2f(lo16(w[q])), hi = h2f(hi16(w[q]));
-        a1 += lo;
-        a2 = fmaf(lo, lo, a2);
-        a3 += fabsf(lo);
-        a1 += hi;
-        a2 = fmaf(hi, hi, a2);
-        a3 += fabsf(hi);
-    }
-}
-
 // fp8 engine, auxiliary threads after staging one token: split the staged slice of x into 8
 // e4m3 columns with x = 2^e * sum_c 2^(-4c) X_c.  e puts the slice's max |x| in [128, 256); each
 // column takes the e4m3 rounding of the residual scaled by 16^c and leaves an exact f32 residual,

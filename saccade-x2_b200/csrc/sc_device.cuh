@@ -257,6 +257,22 @@ __device__ __forceinline__ uint16_t hi16(uint32_t v) { return static_cast<uint16
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// Router sums of 8 f16 values (one 16-byte chunk) in f32, in element order: x, x^2 (one rounding
+// through fma) and |x|.
+__device__ __forceinline__ void sum_x8(uint4 v, float& a1, float& a2, float& a3) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const float lo = h2f(lo16(w[q])), hi = h2f(hi16(w[q]));
+        a1 += lo;
+        a2 = fmaf(lo, lo, a2);
+        a3 += fabsf(lo);
+        a1 += hi;
+        a2 = fmaf(hi, hi, a2);
+        a3 += fabsf(hi);
+    }
+}
+
 // First index in [lo, hi) of an ascending u16 column list whose column is >= key.
 __device__ __forceinline__ int64_t lower_bound_u16(const uint16_t* col, int64_t lo, int64_t hi, int64_t key) {
     while (lo < hi) {

@@ -55,6 +55,11 @@ struct Layer {
     uint8_t* fold = nullptr;     // lists, each [9 u16 offsets per 16-row tile | pad to 32 B | u32 entries]
     uint32_t* foldoff = nullptr; // byte offset of list (rt * KB + kb); [RT*KB + 1]; null: no fold
     int fold_cap = 0;            // shared-memory slot of one list: 4096 or 8192 bytes
+    // dW per (128-row tile, 64-column block) for the 9..64-token GEMM: u16 row offsets [129] (padded
+    // to 272 B), then u16 entries (column in the block | i8 value << 6), ascending columns per row.
+    uint8_t* dseg = nullptr;
+    uint32_t* dsegoff = nullptr; // byte offset of segment (rt * KB + kb); [RT*KB + 1]; null: no dW
+    int dseg_max = 0;            // largest segment, bytes (16-byte multiple)
 };
 
 // Shared-memory budget of one dW block in the fused decode kernel.
@@ -86,6 +91,8 @@ struct WsLayout {
     size_t partial = 0, rtcount = 0;
     size_t xkp = 0, perm = 0;    // prefill GEMM: x in routed-first order and that order
     int gemm_ks = 0;             // prefill GEMM column splits (0: the GEMM does not serve the call)
+    size_t xconv = 0;            // 9..64-token GEMM: f16 copy of bf16 (or unaligned) tokens
+    int mid_ks = 0;              // its column splits (0: it does not serve the call)
     size_t total = 0;
     int ksplit = 1;
     int chunk_tokens = 0;        // tokens per decode launch
@@ -183,6 +190,7 @@ int64_t gemm_tile_tokens();
 int gemm_ksplit(const Layer& L, int64_t m);  // column splits of the prefill GEMM for m tokens
 cudaError_t build_fold_lists(Layer& L, const uint32_t* srp, const uint16_t* scol, const int8_t* sval,
                              const float* scale);
+cudaError_t build_dw_segments(Layer& L, const uint32_t* srp, const uint16_t* scol, const int8_t* sval);
 #ifndef SC_GEMM_MIN_TOKENS
 #define SC_GEMM_MIN_TOKENS 9  // calls of at least this many tokens (not decoded fused) run the GEMM
 #endif
@@ -219,6 +227,44 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s);
 int fused_max_active_clusters(int ks);
 int fused_max_kb(int64_t m);  // largest column range (64-column blocks) one fused CTA holds for m tokens
 int64_t fused_prefetch_bytes();  // weight bytes the fused kernel prefetches with one CTA on every SM
+
+// 9..16 tokens (batched decode): k_mid_route (routing, skipped when the caller routed already),
+// then k_ctarq_mid, a tcgen05 f16 GEMM with the tokens as the MMA's N side and dW of the routed
+// tokens from the staged token tiles (sc_mid.cu).  One call serves 1..SC_GROUP_MAX layers reading
+// the same x.
+#ifndef SC_MID_MIN_TOKENS
+#define SC_MID_MIN_TOKENS 9   // calls of at least this many tokens (and at most 64) run it
+#endif
+#ifndef SC_MID_MAX_TOKENS
+#define SC_MID_MAX_TOKENS 16  // ... up to this many (the kernel takes up to 64; with routed tokens beyond 16
+                              // the 128-token GEMM is faster, its dW folded into the weights)
+#endif
+constexpr int64_t kMidMinTokens = SC_MID_MIN_TOKENS;
+constexpr int64_t kMidMaxTokens = SC_MID_MAX_TOKENS;
+struct MidArgs {
+    int n;                                  // layers (same K and input columns)
+    const Layer* layer[SC_GROUP_MAX];
+    const void* x;
+    int x_dtype;
+    int64_t x_stride, x_col0, m;
+    int route_all;
+    int ks;                                 // column splits (mid_ksplit)
+    int routed_in;                          // 1: mask / ridx / nrouted already hold the routing
+    uint32_t* counter;                      // the router's completion counter (zero between calls)
+    uint16_t* xconv;                        // [m][x_stride] f16: bf16 (or unaligned) tokens for the TMA loads
+    uint8_t* mask[SC_GROUP_MAX];
+    int32_t* ridx[SC_GROUP_MAX];
+    int32_t* nrouted[SC_GROUP_MAX];
+    void* y[SC_GROUP_MAX];
+    int y_dtype;
+    const float* bias[SC_GROUP_MAX];
+    int partial_out;
+    float* partial;                         // [sum RT][ks][m][128] f32 (ks > 1)
+    uint32_t* rtcount;                      // [sum RT] counters (zero between calls)
+};
+int mid_ksplit(int64_t rt_total, int64_t kb, int sms, int64_t m);
+bool use_mid(const Layer& L, int64_t m);
+cudaError_t launch_mid(const MidArgs& a, cudaStream_t s);
 
 // Test hook: the next router-fused decode launches leave CTA 0's first weight stage unissued.
 void set_drop_weight_copy(int on);

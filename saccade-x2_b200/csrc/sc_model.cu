@@ -1,0 +1,339 @@
+// sc_model.cu -- the Qwen2 decoder glue around the C-TARQ linears (saccade-runner/src/model.rs),
+// as sm_100a kernels: embedding gather, residual add + RMSNorm, RoPE + KV-cache append, GQA
+// attention over the cache, SiLU(gate) * up.  Every tensor is f32 except the inputs of the linears,
+// which the kernels write as f16 directly (the projection layer's to_dtype(F16), model.rs:58-61).
+//
+// The KV cache is f32, like the reference's (model.rs:228-236 concatenates f32 tensors), laid out
+// [slot][kv_head][position][head_dim] so that one (slot, kv head) is a contiguous stream.
+#include <cuda_fp16.h>
+
+#include "saccade_qwen2.h"
+#include "sc_device.cuh"
+#include "sc_internal.h"
+
+namespace sc {
+
+// ---------------------------------------------------------------- embedding (model.rs:512)
+__global__ void k_embed(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table, int64_t hidden,
+                        int64_t vocab, float* __restrict__ out, uint32_t* status) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t t = blockIdx.x;
+    int64_t id = ids[t];
+    if (id < 0 || id >= vocab) {
+        record_error(status, DEV_BAD_INDEX);
+        id = 0;
+    }
+    const uint16_t* row = table + id * hidden;
+    for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) out[t * hidden + h] = h2f(row[h]);
+}
+
+// ---------------------------------------------------------------- residual add + RMSNorm (model.rs:92-98)
+// resid += delta (when given); out = f16((resid / sqrt(mean(resid^2) + eps)) * w).  The mean is a
+// fixed-order f32 sum: thread t adds elements t, t + 256, ... in order, then thread 0 adds the 256
+// partial sums in order.
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) k_add_rmsnorm(float* __restrict__ resid, const float* __restrict__ delta,
+                                                               const float* __restrict__ w, int64_t hidden, float eps,
+                                                               void* __restrict__ out, int out_f32) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float part[kNormThreads];
+    __shared__ float s_denom;
+    const int64_t t = blockIdx.x;
+    float* x = resid + t * hidden;
+    float acc = 0.0f;
+    for (int64_t h = threadIdx.x; h < hidden; h += kNormThreads) {
+        float v = x[h];
+        if (delta) {
+            v = __fadd_rn(v, delta[t * hidden + h]);
+            x[h] = v;
+        }
+        acc = __fadd_rn(acc, __fmul_rn(v, v));
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int i = 0; i < kNormThreads; ++i) s = __fadd_rn(s, part[i]);
+        const float var = __fdiv_rn(s, static_cast<float>(hidden));
+        s_denom = __fsqrt_rn(__fadd_rn(var, eps));
+    }
+    __syncthreads();
+    const float d = s_denom;
+    for (int64_t h = threadIdx.x; h < hidden; h += kNormThreads) {
+        const float y = __fmul_rn(__fdiv_rn(x[h], d), w[h]);
+        if (out_f32) static_cast<float*>(out)[t * hidden + h] = y;
+        else static_cast<uint16_t*>(out)[t * hidden + h] = f32_to_f16_bits(y);
+    }
+}
+
+// ---------------------------------------------------------------- RoPE + KV append (model.rs:111-154, 228-236)
+// q [T][nh][hd], k, v [T][nkv][hd] (f32, biases already added).  Token t sits in cache slot
+// slot[t] at position pos[t]: q and k are rotated in f32 (x * cos + rotate_half(x) * sin, two
+// roundings as the reference's separate multiply and add), k and v are written into the cache.
+__global__ void k_rope_append(float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+                              const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                              const int32_t* __restrict__ slot, const int32_t* __restrict__ pos, int nh, int nkv, int hd,
+                              int max_pos, float* __restrict__ kc, float* __restrict__ vc) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t t = blockIdx.x;
+    const int p = pos[t], s = slot[t];
+    const int half = hd / 2;
+    const float* c = cos_t + static_cast<int64_t>(p) * hd;
+    const float* sn = sin_t + static_cast<int64_t>(p) * hd;
+    for (int i = threadIdx.x; i < nh * half; i += blockDim.x) {
+        const int h = i / half, d = i % half;
+        float* qh = q + (t * nh + h) * hd;
+        const float x1 = qh[d], x2 = qh[d + half];
+        // out[d] = x1 * cos[d] + (-x2) * sin[d];  out[d + half] = x2 * cos[d + half] + x1 * sin[d + half]
+        const float o1 = __fadd_rn(__fmul_rn(x1, c[d]), __fmul_rn(-x2, sn[d]));
+        const float o2 = __fadd_rn(__fmul_rn(x2, c[d + half]), __fmul_rn(x1, sn[d + half]));
+        qh[d] = o1;
+        qh[d + half] = o2;
+    }
+    for (int i = threadIdx.x; i < nkv * half; i += blockDim.x) {
+        const int h = i / half, d = i % half;
+        const float* kh = k + (t * nkv + h) * hd;
+        const float x1 = kh[d], x2 = kh[d + half];
+        float* dst = kc + ((static_cast<int64_t>(s) * nkv + h) * max_pos + p) * hd;
+        dst[d] = __fadd_rn(__fmul_rn(x1, c[d]), __fmul_rn(-x2, sn[d]));
+        dst[d + half] = __fadd_rn(__fmul_rn(x2, c[d + half]), __fmul_rn(x1, sn[d + half]));
+    }
+    for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) {
+        const int h = i / hd, d = i % hd;
+        vc[((static_cast<int64_t>(s) * nkv + h) * max_pos + p) * hd + d] = v[(t * nkv + h) * hd + d];
+    }
+}
+
+// ---------------------------------------------------------------- attention (model.rs:238-257)
+// One CTA per (token, kv head, block of keys): the G = nh / nkv query heads of the group against
+// keys [kb * kKeys, min(pos + 1, (kb + 1) * kKeys)) of the token's cache slot (causal: keys up to
+// its own position).  scores = (q . k) * scale, softmax over all keys, out = attn . v.  A CTA writes
+// its block's max, sum of exp and unnormalised output; k_attn_combine rescales and adds the blocks
+// in order (one block: the plain softmax).
+constexpr int kAttnThreads = 256;
+constexpr int kAttnKeys = 256;      // keys per CTA
+constexpr int kAttnMaxG = 8;        // query heads per kv head
+constexpr int kAttnMaxHd = 128;
+
+__global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q, const float* __restrict__ kc,
+                                                       const float* __restrict__ vc, const int32_t* __restrict__ slot,
+                                                       const int32_t* __restrict__ pos, int nh, int nkv, int hd,
+                                                       int max_pos, float scale, int nblk, float* __restrict__ part_o,
+                                                       float* __restrict__ part_ml) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float s_q[kAttnMaxG][kAttnMaxHd];
+    __shared__ float s_p[kAttnMaxG][kAttnKeys];
+    __shared__ float s_m[kAttnMaxG], s_l[kAttnMaxG];
+    const int64_t t = blockIdx.x / (nkv * nblk);
+    const int rem = blockIdx.x % (nkv * nblk);
+    const int h = rem / nblk, kb = rem % nblk;
+    const int G = nh / nkv;
+    const int L = pos[t] + 1;
+    const int k0 = kb * kAttnKeys, k1 = min(L, k0 + kAttnKeys);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* kbase = kc + (static_cast<int64_t>(slot[t]) * nkv + h) * max_pos * hd;
+    const float* vbase = vc + (static_cast<int64_t>(slot[t]) * nkv + h) * max_pos * hd;
+    for (int i = tid; i < G * hd; i += kAttnThreads) s_q[i / hd][i % hd] = q[(t * nh + h * G + i / hd) * hd + i % hd];
+    __syncthreads();
+    const int nk = k1 > k0 ? k1 - k0 : 0;
+    // scores: one warp per key, lanes over head_dim, a fixed shuffle tree
+    for (int j = warp; j < nk; j += kAttnThreads / 32) {
+        const float* kr = kbase + static_cast<int64_t>(k0 + j) * hd;
+        float kv[kAttnMaxHd / 32];
+#pragma unroll
+        for (int e = 0; e < kAttnMaxHd / 32; ++e) kv[e] = (lane + 32 * e < hd) ? kr[lane + 32 * e] : 0.0f;
+        for (int g = 0; g < G; ++g) {
+            float d = 0.0f;
+#pragma unroll
+            for (int e = 0; e < kAttnMaxHd / 32; ++e)
+                if (lane + 32 * e < hd) d = __fadd_rn(d, __fmul_rn(s_q[g][lane + 32 * e], kv[e]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+            if (lane == 0) s_p[g][j] = __fmul_rn(d, scale);
+        }
+    }
+    __syncthreads();
+    // per head: block max, exp, block sum (one warp per head)
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < nk; j += 32) m = fmaxf(m, s_p[g][j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int j = lane; j < nk; j += 32) {
+            const float e = expf(__fsub_rn(s_p[g][j], m));
+            s_p[g][j] = e;
+            l = __fadd_rn(l, e);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+        if (lane == 0) {
+            s_m[g] = m;
+            s_l[g] = l;
+        }
+    }
+    __syncthreads();
+    // unnormalised output of this block: threads over (g, d), keys in order
+    const int64_t pbase = (t * nkv + h) * static_cast<int64_t>(nblk) + kb;
+    for (int i = tid; i < G * hd; i += kAttnThreads) {
+        const int g = i / hd, d = i % hd;
+        float o = 0.0f;
+        for (int j = 0; j < nk; ++j) o = __fadd_rn(o, __fmul_rn(s_p[g][j], vbase[static_cast<int64_t>(k0 + j) * hd + d]));
+        part_o[(pbase * G + g) * hd + d] = o;
+    }
+    if (tid < G) {
+        part_ml[(pbase * G + tid) * 2] = s_m[tid];
+        part_ml[(pbase * G + tid) * 2 + 1] = s_l[tid];
+    }
+}
+
+// Rescales the key blocks of every (token, head) to their common max, adds them in block order and
+// writes out = o / l as f16 [T][nh * hd] (the o projection's input).
+__global__ void k_attn_combine(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                               const int32_t* __restrict__ pos, int nh, int nkv, int hd, int nblk,
+                               uint16_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t t = blockIdx.x;
+    const int G = nh / nkv;
+    const int nb = (pos[t] + kAttnKeys) / kAttnKeys;  // blocks holding keys of this token
+    for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) {
+        const int hq = i / hd, d = i % hd;
+        const int h = hq / G, g = hq % G;
+        const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
+        float m = -INFINITY;
+        for (int b = 0; b < nb; ++b) m = fmaxf(m, part_ml[((pb + b) * G + g) * 2]);
+        float l = 0.0f, o = 0.0f;
+        for (int b = 0; b < nb; ++b) {
+            const float f = nb == 1 ? 1.0f : expf(__fsub_rn(part_ml[((pb + b) * G + g) * 2], m));
+            l = __fadd_rn(l, __fmul_rn(part_ml[((pb + b) * G + g) * 2 + 1], f));
+            o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], f));
+        }
+        out[t * nh * hd + i] = f32_to_f16_bits(__fdiv_rn(o, l));
+    }
+}
+
+// ---------------------------------------------------------------- SiLU(gate) * up (model.rs:295-299)
+// h = f16(silu(g) * u) with g, u the f16 outputs of gate and up widened (the projection layer's
+// to_dtype(F32)) and silu(g) = g / (1 + exp(-g)).
+__global__ void k_silu_mul(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up, int64_t n,
+                           uint16_t* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float g = h2f(gate[i]);
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        out[i] = f32_to_f16_bits(__fmul_rn(s, h2f(up[i])));
+    }
+}
+
+// f16 -> f32 (plus an optional f32 bias per column): the projection layer's to_dtype(F32).
+__global__ void k_f16_to_f32(const uint16_t* __restrict__ x, int64_t n, float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = h2f(x[i]);
+}
+
+static int grid_for(int64_t n, int threads) {
+    int64_t b = (n + threads - 1) / threads;
+    if (b > 4096) b = 4096;
+    return static_cast<int>(b > 0 ? b : 1);
+}
+
+}  // namespace sc
+
+using namespace sc;
+
+extern "C" {
+
+sc_status sc_qwen2_embed(const int64_t* ids, int64_t tokens, const uint16_t* table, int64_t vocab, int64_t hidden,
+                         float* out, uint32_t* status, void* stream) {
+    if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
+    if (!ids || !table || !out || hidden <= 0) return SC_EINVAL;
+    const cudaError_t e = launch_pdl(k_embed, dim3(static_cast<unsigned>(tokens)), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), ids, table, hidden, vocab, out, status);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_embed");
+}
+
+sc_status sc_qwen2_add_rmsnorm(float* resid, const float* delta, const float* weight, int64_t tokens, int64_t hidden,
+                               float eps, void* out, int out_dtype, void* stream) {
+    if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
+    if (!resid || !weight || !out || hidden <= 0 || (out_dtype != SC_F16 && out_dtype != SC_F32)) return SC_EINVAL;
+    const cudaError_t e = launch_pdl(k_add_rmsnorm, dim3(static_cast<unsigned>(tokens)), dim3(kNormThreads), 0,
+                                     static_cast<cudaStream_t>(stream), resid, delta, weight, hidden, eps, out,
+                                     out_dtype == SC_F32 ? 1 : 0);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_add_rmsnorm");
+}
+
+sc_status sc_qwen2_rope_append(float* q, const float* k, const float* v, const float* cos_table, const float* sin_table,
+                               const int32_t* slot, const int32_t* pos, int64_t tokens, int num_heads, int num_kv_heads,
+                               int head_dim, int max_pos, float* k_cache, float* v_cache, void* stream) {
+    if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
+    if (!q || !k || !v || !cos_table || !sin_table || !slot || !pos || !k_cache || !v_cache || head_dim % 2 ||
+        num_kv_heads <= 0 || num_heads % num_kv_heads)
+        return SC_EINVAL;
+    const cudaError_t e = launch_pdl(k_rope_append, dim3(static_cast<unsigned>(tokens)), dim3(256), 0,
+                                     static_cast<cudaStream_t>(stream), q, k, v, cos_table, sin_table, slot, pos,
+                                     num_heads, num_kv_heads, head_dim, max_pos, k_cache, v_cache);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_rope_append");
+}
+
+size_t sc_qwen2_attention_scratch(int64_t tokens, int num_heads, int num_kv_heads, int head_dim, int max_pos) {
+    const int64_t nblk = (max_pos + kAttnKeys - 1) / kAttnKeys;
+    const int64_t G = num_kv_heads > 0 ? num_heads / num_kv_heads : 0;
+    return static_cast<size_t>(tokens * num_kv_heads * nblk * G * (head_dim + 2) * 4);
+}
+
+sc_status sc_qwen2_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* slot,
+                             const int32_t* pos, int64_t tokens, int num_heads, int num_kv_heads, int head_dim,
+                             int max_pos, int max_query_pos, float* scratch, size_t scratch_bytes, uint16_t* out_f16,
+                             void* stream) {
+    if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
+    if (!q || !k_cache || !v_cache || !slot || !pos || !scratch || !out_f16 || num_kv_heads <= 0 ||
+        num_heads % num_kv_heads || num_heads / num_kv_heads > kAttnMaxG || head_dim > kAttnMaxHd ||
+        max_query_pos >= max_pos)
+        return SC_EINVAL;
+    if (scratch_bytes < sc_qwen2_attention_scratch(tokens, num_heads, num_kv_heads, head_dim, max_pos))
+        return SC_ENOMEM;
+    // blocks up to the largest query position of this call (every token attends keys <= its own)
+    const int nblk_alloc = (max_pos + kAttnKeys - 1) / kAttnKeys;
+    const int nblk = (max_query_pos + kAttnKeys) / kAttnKeys;
+    (void)nblk_alloc;
+    const int G = num_heads / num_kv_heads;
+    float* part_o = scratch;
+    float* part_ml = scratch + tokens * num_kv_heads * static_cast<int64_t>(nblk) * G * head_dim;
+    const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(head_dim)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_pdl(k_attn, dim3(static_cast<unsigned>(tokens * num_kv_heads * nblk)), dim3(kAttnThreads), 0, s,
+                               q, k_cache, v_cache, slot, pos, num_heads, num_kv_heads, head_dim, max_pos, scale, nblk,
+                               part_o, part_ml);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_attn_combine, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s, part_o, part_ml, pos,
+                       num_heads, num_kv_heads, head_dim, nblk, out_f16);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_attention");
+}
+
+sc_status sc_qwen2_silu_mul(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out_f16, void* stream) {
+    if (n <= 0) return n == 0 ? SC_OK : SC_EINVAL;
+    if (!gate || !up || !out_f16) return SC_EINVAL;
+    const cudaError_t e = launch_pdl(k_silu_mul, dim3(grid_for(n, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                     gate, up, n, out_f16);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_silu_mul");
+}
+
+sc_status sc_qwen2_f16_to_f32(const uint16_t* x, int64_t n, float* out, void* stream) {
+    if (n <= 0) return n == 0 ? SC_OK : SC_EINVAL;
+    if (!x || !out) return SC_EINVAL;
+    const cudaError_t e =
+        launch_pdl(k_f16_to_f32, dim3(grid_for(n, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), x, n, out);
+    return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_f16_to_f32");
+}
+
+}  // extern "C"

@@ -94,6 +94,7 @@ SIGNATURES = {
     "sc_forward_static": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp]),
     "sc_group_create": (_int, [_vp, _int, _vp]),
     "sc_group_destroy": (None, [_vp]),
+    "sc_group_workspace_size": (ctypes.c_size_t, [_vp, _i64]),
     "sc_forward_group": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_forward_partial": (_int, [_vp, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_finalize": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
@@ -104,6 +105,18 @@ SIGNATURES = {
     "sc_calibrate": (_int, [_vp, _int, _i64, _i64, _f32, _f32, ctypes.POINTER(_f32), ctypes.POINTER(_f32), _vp]),
 }
 
+# the Qwen2 decoder glue (include/saccade_qwen2.h)
+SIGNATURES_QWEN2 = {
+    "sc_qwen2_embed": (_int, [_vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp]),
+    "sc_qwen2_add_rmsnorm": (_int, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _int, _vp]),
+    "sc_qwen2_rope_append": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _vp, _vp, _vp]),
+    "sc_qwen2_attention_scratch": (ctypes.c_size_t, [_i64, _int, _int, _int, _int]),
+    "sc_qwen2_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, ctypes.c_size_t,
+                                  _vp, _vp]),
+    "sc_qwen2_silu_mul": (_int, [_vp, _vp, _i64, _vp, _vp]),
+    "sc_qwen2_f16_to_f32": (_int, [_vp, _i64, _vp, _vp]),
+}
+
 
 def _load():
     if not os.path.exists(LIB_PATH):
@@ -111,7 +124,7 @@ def _load():
             f"libsaccade_ctarq.so not found at {LIB_PATH}; build it with "
             "`make -C saccade-x2_b200/csrc` (or __graft_entry__.build()). There is no fallback path.")
     lib = ctypes.CDLL(LIB_PATH)
-    for name, (res, args) in SIGNATURES.items():
+    for name, (res, args) in list(SIGNATURES.items()) + list(SIGNATURES_QWEN2.items()):
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args

@@ -324,7 +324,8 @@ class SaccadeLinearGroup:
             self._h = None
 
     def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16, outs=None,
-                return_routing: bool = False):
+                return_routing: bool = False, biases=None):
+        """biases: optional per-layer f32 [N] tensors (or None entries), added after the f16 rounding."""
         n = len(self.ops)
         m = self.ops[0]._prep_x(x, self.ops[0].in_features)
         shapes = [x.shape[:-1] + (op.out_features,) for op in self.ops]
@@ -342,7 +343,7 @@ class SaccadeLinearGroup:
                         torch.zeros(1, dtype=torch.int32, device=self.device)) for _ in range(n)]
         if m > 0:
             stream = torch.cuda.current_stream(self.device)
-            need = max(op.workspace_size(m) for op in self.ops)
+            need = int(LIB.sc_group_workspace_size(self._h, m))
             ws = WORKSPACES.get(self.device, stream, need)
             yp = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
             mp = rp = np_ = None
@@ -350,7 +351,12 @@ class SaccadeLinearGroup:
                 mp = (ctypes.c_void_p * n)(*[r[0].data_ptr() for r in routing])
                 rp = (ctypes.c_void_p * n)(*[r[1].data_ptr() for r in routing])
                 np_ = (ctypes.c_void_p * n)(*[r[2].data_ptr() for r in routing])
-            check(LIB.sc_forward_group(self._h, x.data_ptr(), _DT[x.dtype], m, yp, _DT[out_dtype], None, mp, rp, np_,
+            bp = None
+            if biases is not None:
+                bl = [None if b is None else b.to(device=self.device, dtype=torch.float32).contiguous() for b in biases]
+                self._keep_bias = bl
+                bp = (ctypes.c_void_p * n)(*[None if b is None else b.data_ptr() for b in bl])
+            check(LIB.sc_forward_group(self._h, x.data_ptr(), _DT[x.dtype], m, yp, _DT[out_dtype], bp, mp, rp, np_,
                                        ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream)))
         if return_routing:
             return ys, routing

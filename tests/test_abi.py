@@ -9,10 +9,11 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "saccade_ctarq.h")
+HEADER_QWEN2 = os.path.join(ROOT, "include", "saccade_qwen2.h")
 
 
-def declared_symbols():
-    text = open(HEADER).read()
+def declared_symbols(path=HEADER):
+    text = open(path).read()
     return sorted(set(re.findall(r"^SC_API\s+[\w\s\*]+?\b(sc_\w+)\s*\(", text, flags=re.M)))
 
 
@@ -28,6 +29,9 @@ def test_library_exports_every_declared_symbol():
     for name in declared_symbols():
         assert hasattr(lib, name), f"{name} declared in the header but not exported"
     assert set(declared_symbols()) == set(_lib.SIGNATURES), "ctypes signatures must cover the header exactly"
+    for name in declared_symbols(HEADER_QWEN2):
+        assert hasattr(lib, name), f"{name} declared in saccade_qwen2.h but not exported"
+    assert set(declared_symbols(HEADER_QWEN2)) == set(_lib.SIGNATURES_QWEN2)
 
 
 def test_only_c_abi_is_exported():
