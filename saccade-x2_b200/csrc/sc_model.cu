@@ -13,6 +13,11 @@
 
 namespace sc {
 
+// exp of an f32 value evaluated in f64 and rounded once to f32: the correctly rounded result but for
+// inputs whose f64 value lies within an f64 rounding error of an f32 halfway point, so that a host
+// computing exp in f64 and rounding to f32 gets the same f32.
+__device__ __forceinline__ float exp_f32(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+
 // ---------------------------------------------------------------- embedding (model.rs:512)
 __global__ void k_embed(const int64_t* __restrict__ ids, const uint16_t* __restrict__ table, int64_t hidden,
                         int64_t vocab, float* __restrict__ out, uint32_t* status) {
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.0f;
         for (int j = lane; j < nk; j += 32) {
-            const float e = expf(__fsub_rn(s_p[g][j], m));
+            const float e = exp_f32(__fsub_rn(s_p[g][j], m));
             s_p[g][j] = e;
             l = __fadd_rn(l, e);
         }
@@ -209,7 +214,7 @@ __global__ void k_attn_combine(const float* __restrict__ part_o, const float* __
         for (int b = 0; b < nb; ++b) m = fmaxf(m, part_ml[((pb + b) * G + g) * 2]);
         float l = 0.0f, o = 0.0f;
         for (int b = 0; b < nb; ++b) {
-            const float f = nb == 1 ? 1.0f : expf(__fsub_rn(part_ml[((pb + b) * G + g) * 2], m));
+            const float f = nb == 1 ? 1.0f : exp_f32(__fsub_rn(part_ml[((pb + b) * G + g) * 2], m));
             l = __fadd_rn(l, __fmul_rn(part_ml[((pb + b) * G + g) * 2 + 1], f));
             o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], f));
         }
@@ -227,7 +232,7 @@ __global__ void k_silu_mul(const uint16_t* __restrict__ gate, const uint16_t* __
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const float g = h2f(gate[i]);
-        const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        const float s = __fdiv_rn(g, __fadd_rn(1.0f, exp_f32(-g)));
         out[i] = f32_to_f16_bits(__fmul_rn(s, h2f(up[i])));
     }
 }

@@ -1,0 +1,138 @@
+"""The Qwen2 decoder on the GPU (every linear C-TARQ) against the CPU model oracle.
+
+The glue kernels are checked one by one against the oracle's numpy restatement; a small model's
+greedy tokens against the oracle's; and the Qwen2-0.5B architecture (24 layers, hidden 896,
+vocabulary 151936, random init, 1 % dW, thresholds calibrated per projection at the 75th percentile
+on a separate prompt) greedy-decodes 128 tokens after a 128-token prompt with every token identical
+to the oracle's, the top-2 logit gap of each step logged.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import qwen2_oracle as QO
+from qwen2_cases import oracle_model
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def q2():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import saccade_core
+    from saccade_core import qwen2
+    saccade_core.set_bypass_c_tarq(False)
+    return qwen2
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def test_rmsnorm_kernel_matches_oracle(q2):
+    from saccade_core._lib import LIB, SC_F16, SC_F32, check
+    rng = np.random.default_rng(1)
+    T, H = 5, 896
+    x = (rng.standard_normal((T, H)) * 3).astype(np.float32)
+    d = rng.standard_normal((T, H)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    xr = torch.from_numpy(x).cuda()
+    wd = torch.from_numpy(w).cuda()
+    out = torch.empty(T, H, dtype=torch.float32, device="cuda")
+    check(LIB.sc_qwen2_add_rmsnorm(xr.data_ptr(), torch.from_numpy(d).cuda().data_ptr(), wd.data_ptr(), T, H,
+                                   ctypes.c_float(1e-6), out.data_ptr(), SC_F32, _stream()))
+    ref_x = (x + d).astype(np.float32)
+    ref = QO.rmsnorm(ref_x, w, 1e-6)
+    assert np.array_equal(xr.cpu().numpy(), ref_x)
+    assert np.array_equal(out.cpu().numpy(), ref), "same fixed order, same IEEE steps"
+    o16 = torch.empty(T, H, dtype=torch.float16, device="cuda")
+    check(LIB.sc_qwen2_add_rmsnorm(xr.data_ptr(), None, wd.data_ptr(), T, H, ctypes.c_float(1e-6), o16.data_ptr(),
+                                   SC_F16, _stream()))
+    assert np.array_equal(o16.cpu().numpy(), ref.astype(np.float16))
+
+
+@pytest.mark.parametrize("nh,nkv,hd,L", [(14, 2, 64, 1), (14, 2, 64, 300), (28, 4, 128, 700)])
+def test_rope_and_attention_match_oracle(q2, nh, nkv, hd, L):
+    from saccade_core._lib import LIB, check
+    cfg = q2.Qwen2Config(nh * hd, 64, 1, nh, nkv, hd, 100)
+    max_pos = 1024
+    cos, sin = q2.rope_tables(cfg, max_pos)
+    rng = np.random.default_rng(L)
+    # one sequence of L tokens at positions 0..L-1, every token attending the keys up to its own
+    q = rng.standard_normal((L, nh, hd)).astype(np.float32)
+    k = rng.standard_normal((L, nkv, hd)).astype(np.float32)
+    v = rng.standard_normal((L, nkv, hd)).astype(np.float32)
+    qd = torch.from_numpy(q.copy()).cuda()
+    kc = torch.zeros(1, nkv, max_pos, hd, device="cuda")
+    vc = torch.zeros_like(kc)
+    slot = torch.zeros(L, dtype=torch.int32, device="cuda")
+    pos = torch.arange(L, dtype=torch.int32, device="cuda")
+    cos_d, sin_d = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    kd, vd = torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda()
+    check(LIB.sc_qwen2_rope_append(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), cos_d.data_ptr(), sin_d.data_ptr(),
+                                   slot.data_ptr(), pos.data_ptr(), L, nh, nkv, hd, max_pos, kc.data_ptr(),
+                                   vc.data_ptr(), _stream()))
+    qr = QO.rope(q, cos[:L], sin[:L])
+    kr = QO.rope(k, cos[:L], sin[:L])
+    assert np.array_equal(qd.cpu().numpy(), qr)
+    assert np.array_equal(kc[0, :, :L].permute(1, 0, 2).cpu().numpy(), kr)
+    nbytes = int(LIB.sc_qwen2_attention_scratch(L, nh, nkv, hd, max_pos))
+    scratch = torch.empty(nbytes // 4 + 1, dtype=torch.float32, device="cuda")
+    out = torch.empty(L, nh * hd, dtype=torch.float16, device="cuda")
+    check(LIB.sc_qwen2_attention(qd.data_ptr(), kc.data_ptr(), vc.data_ptr(), slot.data_ptr(), pos.data_ptr(), L, nh,
+                                 nkv, hd, max_pos, L - 1, scratch.data_ptr(), nbytes, out.data_ptr(), _stream()))
+    scale = np.float32(1.0 / np.sqrt(hd))
+    ref = QO.attention(qr, kr, v, np.arange(L), scale)
+    got = out.cpu().numpy().reshape(L, nh, hd)
+    assert np.array_equal(got.view(np.uint16), ref.astype(np.float16).view(np.uint16)), \
+        "same reduction order, same exp: bit-identical"
+    # and close to a plain softmax in f64
+    G = nh // nkv
+    causal = np.arange(L)[:, None] >= np.arange(L)[None, :]
+    for hq in range(nh):
+        s = (qr[:, hq].astype(np.float64) @ kr[:, hq // G].T.astype(np.float64)) * float(scale)
+        s = np.where(causal, s, -np.inf)
+        e = np.exp(s - s.max(axis=1, keepdims=True))
+        plain = (e / e.sum(axis=1, keepdims=True)) @ v[:, hq // G]
+        assert np.abs(got[:, hq].astype(np.float64) - plain).max() <= 2e-3 * np.abs(plain).max() + 1e-3
+
+
+def _greedy_pair(q2, cfg, seed, prompt_len, steps, mode="fast"):
+    ck = q2.random_checkpoint(cfg, seed=seed, fill=0.01)
+    rng = np.random.default_rng(seed)
+    calib = torch.from_numpy(rng.integers(0, cfg.vocab, (1, prompt_len))).cuda()
+    q2.calibrate(ck, calib, max_pos=prompt_len + steps)
+    prompt = rng.integers(0, cfg.vocab, prompt_len)
+    model = q2.Qwen2Model(ck, max_batch=1, max_pos=prompt_len + steps, mode=mode)
+    dec = q2.GreedyDecoder(model, 1)
+    dec.capture()
+    toks, gaps = dec.generate(torch.from_numpy(prompt[None]).cuda(), steps, record_logits=True)
+    torch.cuda.synchronize()
+    model.check_device()
+    orc = oracle_model(ck, prompt_len + steps)
+    otoks, ogaps = orc.greedy(prompt, steps)
+    return toks.cpu().numpy()[0], gaps.numpy()[0], otoks, ogaps
+
+
+def test_small_model_greedy_matches_oracle(q2):
+    cfg = q2.Qwen2Config(hidden=256, intermediate=704, layers=3, heads=4, kv_heads=2, head_dim=64, vocab=4096)
+    toks, gaps, otoks, ogaps = _greedy_pair(q2, cfg, seed=7, prompt_len=24, steps=24)
+    assert np.array_equal(toks, otoks), (toks, otoks, gaps)
+
+
+def test_qwen2_0_5b_greedy_128_steps_identical(q2, capsys):
+    """Qwen2-0.5B architecture, random init, all linears C-TARQ (1 % dW), batch 1, 128-token random
+    prompt, 128 greedy steps: every token equals the oracle's.  The linears run in exact mode (op.rs's
+    f32 order) and the glue in the oracle's order, so every f32 of the decoder is the oracle's: the
+    router's thresholds sit inside the dense cluster of RmsNorm-output variances (all near 1), where
+    the fast mode's last-bit differences move tokens across them."""
+    cfg = q2.Qwen2Config.qwen2_0_5b()
+    toks, gaps, otoks, ogaps = _greedy_pair(q2, cfg, seed=42, prompt_len=128, steps=128, mode="exact")
+    with capsys.disabled():
+        print(f"\nqwen2-0.5b greedy: {int((toks == otoks).sum())}/128 identical; smallest top-2 logit gap "
+              f"{float(np.min(ogaps)):.3e} (oracle), median {float(np.median(ogaps)):.3e}")
+    assert np.array_equal(toks, otoks), np.nonzero(toks != otoks)[0][:5]
