@@ -1,7 +1,15 @@
 #!/usr/bin/env python
-"""C-TARQ linear effective HBM GB/s on the Qwen2-7B decoder-linear stack (decode).
+"""Qwen2-7B decode tok/s (default workload) and C-TARQ linear effective HBM GB/s (--workload linear).
 
-One step = one decode pass of M tokens through every C-TARQ linear of Qwen2-7B
+--workload decode (default): the Qwen2-7B architecture (hidden 3584, intermediate 18944, 28 layers,
+28 query / 4 KV heads, head_dim 128, vocab 152064), random init, every linear C-TARQ (1 % dW,
+router thresholds calibrated per projection at the 75th / 95th percentile), batch 64, 512-token
+random prompts, then greedy decoding.  One step = one decode step of the 64 sequences (64 tokens),
+replayed as one CUDA graph; tensor parallel over --gpus N (column-sharded q/k/v/gate/up, row-sharded
+o/down with one NCCL all-reduce of [y_base | y_delta | router sums] each, vocab-parallel lm_head).
+value = 64 tokens per step / max-over-ranks device time per step.
+
+--workload linear: one step = one decode pass of M tokens through every C-TARQ linear of Qwen2-7B
 (28 layers x {q 3584->3584, k 3584->512, v 3584->512, o 3584->3584, gate 3584->18944,
 up 3584->18944, down 18944->3584}), 1 % dW, a seeded 25 % of the calls routed.
 Weights total 3.3 GB, far above L2, so no flush is needed between steps.
@@ -10,7 +18,8 @@ Effective bytes per call (the metric's numerator, independent of the device layo
     2*M*K (x) + N*K/2 (int4 base) + 2*N (f16 scales) + [any token routed]*(3*nnz + 4*(N+1)) + 2*M*N (y)
 value = bytes of all calls of all ranks / max-over-ranks device time (CUDA events).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens M] [--impl reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]          # decode tok/s
+  python bench.py --workload linear [--tokens M] [--impl reference]                # linear GB/s
   python bench.py --sweep OUT.md [--sweep-fills 0.005,0.01,0.04]
                                       # single calls: 4 shapes x M 1..4096 x routed 0/10/25/100 %
                                       # x dW densities
@@ -47,8 +56,13 @@ METRIC = "C-TARQ linear effective HBM GB/s"
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="decode", choices=["decode", "linear"])
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (decode 100, linear 20)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed steps (decode 5, linear 3)")
+    ap.add_argument("--batch", type=int, default=64, help="decode: sequences")
+    ap.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens per sequence")
+    ap.add_argument("--decode-steps", type=int, default=256, help="decode: greedy steps of the workload")
+    ap.add_argument("--prefill-chunk", type=int, default=16, help="decode: sequences per prefill pass")
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--fill", type=float, default=0.01)
@@ -66,7 +80,12 @@ def parse(argv=None):
                     help="comma-separated dW densities for --sweep (default: --fill)")
     ap.add_argument("--sweep-tokens", default=None, metavar="LIST",
                     help="comma-separated token counts for --sweep (default: 1,4,16,64,256,1024,4096)")
-    return ap.parse_args(argv)
+    a = ap.parse_args(argv)
+    if a.steps is None:
+        a.steps = 100 if a.workload == "decode" else 20
+    if a.warmup is None:
+        a.warmup = 5 if a.workload == "decode" else 3
+    return a
 
 
 def launches_per_call(args):
@@ -262,7 +281,7 @@ def cpu_baseline(args):
                       f"C restatement of op.rs, OpenMP over rows ({'-march=native' if native else 'x86-64-v3'})"}
 
 
-def run_reference(args, rank):
+def run_reference_linear(args, rank):
     if rank != 0:
         return
     from oracle import oracle as O
@@ -305,7 +324,7 @@ def run_reference(args, rank):
 
 # ------------------------------------------------------------------ GPU side
 
-def run_ours(args, rank, world):
+def run_linear(args, rank, world):
     import torch
     import torch.distributed as dist
 
@@ -512,6 +531,331 @@ def run_ours(args, rank, world):
         print(json.dumps(out), flush=True)
 
 
+# ------------------------------------------------------------------ Qwen2-7B decode
+
+DECODE_METRIC = "Qwen2-7B decode tok/s"
+DECODE_PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def decode_config(args, world):
+    return {"workload": "qwen2-7b batched greedy decode", "model": "qwen2-7b (random init, every linear C-TARQ)",
+            "layers": args.layers, "global_batch": args.batch, "prompt_tokens": args.prompt,
+            "decode_steps": args.decode_steps, "dw_fill": args.fill,
+            "thresholds": "per projection at the 75th / 95th percentile of a 512-token calibration prompt",
+            "parallelism": f"tp{world}" if world > 1 else "tp1"}
+
+
+def decode_step_bytes(cfg, model, batch, pos):
+    """Algorithmic HBM bytes of one decode step on one rank at cache length `pos`: every C-TARQ call
+    (call_bytes, dW counted: some of the 64 tokens route in every call), the lm_head slice (f16),
+    the KV cache read (f32 K and V of `pos` keys per sequence and KV head) and written."""
+    total = 0
+    for L in model.layers:
+        for name in DECODE_PROJ:
+            op = L[name]
+            total += call_bytes(op.out_features, op.in_features, batch, op.delta_nnz, True)
+    total += (model.v1 - model.v0) * cfg.hidden * 2
+    total += len(model.layers) * batch * model.nkv * cfg.head_dim * 4 * 2 * (pos + 1)
+    return total
+
+
+def build_decode(args, rank, world, dev, group):
+    import torch
+
+    from saccade_core import qwen2 as Q
+    cfg = Q.Qwen2Config.qwen2_7b(layers=args.layers)
+    ck = Q.random_checkpoint(cfg, seed=42, fill=args.fill, device=dev)
+    g = torch.Generator()
+    g.manual_seed(7)
+    calib = torch.randint(0, cfg.vocab, (1, args.prompt), generator=g)
+    Q.calibrate(ck, calib.to(dev), max_pos=args.prompt)
+    if world > 1:  # every rank calibrates the same model; rank 0's thresholds are the ones used
+        import torch.distributed as dist
+        th = torch.tensor([ck.thresholds[li][n] for li in range(len(ck.blocks)) for n in DECODE_PROJ],
+                          dtype=torch.float32, device=dev)
+        dist.broadcast(th, 0, group=group)
+        th = th.cpu().numpy().reshape(len(ck.blocks), len(DECODE_PROJ), 2)
+        for li in range(len(ck.blocks)):
+            for j, n in enumerate(DECODE_PROJ):
+                ck.thresholds[li][n] = (float(th[li, j, 0]), float(th[li, j, 1]))
+    need = 1 + 2 * (args.warmup + args.steps) + 3
+    max_pos = args.prompt + max(args.decode_steps, need)
+    model = Q.Qwen2Model(ck, dev, max_batch=args.batch, max_pos=max_pos, mode=args.mode,
+                         tp=(rank, world, group) if world > 1 else None)
+    # reference-format buffers of the last layer's gate and up for the parity check, then free the rest
+    last = {n: {k: v.cpu() for k, v in ck.blocks[-1][n].items()} for n in ("gate", "up")}
+    last_thr = {n: ck.thresholds[-1][n] for n in ("gate", "up")}
+    del ck
+    torch.cuda.empty_cache()
+    return cfg, model, last, last_thr
+
+
+def check_decode_against_oracle(model, last, last_thr, batch, rows_per_call=128):
+    """The last layer's gate and up outputs of the last step (this rank's rows) against the oracle on
+    the same input rows (fast-mode tolerance 1e-3 * RMS + one f16 ulp; router masks identical)."""
+    import torch
+
+    from oracle import oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from qwen2_cases import to_compressed
+    cfg = model.cfg
+    x16 = model._bufs[("x16", batch)]
+    outs = {"gate": model._bufs[("g16", batch)], "up": model._bufs[("u16", batch)]}
+    xb = x16.cpu().numpy().view(np.uint16)
+    worst = 0.0
+    for name in ("gate", "up"):
+        full = to_compressed(last[name], cfg.intermediate, cfg.hidden)
+        rng = np.random.default_rng(5)
+        local = np.sort(rng.choice(model.i1 - model.i0, size=min(rows_per_call, model.i1 - model.i0), replace=False))
+        rows = local + model.i0
+        rp = full.delta_row_ptrs.astype(np.int64)
+        sel = [np.arange(rp[r], rp[r + 1]) for r in rows]
+        ent = np.concatenate(sel) if sel else np.zeros(0, np.int64)
+        ptrs = np.concatenate([[0], np.cumsum([len(e) for e in sel])]).astype(np.uint32)
+        c = O.Compressed(np.ascontiguousarray(full.packed_base[rows]), np.ascontiguousarray(full.scale_base[rows]),
+                         ptrs, full.delta_col_indices[ent].copy(), full.delta_values[ent].copy(), full.delta_scale,
+                         len(rows), cfg.hidden)
+        yr, routed, _ = O.OracleLinear(c, *last_thr[name]).forward(xb)
+        yg = outs[name].cpu().numpy().view(np.uint16)[:, local]
+        a, b = yg.view(np.float16).astype(np.float32), yr.view(np.float16).astype(np.float32)
+        rms = float(np.sqrt(np.mean(b.astype(np.float64) ** 2)))
+        tol = 1e-3 * rms + np.spacing(np.abs(b).astype(np.float16)).astype(np.float32)
+        ratio = float(np.max(np.abs(a - b) / tol))
+        worst = max(worst, ratio)
+        if ratio > 1.0:
+            raise AssertionError(f"bench parity: last layer {name} differs from the oracle ({ratio:.3f} of tolerance)")
+    return {"calls": "last layer gate and up of the last timed step", "rows_per_call": rows_per_call,
+            "routed_tokens": int(np.count_nonzero(routed)), "max_err_over_tol": round(worst, 4),
+            "tolerance": "1e-3 * RMS(ref) + 1 f16 ulp", "ok": True}
+
+
+def run_decode(args, rank, world):
+    import torch
+    import torch.distributed as dist
+
+    import saccade_core as sc
+    from saccade_core import qwen2 as Q
+    from saccade_core._lib import LIB
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    group = dist.group.WORLD if world > 1 else None
+    t_setup = time.perf_counter()
+    cfg, model, last, last_thr = build_decode(args, rank, world, dev, group)
+    B, S = args.batch, args.prompt
+    g = torch.Generator()
+    g.manual_seed(11)
+    prompts = torch.randint(0, cfg.vocab, (B, S), generator=g)
+    dec = Q.GreedyDecoder(model, B)
+    with torch.cuda.stream(dec.stream):
+        dec.prefill(prompts.to(dev), chunk=args.prefill_chunk)
+    dec.stream.synchronize()
+    dec.capture()
+    setup_s = time.perf_counter() - t_setup
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # the timed region: K back-to-back step graphs (each feeds its argmax to the next)
+    for _ in range(args.warmup):
+        dec.step()
+    dec.stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    pos0 = int(dec.pos[0].item())
+    clocks = ClockSampler(dev)
+    clocks.start()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(dec.stream):
+        s_ev.record()
+        for _ in range(args.steps):
+            dec.graph.replay()
+        e_ev.record()
+    dec.stream.synchronize()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s_ev.elapsed_time(e_ev) / args.steps)
+
+    # end to end: token ids from pinned host memory in, next ids to pinned host memory out, every step
+    ids_host = torch.empty(B, dtype=torch.int64).pin_memory()
+    out_host = torch.empty(B, dtype=torch.int64).pin_memory()
+    ids_host.copy_(dec.next.cpu())
+    e2e_steps = args.steps
+
+    def e2e_step():
+        nxt = dec.step(ids_host)
+        with torch.cuda.stream(dec.stream):
+            out_host.copy_(nxt, non_blocking=True)
+        dec.stream.synchronize()
+        ids_host.copy_(out_host)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(dec.stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(dec.stream)
+    dec.stream.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(s2.elapsed_time(e2) / e2e_steps)
+    model.check_device()
+    undecided = model.undecided_routes()
+    parity = check_decode_against_oracle(model, last, last_thr, B) if rank == 0 else None
+
+    # the dominant kernel: each layer's gate+up call (one grouped C-TARQ launch unit) at M = 64 on
+    # the last step's post-attention normed state, replayed over all layers (weights >> L2)
+    x16 = model._bufs[("x16", B)]
+    gbuf, ubuf = model._bufs[("g16", B)].clone(), model._bufs[("u16", B)].clone()
+
+    def gateup_all():
+        for L in model.layers:
+            L["gateup"].forward(x16, outs=[gbuf, ubuf])
+
+    n0 = int(LIB.sc_launch_count())
+    cap = sc.CapturedStep(gateup_all, dev)  # one eager call, one captured
+    gu_launches = (int(LIB.sc_launch_count()) - n0) // (2 * len(model.layers))
+    for _ in range(3):
+        cap.replay()
+    cap.synchronize()
+    reps = 10
+    s3, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cap.stream):
+        s3.record()
+        for _ in range(reps):
+            cap.replay()
+        e3.record()
+    cap.synchronize()
+    us_gu = s3.elapsed_time(e3) * 1e3 / (reps * len(model.layers))
+    gu_bytes = sum(call_bytes(L[n].out_features, L[n].in_features, B, L[n].delta_nnz, True)
+                   for n in ("gate", "up") for L in model.layers[:1])
+    achieved = gu_bytes / (us_gu * 1e-6) / 1e9
+    peak, peak_kind = measured_peak()
+
+    pos_mid = pos0 + args.steps // 2
+    step_bytes = decode_step_bytes(cfg, model, B, pos_mid)
+    total_bytes = step_bytes
+    if world > 1:
+        tb = torch.tensor([float(step_bytes)], device=dev, dtype=torch.float64)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        total_bytes = float(tb.item())
+    value = B / (ms / 1e3)
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "decode_gateup_m64_traffic.json")
+    if os.path.exists(tp):
+        try:
+            traffic = json.load(open(tp)).get("dram_bytes_per_launch_unit")
+        except ValueError:
+            pass
+    out = {
+        "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights, random prompt ids)",
+        "config": {**decode_config(args, world), "mode": args.mode, "positions_timed": [pos0, pos0 + args.steps],
+                   "l2": "inputs > L2 (weights and KV cache of one step far above 126 MB)",
+                   "graph": "one CUDA graph per decode step",
+                   "collectives_per_step": (2 * len(model.layers) + 1) if world > 1 else 0,
+                   "bytes_per_step_all_ranks": int(total_bytes),
+                   "step_hbm_frac": round(total_bytes / world / (ms / 1e3) / 1e9 / peak, 4),
+                   "setup_s": round(setup_s, 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": f"gate+up C-TARQ call unit at M={B} ({gu_launches} launches: router, token gather, "
+                               f"tcgen05 GEMM), {us_gu:.1f} us per layer, {gu_bytes} algorithmic bytes",
+                     "peak_kind": f"{peak_kind} hbm copy"},
+        "clocks": clk,
+        "e2e": {"value": round(B / (ms_e2e / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 8,
+                "d2h_bytes_per_step": B * 8,
+                "how": "per step: token ids from pinned host memory, the step graph, next ids to pinned host "
+                       "memory, host synchronisation"},
+        "gpu_launches": dec.launches_per_step * args.steps,
+        "undecided_split_routes": undecided,
+        "parity_check": parity,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline_decode(args)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+def decode_layer_items(args, tokens):
+    """One Qwen2-7B decoder layer's seven linears on the oracle (synthetic reference-format weights),
+    `tokens` tokens with a seeded 25 % boosted over the router threshold."""
+    calls = stack_spec(1, tokens, args.route_frac, seed=4321)
+    return build_oracle_stack(calls, args.fill, 98, tokens)
+
+
+def cpu_decode_rate(args, seconds):
+    from oracle import oracle as O
+    try:
+        O.lib(native=True)
+        native = True
+    except Exception:  # noqa: BLE001
+        native = False
+    items = decode_layer_items(args, 1)
+    _, dt1 = time_oracle(items, 1, native)
+    reps = max(1, int(seconds / max(dt1, 1e-4)))
+    _, dt = time_oracle(items, reps, native)
+    per_layer = dt / reps
+    return 1.0 / (per_layer * LAYERS), reps, dt, native
+
+
+def cpu_baseline_decode(args):
+    """The oracle's op.rs restatement on the host cores, per layer (the seven linears of one decoder
+    layer, one token), scaled to 28 layers: tokens per second of the linears alone."""
+    rate, reps, dt, native = cpu_decode_rate(args, args.cpu_seconds)
+    return {"value": round(rate, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 Qwen2-7B decoder layer (7 C-TARQ linears, 1 token) x {reps} reps in {dt:.1f} s, scaled "
+                      f"x{LAYERS} layers (linears only: no attention, norms or lm_head); C restatement of op.rs, "
+                      f"OpenMP over rows ({'-march=native' if native else 'x86-64-v3'})"}
+
+
+def run_reference_decode(args, rank):
+    """--impl reference: the reference's CPU algorithm for the decode step's linears (the oracle's
+    op.rs restatement; the Rust reference cannot be built here), per layer, scaled to 28 layers."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    try:
+        O.lib(native=True)
+        native = True
+    except Exception:  # noqa: BLE001
+        native = False
+    items = decode_layer_items(args, 1)
+    _, dt1 = time_oracle(items, 1, native)
+    budget = min(150.0, 10.0 * args.cpu_seconds) / max(1, args.steps + args.warmup)  # seconds per step
+    reps = max(1, int(budget / max(dt1, 1e-4)))
+    for _ in range(args.warmup):
+        time_oracle(items, reps, native)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        time_oracle(items, reps, native)
+    dt = time.perf_counter() - t0
+    per_layer = dt / (args.steps * reps)
+    value = 1.0 / (per_layer * LAYERS)
+    sample = (f"each step: 1 Qwen2-7B decoder layer (7 C-TARQ linears, 1 token) x {reps}, scaled x{LAYERS} layers "
+              f"(linears only); C restatement of op.rs (Rust reference not buildable here), OpenMP over rows")
+    out = {"metric": DECODE_METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_layer * LAYERS * 1e3, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+           "data": "synthetic", "config": decode_config(args, args.gpus), "impl": "reference",
+           "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
 def check_against_oracle(check_src, ops, xs, ys, calls, rows_per_call=96):
     """Compares sampled output rows of the given calls with the oracle on the same inputs (fast-mode
     tolerance: 1e-3 * RMS + one f16 ulp, router masks identical).  Raises on a mismatch."""
@@ -661,7 +1005,10 @@ def main():
             run_sweep(args)
         return
     if args.impl == "reference":
-        run_reference(args, rank)
+        if args.workload == "decode":
+            run_reference_decode(args, rank)
+        else:
+            run_reference_linear(args, rank)
         return
     if world > 1:
         import datetime
@@ -671,7 +1018,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        run_ours(args, rank, world)
+        if args.workload == "decode":
+            run_decode(args, rank, world)
+        else:
+            run_linear(args, rank, world)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define SC_ABI_VERSION 1
+#define SC_ABI_VERSION 2
 #define SC_GROUP_MAX 4      /* layers per sc_group */
 
 #if defined(__GNUC__)
@@ -94,10 +94,15 @@ typedef struct sc_layer_desc {
     /* Tensor-parallel slice of the unsharded matrix described above.
      * COLUMNS: this layer keeps output rows [N*i/n, N*(i+1)/n) rounded to multiples of 16.
      * ROWS:    this layer keeps input columns [K*i/n, K*(i+1)/n) rounded to multiples of 64;
-     *          sc_forward then takes the full [M, K] input (the router needs whole tokens)
-     *          and writes f32 partial sums for an all-reduce (see sc_forward_partial). */
+     *          sc_forward_partial then takes the full [M, K] input (the router needs whole
+     *          tokens) and writes f32 partial sums for an all-reduce; sc_forward_split takes
+     *          only the slice [M, K_slice] (see below).
+     * shard_begin < shard_end overrides index/count with an explicit range: output rows
+     * [begin, end) for COLUMNS (multiples of 16, or end = N), input columns for ROWS
+     * (multiples of 64, or end = K), e.g. whole attention heads of a tensor-parallel rank. */
     int shard_kind;                     /* sc_shard */
     int shard_index, shard_count;
+    int64_t shard_begin, shard_end;     /* ABI 2 */
 } sc_layer_desc;
 
 typedef struct sc_layer_info {
@@ -213,6 +218,31 @@ SC_API sc_status sc_forward_partial(const sc_layer* layer, const void* x, int x_
                              int32_t* n_routed_out, void* workspace, size_t workspace_bytes, void* stream);
 SC_API sc_status sc_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                       void* stream);
+
+/* Tensor parallelism without the whole token on every rank (no counterpart in the reference,
+ * which runs on one CPU; the exchange has the op's own semantics, op.rs:30-185).  A ROWS shard's
+ * sc_forward_split takes only its input slice x [m, K_slice] and writes one f32 exchange buffer
+ * of sc_split_exchange_floats(layer, m) floats:
+ *     [ y_base m*N | y_delta m*N | stats m*3 ]
+ * y_base = (slice of x . (q - 8)) * s for every token, y_delta = the slice's dW for every token,
+ * stats = per token sum x, sum x^2, sum |x| over the slice.  The caller sums the buffers of all
+ * ranks (one all-reduce, e.g. NCCL sum), then sc_finalize_split routes each token on the summed
+ * sums (heuristics.rs:3-14, op.rs:64-73) and writes y = f16(y_base + [routed] y_delta) (+ bias,
+ * cast as sc_forward).  The decision equals the reference's f32 one wherever the f64 score lies
+ * outside the f32 summation's error bound of both thresholds; tokens inside it (which the
+ * unsharded call replays in the exact f32 order, impossible without the whole token) take the
+ * f64 decision and are counted in *undecided_out (device u32, incremented; nullable).
+ * workspace: sc_workspace_size(layer, m) bytes or NULL (the device's default workspace). */
+SC_API size_t sc_split_exchange_floats(const sc_layer* layer, int64_t m);
+SC_API sc_status sc_forward_split(const sc_layer* layer, const void* x, int x_dtype, int64_t m, float* exchange,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+SC_API sc_status sc_finalize_split(const sc_layer* layer, const float* exchange, int64_t m, int ranks, void* y,
+                                   int y_dtype, const float* bias, uint8_t* mask_out, uint32_t* undecided_out,
+                                   void* stream);
+
+/* Kernels launched by this library so far in this process (a host-side count of launch calls:
+ * a captured CUDA graph counts its kernels once, at capture).  No counterpart in the reference. */
+SC_API uint64_t sc_launch_count(void);
 
 /* Router only: per-token variance (exact f32 order of heuristics.rs:3-14) and the routing
  * decision of op.rs:64-73, for m tokens of length k. scores (nullable) f32 [m]. */

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstring>
+#include <limits>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -19,6 +20,7 @@ namespace sc {
 
 static thread_local std::string g_last_error;
 static std::atomic<int> g_bypass{0};
+std::atomic<uint64_t> g_launches{0};
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -239,7 +241,8 @@ static sc_status default_workspace(int dev, size_t need, void** out) {
 
 static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
                               const float* bias, uint8_t* mask_out, int32_t* ridx_out, int32_t* nrouted_out,
-                              void* ws, size_t ws_bytes, cudaStream_t stream, bool partial) {
+                              void* ws, size_t ws_bytes, cudaStream_t stream, bool partial,
+                              bool base_only = false) {
     if (m < 0) {
         set_error("sc_forward: negative token count");
         return SC_EINVAL;
@@ -268,7 +271,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         return SC_ENOMEM;
     }
     unsigned char* base = static_cast<unsigned char*>(ws);
-    const bool bypass_now = g_bypass.load() != 0;
+    const bool bypass_now = !base_only && g_bypass.load() != 0;
     if (use_fused(L, m)) {
         // one launch: router, x staging, base product and dW in the same kernel
         FusedArgs f;
@@ -327,7 +330,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
     uint8_t* mask = mask_out ? mask_out : reinterpret_cast<uint8_t*>(base + w.mask);
     int32_t* ridx = ridx_out ? ridx_out : reinterpret_cast<int32_t*>(base + w.ridx);
     int32_t* nrouted = nrouted_out ? nrouted_out : reinterpret_cast<int32_t*>(base + w.nrouted);
-    const bool bypass = g_bypass.load() != 0;
+    const bool bypass = bypass_now;
 
     RouterArgs r;
     r.x = x;
@@ -477,6 +480,7 @@ size_t sc_last_error(char* buf, size_t len) {
 }
 
 void sc_set_bypass_c_tarq(int on) { g_bypass.store(on ? 1 : 0); }
+uint64_t sc_launch_count(void) { return g_launches.load(); }
 
 void sc_test_drop_weight_copy(int on) { set_drop_weight_copy(on); }
 int sc_is_c_tarq_bypassed(void) { return g_bypass.load(); }
@@ -541,7 +545,28 @@ sc_status sc_layer_create(const sc_layer_desc* desc, sc_layer** out) {
     L.t8 = desc->t8;
     L.shard_kind = desc->shard_kind;
     int64_t r0 = 0, r1 = N, c0 = 0, c1 = K;
-    if (desc->shard_kind != SC_SHARD_NONE) {
+    if (desc->shard_kind != SC_SHARD_NONE && desc->shard_end > desc->shard_begin) {
+        // an explicit range: whole heads, or the intermediate slice shared with the next layer
+        const int64_t b = desc->shard_begin, en = desc->shard_end;
+        if (desc->shard_kind == SC_SHARD_COLUMNS) {
+            if (b < 0 || en > N || b % 16 != 0 || (en % 16 != 0 && en != N)) {
+                set_error("sc_layer_create: COLUMNS range must lie in [0, N) on multiples of 16");
+                return SC_EINVAL;
+            }
+            r0 = b;
+            r1 = en;
+        } else if (desc->shard_kind == SC_SHARD_ROWS) {
+            if (b < 0 || en > K || b % 64 != 0 || (en % 64 != 0 && en != K)) {
+                set_error("sc_layer_create: ROWS range must lie in [0, K) on multiples of 64");
+                return SC_EINVAL;
+            }
+            c0 = b;
+            c1 = en;
+        } else {
+            set_error("sc_layer_create: unknown shard kind");
+            return SC_EINVAL;
+        }
+    } else if (desc->shard_kind != SC_SHARD_NONE) {
         const int n = desc->shard_count, i = desc->shard_index;
         if (n <= 0 || i < 0 || i >= n) {
             set_error("sc_layer_create: bad shard index/count");
@@ -884,6 +909,70 @@ sc_status sc_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dty
     }
     cudaError_t e = launch_finalize(acc, m, n, y, y_dtype, bias, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "sc_finalize launch");
+    return SC_OK;
+}
+
+size_t sc_split_exchange_floats(const sc_layer* layer, int64_t m) {
+    if (!layer || m < 0) return 0;
+    return static_cast<size_t>(2 * m * layer->L.N + 3 * m);
+}
+
+sc_status sc_forward_split(const sc_layer* layer, const void* x, int x_dtype, int64_t m, float* exchange,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (!layer || !exchange || m < 0) {
+        set_error("sc_forward_split: bad argument");
+        return SC_EINVAL;
+    }
+    if (layer->L.shard_kind != SC_SHARD_ROWS) {
+        set_error("sc_forward_split: the layer is not a ROWS shard");
+        return SC_EINVAL;
+    }
+    if (m == 0) return SC_OK;
+    if (x_dtype != SC_F16 && x_dtype != SC_BF16) {
+        set_error("sc_forward_split: x dtype must be F16 or BF16");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(layer->L.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward_split: set device");
+    // the base product of the slice alone: the layer as an unsharded [N, K_slice] matrix whose
+    // thresholds (NaN) route no token
+    Layer B = layer->L;
+    B.shard_kind = SC_SHARD_NONE;
+    B.t4 = B.t8 = std::numeric_limits<float>::quiet_NaN();
+    void* ws = workspace;
+    size_t wsb = workspace_bytes;
+    if (!ws) {
+        wsb = plan_workspace(B, m).total;
+        sc_status st = default_workspace(B.device, wsb, &ws);
+        if (st != SC_OK) return st;
+    }
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    sc_status st = forward_impl(B, x, x_dtype, m, exchange, SC_F32, nullptr, nullptr, nullptr, nullptr, ws, wsb, s,
+                                true, true);
+    if (st != SC_OK) return st;
+    const int64_t mn = m * layer->L.N;
+    cudaError_t e = launch_split_extras(layer->L, x, x_dtype, m, exchange + mn, exchange + 2 * mn, s);
+    if (e != cudaSuccess) return cuda_fail(e, "sc_forward_split launch");
+    return SC_OK;
+}
+
+sc_status sc_finalize_split(const sc_layer* layer, const float* exchange, int64_t m, int ranks, void* y, int y_dtype,
+                            const float* bias, uint8_t* mask_out, uint32_t* undecided_out, void* stream) {
+    if (!layer || !exchange || !y || m < 0 || ranks < 1 ||
+        (y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32)) {
+        set_error("sc_finalize_split: bad argument");
+        return SC_EINVAL;
+    }
+    if (layer->L.shard_kind != SC_SHARD_ROWS) {
+        set_error("sc_finalize_split: the layer is not a ROWS shard");
+        return SC_EINVAL;
+    }
+    if (m == 0) return SC_OK;
+    DeviceGuard guard(layer->L.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_finalize_split: set device");
+    cudaError_t e = launch_split_finalize(layer->L, exchange, m, ranks, g_bypass.load() != 0 ? 1 : 0, y, y_dtype,
+                                          bias, mask_out, undecided_out, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "sc_finalize_split launch");
     return SC_OK;
 }
 

@@ -1658,6 +1658,7 @@ cudaError_t launch_decode_fused(const FusedArgs* f, int n, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = ksplit > 1 ? 2 : 1;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaLaunchKernelEx(&cfg, kern, g);
 }
 

@@ -536,9 +536,10 @@ __host__ __device__ inline RouteConsts route_consts(int64_t Kfull) {
     return RouteConsts{1.0 / n, nu / (1.0 - nu)};
 }
 
-__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, const RouteConsts& rc,
-                                            float t4, float t8, const void* xrow, int x_dtype, float* score_out,
-                                            double E1x = 0.0, double E2x = 0.0) {
+// The decision from the sums alone: 1 routed, 0 not routed, -1 when a threshold lies inside the
+// band (only the exact f32 chain decides then).  *var_out receives the f64 score.
+__device__ __forceinline__ int route_band(double S1, double S2, double SA, const RouteConsts& rc, float t4, float t8,
+                                          double E1x, double E2x, double* var_out) {
     const double u = 5.9604644775390625e-08;  // 2^-24
     const double inv_n = rc.inv_n;            // products with 1/n differ from quotients by f64 ulps, far inside B
     const double gam = rc.gam;
@@ -553,9 +554,19 @@ __device__ __forceinline__ bool route_token(double S1, double S2, double SA, int
     B = 2.0 * B + 1e-37;
     const double d4 = fabs(var - static_cast<double>(t4));
     const double d8 = fabs(var - static_cast<double>(t8));
-    if (isfinite(var) && isfinite(B) && !(d4 <= B) && !(d8 <= B)) {
+    *var_out = var;
+    if (isfinite(var) && isfinite(B) && !(d4 <= B) && !(d8 <= B)) return route_rule_f64(var, t4, t8) ? 1 : 0;
+    return -1;
+}
+
+__device__ __forceinline__ bool route_token(double S1, double S2, double SA, int64_t Kfull, const RouteConsts& rc,
+                                            float t4, float t8, const void* xrow, int x_dtype, float* score_out,
+                                            double E1x = 0.0, double E2x = 0.0) {
+    double var;
+    const int d = route_band(S1, S2, SA, rc, t4, t8, E1x, E2x, &var);
+    if (d >= 0) {
         if (score_out) *score_out = static_cast<float>(var);
-        return route_rule_f64(var, t4, t8);
+        return d == 1;
     }
     const float score = exact_variance(xrow, x_dtype, Kfull);
     if (score_out) *score_out = score;

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "saccade_ctarq.h"
@@ -106,6 +107,9 @@ sc_status cuda_fail(cudaError_t e, const char* what);
 // Launch with programmatic stream serialization (PDL): the kernel may start while the
 // previous kernel on the stream finishes; it must call griddepcontrol.wait before touching
 // anything that kernel writes or reads.
+// Kernels this library has launched (host-side count of launch calls, sc_launch_count).
+extern std::atomic<uint64_t> g_launches;
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                        Args&&... args) {
@@ -119,6 +123,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
@@ -269,6 +274,12 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s);
 // Test hook: the next router-fused decode launches leave CTA 0's first weight stage unissued.
 void set_drop_weight_copy(int on);
 
+// Exchange step of a ROWS shard that holds only its input slice (sc_split.cu).
+cudaError_t launch_split_extras(const Layer& L, const void* x, int x_dtype, int64_t m, float* y_delta, float* stats,
+                                cudaStream_t s);
+cudaError_t launch_split_finalize(const Layer& L, const float* exch, int64_t m, int ranks, int route_all, void* y,
+                                  int y_dtype, const float* bias, uint8_t* mask_out, uint32_t* undecided,
+                                  cudaStream_t s);
 cudaError_t launch_finalize(const float* acc, int64_t m, int64_t n, void* y, int y_dtype, const float* bias,
                             cudaStream_t s);
 

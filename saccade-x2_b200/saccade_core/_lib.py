@@ -41,6 +41,8 @@ class ScLayerDesc(ctypes.Structure):
         ("shard_kind", ctypes.c_int),
         ("shard_index", ctypes.c_int),
         ("shard_count", ctypes.c_int),
+        ("shard_begin", ctypes.c_int64),
+        ("shard_end", ctypes.c_int64),
     ]
 
 
@@ -98,6 +100,10 @@ SIGNATURES = {
     "sc_forward_group": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_forward_partial": (_int, [_vp, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_finalize": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
+    "sc_split_exchange_floats": (ctypes.c_size_t, [_vp, _i64]),
+    "sc_forward_split": (_int, [_vp, _vp, _int, _i64, _vp, _vp, ctypes.c_size_t, _vp]),
+    "sc_finalize_split": (_int, [_vp, _vp, _i64, _int, _vp, _int, _vp, _vp, _vp, _vp]),
+    "sc_launch_count": (ctypes.c_uint64, []),
     "sc_variance_heuristic": (_int, [_vp, _int, _i64, _i64, _vp, _vp]),
     "sc_percentile_threshold": (_int, [_vp, _i64, _i64, _f32, ctypes.POINTER(_f32), _vp]),
     "sc_compress": (_int, [_vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _i64, ctypes.POINTER(_i64),

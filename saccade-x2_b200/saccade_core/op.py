@@ -72,15 +72,19 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 
 
 class _Workspaces:
-    """Zero-filled workspaces keyed by (device, stream); grown on demand."""
+    """Zero-filled workspaces keyed by (device, stream); grown on demand.  A replaced workspace is
+    kept alive: a CUDA graph captured with it still writes there when replayed."""
 
     def __init__(self):
         self._ws = {}
+        self._retired = []
 
     def get(self, device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor:
         key = (device.index, stream.cuda_stream)
         ws = self._ws.get(key)
         if ws is None or ws.numel() < nbytes:
+            if ws is not None:
+                self._retired.append(ws)
             ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
             self._ws[key] = ws
         return ws
@@ -106,7 +110,8 @@ class SaccadeLinearOp:
     mode "fast" (tensor cores, default), "fast_tc" (the same contract; decode dequantises the
     weights into tensor memory for tcgen05 MMAs), "fast_tc8" (as fast_tc, one-token decode on fp8
     tcgen05 MMAs with an exact e4m3 split of x) or "exact" (op.rs's f32 order, bit-identical).
-    shard=("columns"|"rows", index, count) keeps a tensor-parallel slice.
+    shard=("columns"|"rows", index, count) keeps a tensor-parallel slice; ("columns_range"|"rows_range",
+    begin, end) keeps exactly output rows / input columns [begin, end).
     """
 
     NAME = "fused_c_tarq_saccade_linear"
@@ -166,9 +171,13 @@ class SaccadeLinearOp:
         d.buffers_on_device = 1 if on_dev else 0
         d.mode = _mode_code(mode)
         if shard is not None:
-            kind, idx, cnt = shard
-            d.shard_kind = {"columns": _lib.SC_SHARD_COLUMNS, "rows": _lib.SC_SHARD_ROWS}[kind]
-            d.shard_index, d.shard_count = int(idx), int(cnt)
+            kind, a, b = shard
+            base_kind = kind[:-6] if kind.endswith("_range") else kind
+            d.shard_kind = {"columns": _lib.SC_SHARD_COLUMNS, "rows": _lib.SC_SHARD_ROWS}[base_kind]
+            if kind.endswith("_range"):
+                d.shard_begin, d.shard_end = int(a), int(b)
+            else:
+                d.shard_index, d.shard_count = int(a), int(b)
         if on_dev:
             torch.cuda.synchronize(self.device)
         h = ctypes.c_void_p()
@@ -179,7 +188,10 @@ class SaccadeLinearOp:
         self.info = info
         self.out_features = int(info.out_features)
         self.in_features = int(info.in_features)
-        self.shard_kind = shard[0] if shard else None
+        self.shard_kind = (shard[0][:-6] if shard[0].endswith("_range") else shard[0]) if shard else None
+        self.col_begin = int(info.col_begin)
+        self.row_begin = int(info.row_begin)
+        self.undecided = torch.zeros(1, dtype=torch.int32, device=self.device)  # split routing, see finalize_split
         self.mode = mode
 
     # ------------------------------------------------------------------ surface of op.rs
@@ -272,6 +284,46 @@ class SaccadeLinearOp:
                                          _ptr(mask), None, None, ws.data_ptr(), ws.numel(),
                                          ctypes.c_void_p(stream.cuda_stream)))
         return (y, mask) if return_routing else y
+
+
+    def exchange_size(self, m: int) -> int:
+        """f32 elements of the split exchange buffer for m tokens: [y_base m*N | y_delta m*N | stats m*3]."""
+        return int(LIB.sc_split_exchange_floats(self._h, int(m)))
+
+    def forward_split(self, x_slice: torch.Tensor, exchange: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Rows shard, tensor parallelism without the whole token: x_slice [..., K_slice] (this shard's
+        input columns only) -> the f32 exchange buffer to be summed over the ranks (all-reduce), then
+        passed to finalize_split."""
+        if self.shard_kind != "rows":
+            raise ValueError("forward_split needs a rows shard")
+        m = self._prep_x(x_slice, self.in_features)
+        size = self.exchange_size(m)
+        if exchange is None:
+            exchange = torch.empty(size, dtype=torch.float32, device=self.device)
+        elif exchange.numel() < size or exchange.dtype != torch.float32 or not exchange.is_contiguous():
+            raise ValueError(f"exchange must be a contiguous f32 tensor of >= {size} elements")
+        if m > 0:
+            stream = torch.cuda.current_stream(self.device)
+            need = self.workspace_size(m)
+            ws = WORKSPACES.get(self.device, stream, need)
+            check(LIB.sc_forward_split(self._h, x_slice.data_ptr(), _DT[x_slice.dtype], m, exchange.data_ptr(),
+                                       ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream)))
+        return exchange
+
+    def finalize_split(self, exchange: torch.Tensor, m: int, ranks: int, *, out_dtype=torch.float16,
+                       bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                       return_routing: bool = False):
+        """The summed exchange buffer -> y [m, N]: routed on the summed router sums, f16-rounded, bias
+        after.  Tokens whose decision the f32 error bound leaves open add to self.undecided."""
+        y = out if out is not None else torch.empty((m, self.out_features), dtype=out_dtype, device=self.device)
+        mask = torch.empty(max(m, 1), dtype=torch.uint8, device=self.device) if return_routing else None
+        if bias is not None:
+            bias = bias.to(device=self.device, dtype=torch.float32).contiguous()
+        if m > 0:
+            check(LIB.sc_finalize_split(self._h, exchange.data_ptr(), int(m), int(ranks), y.data_ptr(),
+                                        _DT[y.dtype], _ptr(bias), _ptr(mask), self.undecided.data_ptr(),
+                                        ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+        return (y, mask[:m]) if return_routing else y
 
 
 def finalize(acc: torch.Tensor, *, out_dtype=torch.float16, bias: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -18,9 +18,11 @@ state (x = hi + lo to 2^-22 relative).
 
 Tensor parallelism (tp = (rank, world, group)): q/k/v and gate/up keep this rank's output rows
 (whole heads; a KV head shared by two ranks when there are fewer KV heads than ranks), o and down
-keep the matching input columns and produce f32 partial sums, all-reduced over the group (NCCL)
-before the residual add; the row-sharded layers route on the whole token: each rank's partial
-carries its slice's router sums, all-reduced with it, and the decision is taken after the sum.
+keep the matching input columns.  A row-sharded layer sees only its slice of each token, so it
+writes one f32 exchange buffer [y_base | y_delta | router sums] (sc_forward_split), the buffers are
+summed over the group by one NCCL all-reduce, and sc_finalize_split routes every token on the
+summed sums and rounds.  The lm_head is vocab-parallel: each rank scores its slice of the
+vocabulary and greedy decoding all-gathers each rank's (max, argmax) per sequence.
 """
 from __future__ import annotations
 
@@ -106,6 +108,14 @@ def head_split(cfg: Qwen2Config, rank: int, world: int):
     q0 = kv * G + (G * j) // share
     q1 = kv * G + (G * (j + 1)) // share
     return q0, q1, kv, kv + 1
+
+
+def vocab_split(cfg: Qwen2Config, rank: int, world: int):
+    """This rank's lm_head rows [v0, v1) (multiples of 64 except the last end)."""
+    vb = (cfg.vocab + 63) // 64
+    v0 = (vb * rank // world) * 64
+    v1 = min(cfg.vocab, (vb * (rank + 1) // world) * 64) if rank + 1 < world else cfg.vocab
+    return v0, v1
 
 
 def inter_split(cfg: Qwen2Config, rank: int, world: int):
@@ -211,7 +221,11 @@ class Qwen2Model:
             self.layers.append(L)
         self.final_norm = ck.final_norm.float().contiguous()
         self.embed = ck.embed.contiguous()
-        self.lm_head_t = (ck.embed if ck.lm_head is None else ck.lm_head).t()  # [hidden, vocab] view, f16
+        self.v0, self.v1 = vocab_split(cfg, self.rank, self.world)
+        table = ck.embed if ck.lm_head is None else ck.lm_head
+        if self.world > 1:
+            table = table[self.v0:self.v1].contiguous()
+        self.lm_head_t = table.t()  # [hidden, vocab slice] view, f16
         cos, sin = rope_tables(cfg, max_pos)
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
@@ -242,8 +256,8 @@ class Qwen2Model:
     def forward_tokens(self, ids: torch.Tensor, slot: torch.Tensor, pos: torch.Tensor, last: torch.Tensor,
                        max_query_pos: int) -> torch.Tensor:
         """Runs T tokens (ids [T] int64, cache slot [T] and position [T] int32) through the model,
-        appending their keys and values; returns the f32 logits [len(last), vocab] of the tokens
-        at indices `last` (int64)."""
+        appending their keys and values; returns the f32 logits [len(last), v1 - v0] of the tokens
+        at indices `last` (int64) over this rank's vocabulary slice [v0, v1) (all of it on one GPU)."""
         cfg, dev = self.cfg, self.device
         T = ids.numel()
         H, hd = cfg.hidden, cfg.head_dim
@@ -299,11 +313,11 @@ class Qwen2Model:
         if self.world == 1:
             op.forward(x16, out_dtype=torch.float32, out=out_f32)
             return
-        T, n = x16.shape[0], op.out_features
-        part = self._buf(key + ("part",), (2 * T * n + 3 * T * 2,), torch.float32)
+        T = x16.shape[0]
+        part = self._buf(key + ("part",), (op.exchange_size(T),), torch.float32)
         op.forward_split(x16, part)
         self._all_reduce(part)
-        op.finalize_split(part, T, out_f32)
+        op.finalize_split(part, T, self.world, out=out_f32)
 
     def _lm_head(self, xn: torch.Tensor) -> torch.Tensor:
         """logits = x . W^T with f16 W: x = hi + lo (f16 each), two f16 GEMMs with f32 accumulation."""
@@ -314,6 +328,12 @@ class Qwen2Model:
         hilo[nl:].copy_((xn - hi.float()).to(torch.float16))
         p = torch.mm(hilo, self.lm_head_t, out_dtype=torch.float32)
         return p[:nl] + p[nl:]
+
+    def undecided_routes(self) -> int:
+        """Row-layer tokens routed on the f64 score inside the f32 error bound (tensor parallel only)."""
+        if self.world == 1:
+            return 0
+        return int(sum(int(L[n].undecided.item()) for L in self.layers for n in ("o", "down")))
 
     def check_device(self):
         for L in self.layers:
@@ -371,7 +391,8 @@ def prefill_indices(prompt: torch.Tensor):
 
 class GreedyDecoder:
     """Prefill, then greedy decoding one token per sequence per step (verify.rs:98-130), each decode
-    step replayed as one CUDA graph: token ids in, argmax token ids out."""
+    step replayed as one CUDA graph: token ids in, argmax token ids out (the step also copies them
+    to its own input, so back-to-back replays decode autonomously)."""
 
     def __init__(self, model: Qwen2Model, batch: int):
         self.model = model
@@ -385,56 +406,97 @@ class GreedyDecoder:
         self.logits = None
         self.graph = None
         self.stream = torch.cuda.Stream(device=dev)
+        if model.world > 1:
+            self._cand = torch.zeros(batch, 2, dtype=torch.float32, device=dev)
+            self._gath = torch.zeros(model.world, batch, 2, dtype=torch.float32, device=dev)
 
-    def prefill(self, prompt: torch.Tensor) -> torch.Tensor:
+    def argmax(self, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Greedy token of each row: over this rank's vocabulary slice, then (tensor parallel) the
+        first of the ranks' maxima, so ties go to the smallest id as with one argmax."""
+        m = self.model
+        if m.world == 1:
+            return torch.argmax(logits, dim=-1, out=out)
+        val, idx = torch.max(logits, dim=-1)
+        self._cand[:, 0].copy_(val)
+        self._cand[:, 1].copy_(idx + m.v0)  # ids < 2^24 are exact in f32
+        torch.distributed.all_gather_into_tensor(self._gath, self._cand, group=m.group)
+        best = torch.argmax(self._gath[:, :, 0], dim=0)  # first rank holding the maximum
+        out.copy_(self._gath[:, :, 1].gather(0, best[None, :])[0].to(torch.int64))
+        return out
+
+    def prefill(self, prompt: torch.Tensor, chunk: int = 0) -> torch.Tensor:
+        """Runs the prompts [B, S] (`chunk` sequences per pass, all at once by default) and returns the
+        greedy first tokens [B]."""
         m = self.model
         B, S = prompt.shape
-        ids, slot, pos = prefill_indices(prompt.to(m.device))
-        last = torch.arange(B, device=m.device, dtype=torch.int64) * S + (S - 1)
-        logits = m.forward_tokens(ids, slot, pos, last, S - 1)
+        chunk = chunk or B
+        first = torch.empty(B, dtype=torch.int64, device=m.device)
+        self.prefill_logits = []
+        for b0 in range(0, B, chunk):
+            b1 = min(B, b0 + chunk)
+            ids, slot, pos = prefill_indices(prompt[b0:b1].to(m.device))
+            slot += b0
+            last = torch.arange(b1 - b0, device=m.device, dtype=torch.int64) * S + (S - 1)
+            logits = m.forward_tokens(ids, slot, pos, last, S - 1)
+            self.argmax(logits, first[b0:b1])
+            self.prefill_logits.append(logits)
         self.pos.fill_(S)
-        return logits
+        self.next.copy_(first)
+        self.ids.copy_(first)
+        return first
 
     def _step(self):
         self.logits = self.model.forward_tokens(self.ids, self.slot, self.pos, self.last, self.model.max_pos - 1)
-        torch.argmax(self.logits, dim=-1, out=self.next)
+        self.argmax(self.logits, self.next)
+        self.ids.copy_(self.next)
         self.pos.add_(1)
 
     def capture(self):
-        """Records one decode step as a CUDA graph (after one eager step that sizes the buffers)."""
+        """Records one decode step as a CUDA graph, after the prefill (whose larger calls size the
+        workspaces first), following one eager step that sizes the step's buffers (its cache writes
+        are rewritten by the first replay at the same position)."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.model.device))
+        ids0 = self.ids.clone()
         with torch.cuda.stream(self.stream):
             self._step()
             self.pos.sub_(1)
+            self.ids.copy_(ids0)
         self.stream.synchronize()
+        self.launches_per_step = int(LIB.sc_launch_count())
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, stream=self.stream):
             self._step()
+        self.launches_per_step = int(LIB.sc_launch_count()) - self.launches_per_step
         self.stream.synchronize()
 
     def step(self, ids: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """One decode step: ids [B] (device; default: the previous step's argmax) -> argmax ids [B]."""
-        if ids is not None:
-            self.ids.copy_(ids)
-        else:
-            self.ids.copy_(self.next)
+        """One decode step on the decoder's stream: ids [B] (device or pinned host; default: the
+        previous step's argmax, already in place) -> argmax ids [B] (device)."""
         with torch.cuda.stream(self.stream):
+            if ids is not None:
+                self.ids.copy_(ids, non_blocking=True)
             if self.graph is not None:
                 self.graph.replay()
             else:
                 self._step()
         return self.next
 
-    def generate(self, prompt: torch.Tensor, steps: int, record_logits: bool = False):
-        """Greedy tokens [B, steps] (and the top-2 logit gap of each step when record_logits)."""
-        first = self.prefill(prompt)
-        tok = torch.argmax(first, dim=-1)
-        out, gaps = [tok.clone()], []
-        if record_logits:
-            top = torch.topk(first, 2, dim=-1).values
-            gaps.append((top[:, 0] - top[:, 1]).cpu())
-        self.ids.copy_(tok)
+    def generate(self, prompt: torch.Tensor, steps: int, record_logits: bool = False, chunk: int = 0,
+                 graph: bool = True):
+        """Greedy tokens [B, steps] (and the top-2 logit gap of each step when record_logits; one GPU),
+        each decode step a replay of the captured graph unless graph=False."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.model.device))
+        with torch.cuda.stream(self.stream):
+            tok = self.prefill(prompt, chunk)
+            out, gaps = [tok.clone()], []
+            if record_logits:
+                first = torch.cat(self.prefill_logits)
+                top = torch.topk(first, 2, dim=-1).values
+                gaps.append((top[:, 0] - top[:, 1]).cpu())
+        if graph and self.graph is None:
+            self.capture()
         for _ in range(steps - 1):
-            nxt = self.step(self.ids if not out else out[-1])
+            nxt = self.step()
             self.stream.synchronize()
             out.append(nxt.clone())
             if record_logits:

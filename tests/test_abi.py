@@ -45,7 +45,9 @@ def test_host_only_calls():
     from saccade_core import _lib
     L = _lib.LIB
     assert L.sc_op_name() == b"fused_c_tarq_saccade_linear"
-    assert L.sc_abi_version() == 1
+    assert L.sc_abi_version() == 2  # 2: explicit shard ranges in sc_layer_desc
+    assert ctypes.sizeof(_lib.ScLayerDesc) == 120  # the C struct's size on x86-64
+    assert isinstance(L.sc_launch_count(), int)
     L.sc_set_bypass_c_tarq(1)
     assert L.sc_is_c_tarq_bypassed() == 1
     L.sc_set_bypass_c_tarq(0)

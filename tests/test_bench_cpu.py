@@ -40,7 +40,7 @@ def _run(cmd, env=None):
 
 
 def test_reference_arm_json_line():
-    r = _run(["--impl", "reference", "--steps", "2", "--warmup", "1", "--layers", "1"])
+    r = _run(["--workload", "linear", "--impl", "reference", "--steps", "2", "--warmup", "1", "--layers", "1"])
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
     d = json.loads(lines[-1])
@@ -51,8 +51,21 @@ def test_reference_arm_json_line():
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
     calls = bench.stack_spec(1, 1, 0.25, seed=1234)
-    want = bench.workload_config(bench.parse(["--layers", "1"]), calls, d["config"]["bytes_per_step"])
+    want = bench.workload_config(bench.parse(["--workload", "linear", "--layers", "1"]), calls,
+                                 d["config"]["bytes_per_step"])
     assert d["config"] == want
+
+
+def test_reference_arm_decode_json_line():
+    """The default workload's reference arm: Qwen2-7B decode tok/s of the CPU algorithm, per layer."""
+    r = _run(["--impl", "reference", "--steps", "2", "--warmup", "1", "--cpu-seconds", "0.3"])
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads([ln for ln in r.stdout.splitlines() if ln.strip()][-1])
+    assert REQUIRED <= set(d)
+    assert d["metric"] == "Qwen2-7B decode tok/s" and d["unit"] == "tok/s" and d["impl"] == "reference"
+    assert d["value"] > 0 and d["steps"] == 2 and d["warmup"] == 1 and d["scaling"] == "strong"
+    assert d["config"] == bench.decode_config(bench.parse([]), 1)
+    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 
 def test_reference_arm_other_ranks_print_nothing():

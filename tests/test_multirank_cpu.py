@@ -1,11 +1,12 @@
 """The row-sharded (tensor-parallel) path on two ranks over gloo, on the CPU.
 
-Each rank takes its slice of the input columns of a compressed layer (the column ranges a
-ROWS shard of sc_layer_create keeps: K * r / n rounded to 64), routes on the whole token as every
-shard must, computes its f32 partial with the oracle, and the ranks all-reduce (sum) the
-partials -- the exchange step of the sharded layer.  The sum must match the unsharded oracle
-within the fast-path tolerance (only the f32 summation order changes) and the routing masks must
-be identical on every rank."""
+Whole-token form (sc_forward_partial): each rank takes its slice of the input columns of a
+compressed layer (the column ranges a ROWS shard of sc_layer_create keeps: K * r / n rounded up to
+64), routes on the whole token, computes its f32 partial with the oracle, and the ranks all-reduce
+(sum) the partials.  Slice-only form (sc_forward_split): each rank sees only its slice and
+all-reduces one [y_base | y_delta | router sums] vector, then every rank routes on the summed sums
+(oracle/split_oracle.py restates the three steps).  Both must match the unsharded oracle within
+the fast-path tolerance (only the f32 summation order changes) with identical routing masks."""
 import os
 import socket
 
@@ -42,6 +43,16 @@ def column_slice(c, k0, k1):
                         np.array(vals, dtype=np.uint8), c.delta_scale, n, k1 - k0)
 
 
+def rows_shard_columns(k, rank, world):
+    """Input columns [k0, k1) of ROWS shard `rank` of `world`, as sc_layer_create computes them
+    (K * i / n rounded up to a multiple of 64, the last shard ending at K)."""
+    def up64(v):
+        return (v + 63) // 64 * 64
+    k0 = min(k, up64(k * rank // world))
+    k1 = k if rank + 1 == world else min(k, up64(k * (rank + 1) // world))
+    return k0, k1
+
+
 def _rank(rank, world, port, q):
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
@@ -55,9 +66,7 @@ def _rank(rank, world, port, q):
         case = make_case(192, 1024, 6, 0.03, seed=77, boost=[1, 4])
         full = case.oracle()
         _, routed_full, _ = full.forward(case.x_bits)
-        kb = case.k // 64
-        k0 = (kb * rank // world) * 64
-        k1 = (kb * (rank + 1) // world) * 64 if rank + 1 < world else case.k
+        k0, k1 = rows_shard_columns(case.k, rank, world)
         part = O.OracleLinear(column_slice(case.c, k0, k1), case.t4, case.t8)
         _, routed, acc = part.forward(np.ascontiguousarray(case.x_bits[:, k0:k1]), force_route=routed_full)
         t = torch.from_numpy(acc.copy())
@@ -128,6 +137,16 @@ def _mlp_layers():
     return gate, up, down, x.astype(np.float16).view(np.uint16)
 
 
+def _down_threshold():
+    """The down router threshold of the MLP case: between the unboosted and the boosted token's
+    variance of h (computed on the unsharded oracle, as calibration would)."""
+    from oracle import oracle as O
+    gate, up, _, xb = _mlp_layers()
+    g, _, _ = O.OracleLinear(gate, 8.0, 3e38).forward(xb)
+    u, _, _ = O.OracleLinear(up, 8.0, 3e38).forward(xb)
+    return _down_route(_silu_mul(g, u))[0]
+
+
 def _down_route(h_bits):
     """Threshold between the unboosted and the boosted token's variance of h, and the mask."""
     from oracle import oracle as O
@@ -142,6 +161,7 @@ def _mlp_rank(rank, world, port, q):
     sys.path.insert(0, here)
     sys.path.insert(0, os.path.dirname(here))
     from oracle import oracle as O
+    from oracle import split_oracle as S
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
@@ -152,18 +172,14 @@ def _mlp_rank(rank, world, port, q):
         g, _, _ = O.OracleLinear(row_slice(gate, r0, r1), 8.0, 3e38).forward(xb)
         u, _, _ = O.OracleLinear(row_slice(up, r0, r1), 8.0, 3e38).forward(xb)
         h_part = _silu_mul(g, u)
-        # down routes on the whole token: gather h (the router needs all of K); the f16 bit
-        # patterns travel as int32 (gloo has no 16-bit integer type)
-        parts = [torch.zeros(h_part.shape, dtype=torch.int32) for _ in range(world)]
-        dist.all_gather(parts, torch.from_numpy(h_part.astype(np.int32)))
-        h = np.concatenate([p.numpy().astype(np.uint16) for p in parts], axis=1)
-        t4, routed = _down_route(h)
-        # row-parallel down over this rank's K slice, then the sum over ranks
-        _, _, acc = O.OracleLinear(column_slice(down, r0, r1), t4, 3e38).forward(
-            np.ascontiguousarray(h[:, r0:r1]), force_route=routed)
-        t = torch.from_numpy(acc.copy())
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        q.put((rank, g, u, h, routed, t.numpy()))
+        # row-parallel down on this rank's slice of h only: one all-reduce of the exchange vector,
+        # then the routing decision on the summed router sums (no gather of h)
+        t4 = _down_threshold()
+        ex = torch.from_numpy(S.split_exchange(column_slice(down, r0, r1), h_part))
+        dist.all_reduce(ex, op=dist.ReduceOp.SUM)
+        y, routed, undecided = S.split_finalize(ex.numpy(), h_part.shape[0], down.out_features, inter, world,
+                                                t4, 3e38)
+        q.put((rank, g, u, h_part, routed, y, undecided))
     finally:
         dist.destroy_process_group()
 
@@ -194,10 +210,62 @@ def test_tensor_parallel_mlp_two_ranks():
     y, rd, acc_ref = O.OracleLinear(down, t4, 3e38).forward(h)
     assert rd.tolist() == [0, 0, 0, 1, 0]
     inter = gate.out_features
-    for rank, g_r, u_r, h_r, routed_r, acc in results:
+    for rank, g_r, u_r, h_r, routed_r, y_r, undecided in results:
         r0, r1 = inter * rank // world, inter * (rank + 1) // world
         assert np.array_equal(g_r, g[:, r0:r1]) and np.array_equal(u_r, u[:, r0:r1]), "rows are independent"
-        assert np.array_equal(h_r, h) and np.array_equal(routed_r, rd)
-        assert_acc_close(acc, acc_ref, f"tp mlp rank {rank}")
-        assert_fast_close(acc.astype(np.float16).view(np.uint16), y, f"tp mlp rank {rank} y")
-    assert np.array_equal(results[0][5], results[1][5]), "every rank holds the same reduced sum"
+        assert np.array_equal(h_r, h[:, r0:r1])
+        assert undecided == 0 and np.array_equal(routed_r, rd), "routed on the summed sums as on whole tokens"
+        assert_fast_close(y_r, y, f"tp mlp rank {rank} y")
+    assert np.array_equal(results[0][5], results[1][5]), "every rank holds the same output"
+
+
+def _split_rank(rank, world, port, q, bypass):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    sys.path.insert(0, os.path.dirname(here))
+    from oracle import split_oracle as S
+    from ctarq_cases import make_case
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        case = make_case(160, 1280, 9, 0.02, seed=78, boost=[0, 5, 6], thresholds=(8.0, 3e38))
+        k0, k1 = rows_shard_columns(case.k, rank, world)
+        ex = torch.from_numpy(S.split_exchange(S.slice_columns(case.c, k0, k1),
+                                               np.ascontiguousarray(case.x_bits[:, k0:k1])))
+        dist.all_reduce(ex, op=dist.ReduceOp.SUM)
+        q.put((rank,) + S.split_finalize(ex.numpy(), case.m, case.n, case.k, world, case.t4, case.t8, bypass))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,bypass", [(2, False), (3, False), (2, True)])
+def test_split_exchange_ranks(world, bypass):
+    """The three-step exchange over gloo ranks equals the unsharded oracle: same routing mask, y
+    within the fast-path tolerance, every rank the same result, no undecided token."""
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, here)
+    from ctarq_cases import assert_fast_close, make_case
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_rank, args=(r, world, port, q, bypass)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = sorted([q.get(timeout=120) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    case = make_case(160, 1280, 9, 0.02, seed=78, boost=[0, 5, 6], thresholds=(8.0, 3e38))
+    y_ref, r_ref, _ = case.oracle().forward(case.x_bits, bypass=bypass)
+    if bypass:  # the dense path: every token takes base + dW (the library reports them all routed)
+        r_ref = np.ones(case.m, dtype=np.uint8)
+    else:
+        assert r_ref.tolist() == [1, 0, 0, 0, 0, 1, 1, 0, 0]
+    for _, y, routed, undecided in results:
+        assert undecided == 0
+        assert np.array_equal(routed, r_ref)
+        assert_fast_close(y, y_ref, f"split exchange over {world} ranks")
+    for r in results[1:]:
+        assert np.array_equal(r[1], results[0][1])

@@ -109,8 +109,8 @@ def _greedy_pair(q2, cfg, seed, prompt_len, steps, mode="fast"):
     prompt = rng.integers(0, cfg.vocab, prompt_len)
     model = q2.Qwen2Model(ck, max_batch=1, max_pos=prompt_len + steps, mode=mode)
     dec = q2.GreedyDecoder(model, 1)
-    dec.capture()
     toks, gaps = dec.generate(torch.from_numpy(prompt[None]).cuda(), steps, record_logits=True)
+    assert dec.graph is not None and dec.launches_per_step > 0
     torch.cuda.synchronize()
     model.check_device()
     orc = oracle_model(ck, prompt_len + steps)
