@@ -674,11 +674,13 @@ def run_decode(args, rank, world):
     clocks = ClockSampler(dev)
     clocks.start()
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("decode_steps")
     with torch.cuda.stream(dec.stream):
         s_ev.record()
         for _ in range(args.steps):
             dec.graph.replay()
         e_ev.record()
+    torch.cuda.nvtx.range_pop()
     dec.stream.synchronize()
     clk = clocks.stop()
     barrier()

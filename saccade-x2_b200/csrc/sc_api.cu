@@ -242,7 +242,7 @@ static sc_status default_workspace(int dev, size_t need, void** out) {
 static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_t m, void* y, int y_dtype,
                               const float* bias, uint8_t* mask_out, int32_t* ridx_out, int32_t* nrouted_out,
                               void* ws, size_t ws_bytes, cudaStream_t stream, bool partial,
-                              bool base_only = false) {
+                              bool base_only = false, bool reuse_route = false) {
     if (m < 0) {
         set_error("sc_forward: negative token count");
         return SC_EINVAL;
@@ -352,8 +352,11 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
     r.perm = w.gemm_ks > 0 ? reinterpret_cast<int32_t*>(base + w.perm) : nullptr;
     r.counter = reinterpret_cast<uint32_t*>(base + w.counter);
     r.status = L.status;
-    cudaError_t e = launch_router(r, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "router launch");
+    cudaError_t e = cudaSuccess;
+    if (!reuse_route) {  // else the staged x, routing and token order of the previous call stand
+        e = launch_router(r, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "router launch");
+    }
 
     DecodeArgs d;
     d.L = &L;
@@ -397,6 +400,7 @@ static sc_status forward_impl(const Layer& L, const void* x, int x_dtype, int64_
         g.y_dtype = partial ? SC_F32 : y_dtype;
         g.bias = partial ? nullptr : bias;
         g.partial_out = partial ? 1 : 0;
+        g.skip_gather = reuse_route ? 1 : 0;
         e = launch_gemm(g, stream);
         if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
         return SC_OK;
@@ -1186,6 +1190,40 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
         a.rtcount = reinterpret_cast<uint32_t*>(base + 256);
         const cudaError_t e = launch_mid(a, s);
         if (e != cudaSuccess) return cuda_fail(e, "grouped 9..64-token GEMM launch");
+        return SC_OK;
+    }
+    // prefill GEMM regime: layers reading the same x with the same thresholds share one router and
+    // one token gather (their masks are the same); the others reuse what the first left in the workspace
+    bool share = n > 1 && workspace && L0.mode != SC_MODE_EXACT && L0.shard_kind != SC_SHARD_ROWS &&
+                 g_bypass.load() == 0;
+    for (int i = 0; i < n && share; ++i) {
+        const Layer& L = group->layers[i]->L;
+        share = L.K == L0.K && L.fullK == L0.fullK && L.mode == L0.mode && L.shard_kind == L0.shard_kind &&
+                L.t4 == L0.t4 && L.t8 == L0.t8 && !use_fused(L, m) && !use_mid(L, m) && m >= kGemmMinTokens &&
+                workspace_bytes >= plan_workspace(L, m).total;
+    }
+    if (share) {
+        for (int i = 0; i < n; ++i) {
+            if (!y[i]) {
+                set_error("sc_forward_group: null output " + std::to_string(i));
+                return SC_EINVAL;
+            }
+            const sc_status st = forward_impl(group->layers[i]->L, x, x_dtype, m, y[i], y_dtype, bias ? bias[i] : nullptr,
+                                              nullptr, nullptr, nullptr, workspace, workspace_bytes, s, false, false,
+                                              i > 0);
+            if (st != SC_OK) return st;
+        }
+        const WsLayout w = plan_workspace(L0, m);
+        const unsigned char* base = static_cast<const unsigned char*>(workspace);
+        for (int i = 0; i < n; ++i) {
+            cudaError_t e = cudaSuccess;
+            if (mask_out && mask_out[i]) e = cudaMemcpyAsync(mask_out[i], base + w.mask, m, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && routed_idx_out && routed_idx_out[i])
+                e = cudaMemcpyAsync(routed_idx_out[i], base + w.ridx, 4 * m, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess && n_routed_out && n_routed_out[i])
+                e = cudaMemcpyAsync(n_routed_out[i], base + w.nrouted, 4, cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) return cuda_fail(e, "sc_forward_group: routing outputs");
+        }
         return SC_OK;
     }
     for (int i = 0; i < n; ++i) {

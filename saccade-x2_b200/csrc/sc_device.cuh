@@ -578,4 +578,201 @@ __device__ __forceinline__ bool route_token(double S1, double S2, double SA, int
     return route_token(S1, S2, SA, Kfull, route_consts(Kfull), t4, t8, xrow, x_dtype, score_out, E1x, E2x);
 }
 
+// ---------------------------------------------------------------- parallel exact replay
+//
+// The reference's score of a token whose f64 score lies inside the error band, computed by a whole
+// CTA instead of one thread walking K dependent f32 adds (heuristics.rs:3-14).
+//
+// Sum of squares (terms v_i = x_i^2, exact in f32, all >= 0): while the running f32 sum q stays in
+// one binade [2^B, 2^(B+1)) its grid is g = 2^(B-23) and every step adds an integer number of g:
+// q_i = q_(i-1) + g * r_i with r_i = v_i / g rounded to nearest, ties to the even result (so a tie's
+// r_i depends on the parity of q / g).  The exact prefix sums P_i bound the chain, |q_i - P_i| <=
+// gamma_i P_i for non-negative terms, so a step is provably inside binade B when P_(i-1)(1 - gamma)
+// >= 2^B and P_i + gamma P_(i-1) < 2^(B+1).  Each thread takes a contiguous chunk, computes its
+// offsets by a block scan of the P_i, and summarises its chunk as items in order: runs of such steps
+// of one binade (the sum of r_i for either parity of q / g at the run's start) and ranges of the
+// other steps (binade crossings, leading zeros), at most kReplayItems per thread (the rest of a
+// chunk becomes one range).  One thread then walks the items: a run adds g * R in one exact f32 add
+// (the result stays on the grid inside the binade), a range replays its adds one by one.  The result
+// equals the sequential chain bit for bit.
+//
+// Sum (signed terms): its chain stays within e1 = u sum_i |P_i| (1 + 1.01 n u) of the exact sum
+// (|e_i| <= |e_(i-1)|(1 + u) + u |P_i|), with the exact prefix sums P_i in units of 2^-24.  The score
+// fl(fl(q / n) - fl(m * m)), m = fl(s / n), is monotone in |m|, so [lo, hi] over the chain's possible
+// s holds the reference's score; both ends decide the same unless a threshold lies within about an
+// ulp of the score.  lo = hi = nan when x holds inf or nan.
+constexpr int kReplayItems = 4;
+constexpr int kReplayMaxThreads = 256;
+struct ReplayShared {
+    int4 item[kReplayMaxThreads][kReplayItems];  // {0, B, R even, R odd} or {1, i0, i1, 0}
+    int count[kReplayMaxThreads];
+    double w2[kReplayMaxThreads / 32];
+    long long w1[kReplayMaxThreads / 32];
+    double wabs[kReplayMaxThreads / 32];
+    float lo, hi;
+};
+
+__device__ __forceinline__ float replay_x(const void* xrow, int x_dtype, int64_t i) {
+    return h2f(x_f16_bits(xrow, x_dtype, i));
+}
+
+template <int kThreads>
+__device__ void replay_score(const void* xrow, int x_dtype, int64_t K, ReplayShared& sh) {
+    static_assert(kThreads % 32 == 0 && kThreads <= kReplayMaxThreads, "replay threads");
+    constexpr int kWarps = kThreads / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t c = (K + kThreads - 1) / kThreads;
+    const int64_t i0 = min(K, static_cast<int64_t>(tid) * c), i1 = min(K, i0 + c);
+    double l2 = 0.0;
+    long long l1 = 0;
+    int bad = 0;
+    for (int64_t i = i0; i < i1; ++i) {
+        const float xf = replay_x(xrow, x_dtype, i);
+        if (!isfinite(xf)) {
+            bad = 1;
+            continue;
+        }
+        l2 += static_cast<double>(__fmul_rn(xf, xf));
+        l1 += __float2ll_rn(__fmul_rn(xf, 16777216.0f));  // exact: an f16 times 2^24 is an integer < 2^40
+    }
+    double s2 = l2;
+    long long s1 = l1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double a2 = __shfl_up_sync(0xffffffffu, s2, o);
+        const long long a1 = __shfl_up_sync(0xffffffffu, s1, o);
+        if (lane >= o) {
+            s2 += a2;
+            s1 += a1;
+        }
+    }
+    if (lane == 31) {
+        sh.w2[warp] = s2;
+        sh.w1[warp] = s1;
+    }
+    if (__syncthreads_or(bad)) {
+        if (tid == 0) sh.lo = sh.hi = __int_as_float(0x7fc00000);
+        __syncthreads();
+        return;
+    }
+    double P2 = s2 - l2;
+    long long P1 = s1 - l1;
+    long long tot1 = 0;
+    for (int w = 0; w < kWarps; ++w) {
+        if (w < warp) {
+            P2 += sh.w2[w];
+            P1 += sh.w1[w];
+        }
+        tot1 += sh.w1[w];
+    }
+    double absP1 = 0.0;
+    int n_it = 0, kind = -1, curB = 0, par0 = 0, par1 = 1;
+    float R0 = 0.0f, R1 = 0.0f;
+    int64_t seq0 = 0, seq1 = 0;
+    bool tail = false;
+    for (int64_t i = i0; i < i1; ++i) {
+        const float xf = replay_x(xrow, x_dtype, i);
+        const float v = __fmul_rn(xf, xf);
+        const double Pp = P2;
+        P2 += static_cast<double>(v);
+        P1 += __float2ll_rn(__fmul_rn(xf, 16777216.0f));
+        absP1 += fabs(static_cast<double>(P1));
+        if (tail) continue;
+        bool certain = false;
+        int B = 0;
+        float sc = 0.0f;
+        if (Pp > 0.0) {
+            B = static_cast<int>((__double_as_longlong(Pp) >> 52) & 0x7FF) - 1023;
+            const double iu = static_cast<double>(i + 1) * 5.9604644775390625e-08;
+            const double d = iu / (1.0 - iu) + 1e-9;
+            const double base = __longlong_as_double(static_cast<long long>(B + 1023) << 52);
+            if (Pp * (1.0 - d) >= base && P2 + d * Pp < 2.0 * base) {
+                sc = __fmul_rn(v, __int_as_float((127 + 23 - B) << 23));  // v / g, exact
+                certain = true;
+            }
+        }
+        if (certain) {
+            if (!(kind == 0 && curB == B)) {
+                if (kind == 0) {
+                    sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+                } else if (kind == 1) {
+                    sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(seq1), 0);
+                }
+                if (n_it == kReplayItems - 1) {  // the rest of the chunk as one range
+                    tail = true;
+                    kind = 1;
+                    seq0 = i;
+                    continue;
+                }
+                kind = 0;
+                curB = B;
+                R0 = R1 = 0.0f;
+                par0 = 0;
+                par1 = 1;
+            }
+            const float fl = floorf(sc);
+            const bool tie = __fsub_rn(sc, fl) == 0.5f;
+            const float rr = rintf(sc);
+            const int fli = static_cast<int>(fl);
+            const float r0 = tie ? ((((par0 + fli) & 1) == 0) ? fl : __fadd_rn(fl, 1.0f)) : rr;
+            const float r1 = tie ? ((((par1 + fli) & 1) == 0) ? fl : __fadd_rn(fl, 1.0f)) : rr;
+            R0 = __fadd_rn(R0, r0);  // integers below 2^24: exact
+            R1 = __fadd_rn(R1, r1);
+            par0 = (par0 + static_cast<int>(r0)) & 1;
+            par1 = (par1 + static_cast<int>(r1)) & 1;
+        } else {
+            if (kind != 1) {
+                if (kind == 0) sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+                if (n_it == kReplayItems - 1) tail = true;
+                kind = 1;
+                seq0 = i;
+            }
+            seq1 = i + 1;
+        }
+    }
+    if (kind == 0) {
+        sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+    } else if (kind == 1) {
+        sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(tail ? i1 : seq1), 0);
+    }
+    sh.count[tid] = n_it;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) absP1 += __shfl_down_sync(0xffffffffu, absP1, o);
+    if (lane == 0) sh.wabs[warp] = absP1;
+    __syncthreads();
+    if (tid == 0) {
+        float q = 0.0f;
+        for (int t = 0; t < kThreads; ++t) {
+            const int n = sh.count[t];
+            for (int j = 0; j < n; ++j) {
+                const int4 it = sh.item[t][j];
+                if (it.x == 0) {
+                    const float R = __int_as_float((__float_as_uint(q) & 1u) ? it.w : it.z);
+                    q = __fadd_rn(q, __fmul_rn(R, __int_as_float((127 + it.y - 23) << 23)));
+                } else {
+                    for (int i = it.y; i < it.z; ++i) {
+                        const float xf = replay_x(xrow, x_dtype, i);
+                        q = __fadd_rn(q, __fmul_rn(xf, xf));
+                    }
+                }
+            }
+        }
+        double sabs = 0.0;
+        for (int w = 0; w < kWarps; ++w) sabs += sh.wabs[w];
+        const double u = 5.9604644775390625e-08, n = static_cast<double>(K);
+        const double S1 = static_cast<double>(tot1) * 5.9604644775390625e-08;
+        const double e1 = u * (sabs * 5.9604644775390625e-08) * (1.0 + 1.01 * n * u) * (1.0 + 1e-6) + 1e-300;
+        const float hd = static_cast<float>(K);
+        const float qd = __fdiv_rn(q, hd);
+        const float mlo = __fdiv_rn(__double2float_rd(S1 - e1), hd);
+        const float mhi = __fdiv_rn(__double2float_ru(S1 + e1), hd);
+        const float a = __fmul_rn(mlo, mlo), b = __fmul_rn(mhi, mhi);
+        const float mmax = fmaxf(a, b);
+        const float mmin = (mlo <= 0.0f && mhi >= 0.0f) ? 0.0f : fminf(a, b);
+        sh.lo = __fsub_rn(qd, mmax);
+        sh.hi = __fsub_rn(qd, mmin);
+    }
+    __syncthreads();
+}
+
 }  // namespace sc

@@ -576,9 +576,12 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     p.status = L.status;
     const int64_t chunks = L.KB * a.Mpp * 8;
     const int64_t gblocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(L.sms) * 16);
-    cudaError_t e = launch_pdl(k_gather_tokens, dim3(static_cast<unsigned>(gblocks)), dim3(256), 0, s,
-                               a.xk, a.xkp, a.perm, a.nrouted, a.route_all, a.M, a.Mp, a.Mpp, L.KB);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
+    if (!a.skip_gather) {
+        e = launch_pdl(k_gather_tokens, dim3(static_cast<unsigned>(gblocks)), dim3(256), 0, s, a.xk, a.xkp, a.perm,
+                       a.nrouted, a.route_all, a.M, a.Mp, a.Mpp, L.KB);
+        if (e != cudaSuccess) return e;
+    }
     static std::atomic<uint64_t> flags[3] = {{0}, {0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);

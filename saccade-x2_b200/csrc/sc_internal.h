@@ -189,6 +189,7 @@ struct GemmArgs {
     int y_dtype;
     const float* bias;
     int partial_out;
+    int skip_gather;        // xkp and perm already hold this x (a previous layer of the same group)
 };
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 int64_t gemm_tile_tokens();

@@ -83,6 +83,8 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
     __shared__ double red[3][kWarps];
     __shared__ int s_last;
     __shared__ int s_wsum[kWarps];
+    __shared__ int s_open;
+    __shared__ ReplayShared s_replay;
     const int t = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_launch_dependents();
@@ -113,6 +115,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
         red[2][warp] = sa;
     }
     __syncthreads();
+    const void* xrow = static_cast<const unsigned char*>(a.x) + row_off * 2;
     if (tid == 0) {
         double S1 = 0.0, S2 = 0.0, SA = 0.0;
         for (int w = 0; w < kWarps; ++w) {
@@ -120,11 +123,45 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
             S2 += red[1][w];
             SA += red[2][w];
         }
-        const void* xrow = static_cast<const unsigned char*>(a.x) + row_off * 2;
+        int open = 0;
         for (int l = 0; l < a.nl; ++l) {
-            bool routed = route_token(S1, S2, SA, a.x_stride, a.rc, a.t4[l], a.t8[l], xrow, a.x_dtype, nullptr);
-            if (a.route_all) routed = true;
-            a.mask[l][t] = routed ? 1 : 0;
+            double var;
+            const int d = a.route_all ? 1 : route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var);
+            if (d >= 0) {
+                a.mask[l][t] = static_cast<uint8_t>(d);
+            } else {
+                open = 1;
+            }
+        }
+        s_open = open;
+    }
+    __syncthreads();
+    if (s_open) {
+        // some layer's threshold is inside the f32 error band: the CTA replays the reference's chains
+        // once for the token, then every open decision is taken on that score
+        replay_score<kThreads>(xrow, a.x_dtype, a.x_stride, s_replay);
+        if (tid == 0) {
+            double S1 = 0.0, S2 = 0.0, SA = 0.0;
+            for (int w = 0; w < kWarps; ++w) {
+                S1 += red[0][w];
+                S2 += red[1][w];
+                SA += red[2][w];
+            }
+            bool have_exact = false;
+            float exact = 0.0f;
+            for (int l = 0; l < a.nl; ++l) {
+                double var;
+                if (route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var) >= 0) continue;
+                const bool rl = route_rule_f32(s_replay.lo, a.t4[l], a.t8[l]);
+                const bool rh = route_rule_f32(s_replay.hi, a.t4[l], a.t8[l]);
+                bool routed = rl;
+                if (rl != rh || !(s_replay.lo == s_replay.lo)) {
+                    if (!have_exact) exact = exact_variance(xrow, a.x_dtype, a.x_stride);
+                    have_exact = true;
+                    routed = route_rule_f32(exact, a.t4[l], a.t8[l]);
+                }
+                a.mask[l][t] = routed ? 1 : 0;
+            }
         }
     }
     // completion count; the last CTA compacts every layer's mask

@@ -10,9 +10,10 @@
 // (|fl(sum) - sum| <= gamma_{k-1} * sum|terms|, gamma_n = n*u/(1-n*u), u = 2^-24)
 // bounds how far the reference's f32 score can lie from the f64 one.  When both
 // thresholds are farther than that bound the decision is the reference's; otherwise
-// one thread replays the reference's exact sequential f32 chain for that token.  The
-// mask therefore equals the reference's mask for every token, at the cost of a serial
-// pass only for tokens sitting on a threshold.
+// the CTA replays the reference's sequential f32 chains for that token in parallel
+// (replay_score, sc_device.cuh), and only a threshold within about an ulp of the score
+// sends one thread through the whole chain.  The mask therefore equals the reference's
+// mask for every token.
 //
 // The last CTA to finish (completion counter in the workspace) compacts the mask into
 // the ascending routed-token list and resets the counter for the next call.
@@ -51,6 +52,8 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
     __shared__ double red[3][kWarps];
     __shared__ int s_last;
     __shared__ int s_wsum[kWarps];
+    __shared__ int s_open;
+    __shared__ ReplayShared s_replay;
     const int64_t t = blockIdx.x;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -118,6 +121,7 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
             red[2][warp] = sa;
         }
         __syncthreads();
+        const void* xrow = static_cast<const unsigned char*>(a.x) + row_off * 2;
         if (tid == 0) {
             double S1 = 0.0, S2 = 0.0, SA = 0.0;
             for (int w = 0; w < kWarps; ++w) {
@@ -125,13 +129,29 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
                 S2 += red[1][w];
                 SA += red[2][w];
             }
-            float score = 0.0f;
-            bool routed = route_token(S1, S2, SA, a.Kfull, a.t4, a.t8,
-                                      static_cast<const unsigned char*>(a.x) + row_off * (a.x_dtype == SC_F32 ? 4 : 2),
-                                      a.x_dtype, &score);
-            if (a.route_all) routed = true;
-            a.mask[t] = routed ? 1 : 0;
-            if (a.scores) a.scores[t] = score;
+            double var = 0.0;
+            const int d = a.route_all ? 1 : route_band(S1, S2, SA, route_consts(a.Kfull), a.t4, a.t8, 0.0, 0.0, &var);
+            s_open = d < 0 ? 1 : 0;
+            if (d >= 0) {
+                a.mask[t] = static_cast<uint8_t>(d);
+                if (a.scores) a.scores[t] = static_cast<float>(var);
+            }
+        }
+        __syncthreads();
+        if (s_open) {
+            // the f64 score is inside the f32 error band: the CTA replays the reference's chains
+            replay_score<kThreads>(xrow, a.x_dtype, a.Kfull, s_replay);
+            if (tid == 0) {
+                const bool rl = route_rule_f32(s_replay.lo, a.t4, a.t8), rh = route_rule_f32(s_replay.hi, a.t4, a.t8);
+                float score = s_replay.lo;
+                bool routed = rl;
+                if (rl != rh || !(s_replay.lo == s_replay.lo)) {  // a threshold within an ulp, or inf / nan
+                    score = exact_variance(xrow, a.x_dtype, a.Kfull);
+                    routed = route_rule_f32(score, a.t4, a.t8);
+                }
+                a.mask[t] = routed ? 1 : 0;
+                if (a.scores) a.scores[t] = score;
+            }
         }
     }
 
