@@ -80,6 +80,10 @@ def parse(argv=None):
                     help="comma-separated dW densities for --sweep (default: --fill)")
     ap.add_argument("--sweep-tokens", default=None, metavar="LIST",
                     help="comma-separated token counts for --sweep (default: 1,4,16,64,256,1024,4096)")
+    ap.add_argument("--sweep-shapes", default=None, metavar="LIST",
+                    help="comma-separated shape labels for --sweep (q/o, k/v, gate/up, down; default: all)")
+    ap.add_argument("--sweep-routed", default=None, metavar="LIST",
+                    help="comma-separated routed fractions for --sweep (default: 0,0.1,0.25,1)")
     a = ap.parse_args(argv)
     if a.steps is None:
         a.steps = 100 if a.workload == "decode" else 20
@@ -920,8 +924,10 @@ def run_sweep(args):
         pass
     fills = [float(v) for v in args.sweep_fills.split(",")] if args.sweep_fills else [args.fill]
     tokens = [int(v) for v in args.sweep_tokens.split(",")] if args.sweep_tokens else SWEEP_TOKENS
+    shapes = [sh for sh in SWEEP_SHAPES if not args.sweep_shapes or sh[0] in args.sweep_shapes.split(",")]
+    routed = [float(v) for v in args.sweep_routed.split(",")] if args.sweep_routed else SWEEP_ROUTED
     rows = []
-    for fill, (label, n, k) in [(f, sh) for f in fills for sh in SWEEP_SHAPES]:
+    for fill, (label, n, k) in [(f, sh) for f in fills for sh in shapes]:
         packed = torch.randint(-2 ** 31, 2 ** 31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=gen)
         scale = ((0.02 * (3.0 + torch.rand(n, device=dev, generator=gen))) / 7.0).to(torch.float16)
         nnz = int(round(n * k * fill))
@@ -940,7 +946,7 @@ def run_sweep(args):
         del packed, scale, flat, rr, cc, rp, vals, sp
         for m in tokens:
             y = torch.empty((m, n), dtype=torch.float16, device=dev)
-            for frac in SWEEP_ROUTED:
+            for frac in routed:
                 r = int(round(frac * m))
                 x = torch.randn((m, k), device=dev, generator=gen)
                 if r:
@@ -985,6 +991,8 @@ def run_sweep(args):
         f.write("Command: `python bench.py --sweep " + args.sweep + (f" --mode {args.mode}" if args.mode != "fast" else "")
                 + (f" --sweep-fills {args.sweep_fills}" if args.sweep_fills else "")
                 + (f" --sweep-tokens {args.sweep_tokens}" if args.sweep_tokens else "")
+                + (f" --sweep-shapes {args.sweep_shapes}" if args.sweep_shapes else "")
+                + (f" --sweep-routed {args.sweep_routed}" if args.sweep_routed else "")
                 + (f" --fill {args.fill}" if not args.sweep_fills and args.fill != 0.01 else "") + "`\n\n")
         f.write(f"Peaks: HBM {hbm} GB/s, bf16 dense {tc} TFLOP/s (MEASURED_PEAKS.json). `bound` is the larger of "
                 "bytes/HBM and flops/tensor; `frac` = that bound time / measured time. Routed = fraction of "

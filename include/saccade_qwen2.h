@@ -47,7 +47,12 @@ SC_API sc_status sc_qwen2_rope_append(float* q, const float* k, const float* v, 
 SC_API size_t sc_qwen2_attention_scratch(int64_t tokens, int num_heads, int num_kv_heads, int head_dim, int max_pos);
 
 /* Causal GQA attention: token t attends the keys 0..pos[t] of its cache slot; out_f16 [tokens,
- * num_heads * head_dim].  max_query_pos bounds every pos[t] (it sizes the key blocks launched). */
+ * num_heads * head_dim].  max_query_pos bounds every pos[t] (it sizes the key blocks launched).
+ * Limits (SC_EINVAL otherwise): head_dim 32, 64 or 128; at most 8 query heads per KV head and 128
+ * query heads; max_query_pos < 8192.  Keys go in blocks of 256: per block the scores (per-lane
+ * partial dot products over head_dim, then a 32-lane xor butterfly), its max, exp evaluated in f64
+ * and rounded to f32, the lane-strided sum, p . v over the keys in order; blocks are combined in
+ * order, so the result is a fixed function of the inputs. */
 SC_API sc_status sc_qwen2_attention(const float* q, const float* k_cache, const float* v_cache, const int32_t* slot,
                                     const int32_t* pos, int64_t tokens, int num_heads, int num_kv_heads, int head_dim,
                                     int max_pos, int max_query_pos, float* scratch, size_t scratch_bytes,

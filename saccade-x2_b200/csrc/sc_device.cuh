@@ -63,10 +63,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (and records DEV_TIMEOUT) if the
 // phase does not complete within `limit_ns`; callers then skip their remaining work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                                           uint64_t limit_ns = kWaitNs) {
+    if (mbar_test_wait(bar, parity)) return true;  // a completed phase: no suspend
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
@@ -578,6 +591,26 @@ __device__ __forceinline__ bool route_token(double S1, double S2, double SA, int
     return route_token(S1, S2, SA, Kfull, route_consts(Kfull), t4, t8, xrow, x_dtype, score_out, E1x, E2x);
 }
 
+// ---------------------------------------------------------------- dW/s folded into dequantised weights
+
+// Header of one fold list (per 128-row tile and 64-column block): u16 entry offsets
+// [8 tiles of 16 rows][33 lanes + end], then u32 entries (see build_fold_lists).
+constexpr int kFoldHdr = 528;
+
+// Add f16 value `v` to the half `hi` of 32-bit register h[slot / 4][slot % 4]: one predicated add
+// per register (static indices keep the 16 registers out of local memory, and no lane branches, so
+// lanes with different slots do not serialise on a divergent switch).
+__device__ __forceinline__ void fold_add(uint32_t (&h)[4][4], int slot, int hi, uint16_t v) {
+    const uint32_t add = hi ? (static_cast<uint32_t>(v) << 16) : static_cast<uint32_t>(v);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        const __half2 t = __hadd2(*reinterpret_cast<const __half2*>(&h[q / 4][q % 4]),
+                                  *reinterpret_cast<const __half2*>(&add));
+        const uint32_t r = *reinterpret_cast<const uint32_t*>(&t);
+        h[q / 4][q % 4] = slot == q ? r : h[q / 4][q % 4];
+    }
+}
+
 // ---------------------------------------------------------------- parallel exact replay
 //
 // The reference's score of a token whose f64 score lies inside the error band, computed by a whole
@@ -605,19 +638,31 @@ constexpr int kReplayItems = 4;
 constexpr int kReplayMaxThreads = 256;
 struct ReplayShared {
     int4 item[kReplayMaxThreads][kReplayItems];  // {0, B, R even, R odd} or {1, i0, i1, 0}
+    int4 flat[kReplayMaxThreads * kReplayItems];  // the items of all threads in order
     int count[kReplayMaxThreads];
     double w2[kReplayMaxThreads / 32];
     long long w1[kReplayMaxThreads / 32];
     double wabs[kReplayMaxThreads / 32];
+    int wcnt[kReplayMaxThreads / 32];
     float lo, hi;
 };
 
-__device__ __forceinline__ float replay_x(const void* xrow, int x_dtype, int64_t i) {
-    return h2f(x_f16_bits(xrow, x_dtype, i));
+// The reference's exact sequential f32 score of one row of f16 bits (heuristics.rs:3-14).
+static __device__ __noinline__ float exact_variance_row(const uint16_t* row, int64_t K) {
+    float sum = 0.0f, sq = 0.0f;
+    for (int64_t i = 0; i < K; ++i) {
+        const float v = h2f(row[i]);
+        sum = __fadd_rn(sum, v);
+        sq = __fadd_rn(sq, __fmul_rn(v, v));
+    }
+    const float hd = static_cast<float>(K);
+    const float mean = __fdiv_rn(sum, hd);
+    return __fsub_rn(__fdiv_rn(sq, hd), __fmul_rn(mean, mean));
 }
 
+// `row`: the token's K values as f16 bits, in shared memory (read many times).
 template <int kThreads>
-__device__ void replay_score(const void* xrow, int x_dtype, int64_t K, ReplayShared& sh) {
+__device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
     static_assert(kThreads % 32 == 0 && kThreads <= kReplayMaxThreads, "replay threads");
     constexpr int kWarps = kThreads / 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -627,7 +672,7 @@ __device__ void replay_score(const void* xrow, int x_dtype, int64_t K, ReplaySha
     long long l1 = 0;
     int bad = 0;
     for (int64_t i = i0; i < i1; ++i) {
-        const float xf = replay_x(xrow, x_dtype, i);
+        const float xf = h2f(row[i]);
         if (!isfinite(xf)) {
             bad = 1;
             continue;
@@ -671,7 +716,7 @@ __device__ void replay_score(const void* xrow, int x_dtype, int64_t K, ReplaySha
     int64_t seq0 = 0, seq1 = 0;
     bool tail = false;
     for (int64_t i = i0; i < i1; ++i) {
-        const float xf = replay_x(xrow, x_dtype, i);
+        const float xf = h2f(row[i]);
         const float v = __fmul_rn(xf, xf);
         const double Pp = P2;
         P2 += static_cast<double>(v);
@@ -735,25 +780,38 @@ __device__ void replay_score(const void* xrow, int x_dtype, int64_t K, ReplaySha
     } else if (kind == 1) {
         sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(tail ? i1 : seq1), 0);
     }
-    sh.count[tid] = n_it;
+    // the items in chunk order: an exclusive scan of the counts places each thread's items
+    int cs = n_it;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, cs, o);
+        if (lane >= o) cs += a;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) absP1 += __shfl_down_sync(0xffffffffu, absP1, o);
+    if (lane == 31) sh.wcnt[warp] = cs;
     if (lane == 0) sh.wabs[warp] = absP1;
+    __syncthreads();
+    int at = cs - n_it, total = 0;
+    for (int w = 0; w < kWarps; ++w) {
+        if (w < warp) at += sh.wcnt[w];
+        total += sh.wcnt[w];
+    }
+    for (int j = 0; j < n_it; ++j) sh.flat[at + j] = sh.item[tid][j];
     __syncthreads();
     if (tid == 0) {
         float q = 0.0f;
-        for (int t = 0; t < kThreads; ++t) {
-            const int n = sh.count[t];
-            for (int j = 0; j < n; ++j) {
-                const int4 it = sh.item[t][j];
-                if (it.x == 0) {
-                    const float R = __int_as_float((__float_as_uint(q) & 1u) ? it.w : it.z);
-                    q = __fadd_rn(q, __fmul_rn(R, __int_as_float((127 + it.y - 23) << 23)));
-                } else {
-                    for (int i = it.y; i < it.z; ++i) {
-                        const float xf = replay_x(xrow, x_dtype, i);
-                        q = __fadd_rn(q, __fmul_rn(xf, xf));
-                    }
+        int4 nx = sh.flat[0];
+        for (int j = 0; j < total; ++j) {
+            const int4 it = nx;
+            if (j + 1 < total) nx = sh.flat[j + 1];  // the next item loaded ahead
+            if (it.x == 0) {
+                const float R = __int_as_float((__float_as_uint(q) & 1u) ? it.w : it.z);
+                q = __fadd_rn(q, __fmul_rn(R, __int_as_float((127 + it.y - 23) << 23)));
+            } else {
+                for (int i = it.y; i < it.z; ++i) {
+                    const float xf = h2f(row[i]);
+                    q = __fadd_rn(q, __fmul_rn(xf, xf));
                 }
             }
         }

@@ -48,7 +48,6 @@ namespace sc {
 // variant, 8 KB (~23 %) in a one-row-tile variant for layers whose lists need it.
 constexpr int kFoldCap = 4096;
 constexpr int kFoldCapWide = 8192;
-constexpr int kFoldHdr = 528;   // its header: u16 entry offsets [8 tiles of 16 rows][33 lanes + end]
 
 struct GemmParams {
     const uint32_t* wq;
@@ -111,26 +110,6 @@ struct GemmCfg {
     static_assert(kTotal <= 227 * 1024, "shared memory");
 };
 
-// Add f16 value `v` to the half `hi` of 32-bit register h[slot / 4][slot % 4] (static indices:
-// the switch keeps the 16 registers out of local memory).
-__device__ __forceinline__ void fold_add(uint32_t (&h)[4][4], int slot, int hi, uint16_t v) {
-    const __half2 add = hi ? __halves2half2(__ushort_as_half(0), __ushort_as_half(v))
-                           : __halves2half2(__ushort_as_half(v), __ushort_as_half(0));
-#define SC_FOLD_CASE(q)                                                                  \
-    case q: {                                                                            \
-        __half2 t = __hadd2(*reinterpret_cast<const __half2*>(&h[(q) / 4][(q) % 4]), add); \
-        h[(q) / 4][(q) % 4] = *reinterpret_cast<const uint32_t*>(&t);                     \
-        break;                                                                           \
-    }
-    switch (slot) {
-        SC_FOLD_CASE(0) SC_FOLD_CASE(1) SC_FOLD_CASE(2) SC_FOLD_CASE(3)
-        SC_FOLD_CASE(4) SC_FOLD_CASE(5) SC_FOLD_CASE(6) SC_FOLD_CASE(7)
-        SC_FOLD_CASE(8) SC_FOLD_CASE(9) SC_FOLD_CASE(10) SC_FOLD_CASE(11)
-        SC_FOLD_CASE(12) SC_FOLD_CASE(13) SC_FOLD_CASE(14) SC_FOLD_CASE(15)
-        default: break;
-    }
-#undef SC_FOLD_CASE
-}
 
 // Token tile tt of a row tile, from the routed count R (read after the dependency wait): tiles
 // [0, ceil(R/128)) hold the routed positions [0, R), the next ones the others from

@@ -107,6 +107,9 @@ sc_status cuda_fail(cudaError_t e, const char* what);
 // Launch with programmatic stream serialization (PDL): the kernel may start while the
 // previous kernel on the stream finishes; it must call griddepcontrol.wait before touching
 // anything that kernel writes or reads.
+// Dynamic shared memory of the router kernels (the token row, f16): K <= 65536.
+constexpr int kRouterMaxRowBytes = 128 * 1024;
+
 // Kernels this library has launched (host-side count of launch calls, sc_launch_count).
 extern std::atomic<uint64_t> g_launches;
 
@@ -242,11 +245,14 @@ int64_t fused_prefetch_bytes();  // weight bytes the fused kernel prefetches wit
 #define SC_MID_MIN_TOKENS 9   // calls of at least this many tokens (and at most 64) run it
 #endif
 #ifndef SC_MID_MAX_TOKENS
-#define SC_MID_MAX_TOKENS 16  // ... up to this many (the kernel takes up to 64; with routed tokens beyond 16
-                              // the 128-token GEMM is faster, its dW folded into the weights)
+#define SC_MID_MAX_TOKENS 64  // ... up to this many
+#endif
+#ifndef SC_MID_FOLD_MIN_TOKENS
+#define SC_MID_FOLD_MIN_TOKENS 17  // from this many tokens routed tokens' dW is folded into a second A
 #endif
 constexpr int64_t kMidMinTokens = SC_MID_MIN_TOKENS;
 constexpr int64_t kMidMaxTokens = SC_MID_MAX_TOKENS;
+constexpr int64_t kMidFoldMinTokens = SC_MID_FOLD_MIN_TOKENS;
 struct MidArgs {
     int n;                                  // layers (same K and input columns)
     const Layer* layer[SC_GROUP_MAX];

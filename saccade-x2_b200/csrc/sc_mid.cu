@@ -85,6 +85,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
     __shared__ int s_wsum[kWarps];
     __shared__ int s_open;
     __shared__ ReplayShared s_replay;
+    extern __shared__ __align__(16) uint16_t s_row[];  // the token as f16 bits [x_stride]
     const int t = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_launch_dependents();
@@ -95,6 +96,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
         uint16_t h[8];
         load_f16x8(a.x, a.x_dtype, a.vec_ok, row_off + ch * 8, h);
         if (a.xcopy) *reinterpret_cast<uint4*>(a.xcopy + row_off + ch * 8) = *reinterpret_cast<const uint4*>(h);
+        *reinterpret_cast<uint4*>(&s_row[ch * 8]) = *reinterpret_cast<const uint4*>(h);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const double v = static_cast<double>(h2f(h[j]));
@@ -115,7 +117,6 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
         red[2][warp] = sa;
     }
     __syncthreads();
-    const void* xrow = static_cast<const unsigned char*>(a.x) + row_off * 2;
     if (tid == 0) {
         double S1 = 0.0, S2 = 0.0, SA = 0.0;
         for (int w = 0; w < kWarps; ++w) {
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
     if (s_open) {
         // some layer's threshold is inside the f32 error band: the CTA replays the reference's chains
         // once for the token, then every open decision is taken on that score
-        replay_score<kThreads>(xrow, a.x_dtype, a.x_stride, s_replay);
+        replay_score<kThreads>(s_row, a.x_stride, s_replay);
         if (tid == 0) {
             double S1 = 0.0, S2 = 0.0, SA = 0.0;
             for (int w = 0; w < kWarps; ++w) {
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
                 const bool rh = route_rule_f32(s_replay.hi, a.t4[l], a.t8[l]);
                 bool routed = rl;
                 if (rl != rh || !(s_replay.lo == s_replay.lo)) {
-                    if (!have_exact) exact = exact_variance(xrow, a.x_dtype, a.x_stride);
+                    if (!have_exact) exact = exact_variance_row(s_row, a.x_stride);
                     have_exact = true;
                     routed = route_rule_f32(exact, a.t4[l], a.t8[l]);
                 }
@@ -218,6 +219,8 @@ struct MidLayer {
     const int32_t* nrouted;
     const uint8_t* dseg;   // dW segments per (row tile, block) (null: no dW)
     const uint32_t* dsegoff;
+    const uint8_t* fold;   // dW/s fold lists per (row tile, block) (the folding variant)
+    const uint32_t* foldoff;
     int cta0;              // first CTA of this layer
 };
 
@@ -228,7 +231,8 @@ struct alignas(64) MidParams {
     int T, Tp;             // tokens, tokens rounded up to 16 (MMA N)
     int wstages, xstages;  // ring depths
     int route_all;
-    int dslot;             // shared-memory slot of one dW segment (0: dW read in place from global memory)
+    int dslot;             // shared-memory slot of one dW segment, or of one fold list in the folding
+                           // variant (0: dW read in place from global memory)
     int64_t x_col0;        // first column of the layers' slice within a token
     MidLayer L[SC_GROUP_MAX];
 };
@@ -256,17 +260,19 @@ struct MidCfg {
     static constexpr int kMaxSlot = 4096;        // dW segment slot at most (denser dW: read in place)
     // dynamic shared memory: x ring (1024-aligned stages) first, weight ring, dW segment slots (one
     // per block of the x ring), dW sums, barriers
-    __host__ __device__ static int total_bytes(int ws, int xs, int T, int Tp, int dslot) {
-        return 1024 + xs * xstage_bytes(Tp) + ws * kWStage + xs * SKB * dslot + corr_bytes(T) + kNumBars * 8 + 16;
+    __host__ __device__ static int total_bytes(int ws, int xs, int T, int Tp, int dslot, bool fold) {
+        return 1024 + xs * xstage_bytes(Tp) + ws * kWStage + xs * SKB * dslot + (fold ? 0 : corr_bytes(T)) +
+               kNumBars * 8 + 16;
     }
 };
 
 // Ring depths for T tokens: the weights 8 stages deep (64 KB in flight per CTA), x 4 stages;
 // 6 weight stages when that keeps two CTAs on an SM.
-static void mid_stages(int T, int Tp, int dslot, int* ws, int* xs) {
+static void mid_stages(int T, int Tp, int dslot, bool fold, int* ws, int* xs) {
     *ws = 8;
     *xs = 4;
-    if (MidCfg::total_bytes(8, 4, T, Tp, dslot) > 100 * 1024 && MidCfg::total_bytes(6, 4, T, Tp, dslot) <= 100 * 1024)
+    if (!fold && MidCfg::total_bytes(8, 4, T, Tp, dslot, false) > 100 * 1024 &&
+        MidCfg::total_bytes(6, 4, T, Tp, dslot, false) <= 100 * 1024)
         *ws = 6;
 }
 
@@ -306,14 +312,20 @@ __device__ __forceinline__ float staged_x(const unsigned char* blk, int t, int c
     return h2f(*reinterpret_cast<const uint16_t*>(blk + t * 128 + ((((c >> 3) ^ t) & 7) << 4) + (c & 7) * 2));
 }
 
-__global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_constant__ MidParams P) {
+template <bool kFold>
+__global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(const __grid_constant__ MidParams P) {
     using C = MidCfg;
     constexpr int SKB = C::SKB, AB = C::AB, CPB = C::kColsPerBlock;
+    // folding: D (plain weights) at TMEM column 0, D' (folded) at 64, per block A then A' from 128
+    constexpr uint32_t kTmemCols = kFold ? 512u : C::kTmemCols;
+    constexpr uint32_t kAcol = kFold ? 128u : C::kAcol;
+    constexpr int kBlkCols = kFold ? 2 * CPB : CPB;
     pdl_launch_dependents();
     extern __shared__ unsigned char smem_raw[];
     __shared__ int s_abort;
     __shared__ int s_last;
     __shared__ int s_nr;
+    __shared__ int s_fold;  // folding variant: this launch's tokens include routed ones
     __shared__ int s_ridx[C::kMaxTok];
     __shared__ int s_pos[C::kMaxTok];
     constexpr int kMaxDoff = 512;
@@ -341,7 +353,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
     unsigned char* dring = wring + WS * C::kWStage;  // [XS][SKB] dW segment slots
     const int dslot = P.dslot;
     float* corr_s = reinterpret_cast<float*>(dring + XS * SKB * dslot);
-    uint64_t* wfull = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(corr_s) + C::corr_bytes(T));
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(corr_s) + (kFold ? 0 : C::corr_bytes(T)));
     uint64_t* wempty = wfull + WS;
     uint64_t* xfull = wempty + WS;
     uint64_t* xempty = xfull + XS;
@@ -358,7 +370,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         }
         for (int i = 0; i < XS; ++i) {
             mbar_init(&xfull[i], 1);
-            mbar_init(&xempty[i], 1 + 4);  // the MMA commit and the four auxiliary warps
+            mbar_init(&xempty[i], 1 + 4);  // the MMA commit and the four auxiliary (folding: dequantising) warps
         }
         for (int i = 0; i < AB; ++i) {
             mbar_init(&a_full[i], C::kDqWarps);
@@ -368,9 +380,10 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         fence_mbar_init();
         s_abort = 0;
         s_last = 0;
+        s_fold = 0;
     }
     if (warp == C::kMmaWarp) {
-        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -398,14 +411,18 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
             }
         }
     } else if (warp == C::kXProducerWarp) {
+        pdl_wait();  // the tokens (and their routing) are the previous kernels' output
+        // with a routed token, each stage also brings the blocks' dW segments (fold lists)
+        const uint8_t* lists = kFold ? L.fold : L.dseg;
+        const uint32_t* listoff = kFold ? L.foldoff : L.dsegoff;
+        const bool segs = dslot > 0 && lists != nullptr && (P.route_all || *L.nrouted > 0);
+        // the split's list offsets, loaded by the whole warp before the first stage needs them
+        const bool pre = segs && nkb < kMaxDoff;
+        if (pre)
+            for (int j = lane; j <= nkb; j += 32) s_doff[j] = listoff[rt * L.KB + kb_begin + j];
+        __syncwarp();
         if (lane == 0) {
-            pdl_wait();  // the tokens (and their routing) are the previous kernels' output
-            // with a routed token, each stage also brings the blocks' dW segments
-            const bool segs = dslot > 0 && L.dseg != nullptr && (P.route_all || *L.nrouted > 0);
-            // the split's segment offsets, loaded together before the first stage needs them
-            const bool pre = segs && nkb < kMaxDoff;
-            if (pre)
-                for (int j = 0; j <= nkb; ++j) s_doff[j] = L.dsegoff[rt * L.KB + kb_begin + j];
+            if (kFold) s_fold = segs ? 1 : 0;  // published by the first stage's arrive
             for (int it = 0; it < nst; ++it) {
                 const int xs = it % XS;
                 if (it >= XS && (s_abort || !mbar_wait(&xempty[xs], ((it / XS) - 1) & 1, L.status))) {
@@ -415,7 +432,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
                 const int64_t kb0 = kb_begin + static_cast<int64_t>(it) * SKB;
                 const int n = static_cast<int>(imin64(SKB, kb_end - kb0));
                 auto doff = [&](int64_t kb) {
-                    return pre ? s_doff[kb - kb_begin] : L.dsegoff[rt * L.KB + kb];
+                    return pre ? s_doff[kb - kb_begin] : listoff[rt * L.KB + kb];
                 };
                 uint32_t dbytes = 0;
                 if (segs) dbytes = doff(kb0 + n) - doff(kb0);
@@ -426,7 +443,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
                 if (segs) {
                     for (int k = 0; k < n; ++k) {
                         const uint32_t o0 = doff(kb0 + k), o1 = doff(kb0 + k + 1);
-                        bulk_g2s(dring + (xs * SKB + k) * dslot, L.dseg + o0, o1 - o0, &xfull[xs]);
+                        bulk_g2s(dring + (xs * SKB + k) * dslot, lists + o0, o1 - o0, &xfull[xs]);
                     }
                 }
                 ++xissued;
@@ -435,22 +452,30 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
     } else if (warp == C::kMmaWarp) {
         const uint32_t idesc = idesc_f16_f32(128, Tp);
         bool ok = true;
+        bool fo = false;  // folding: the routed tokens' products on A' as well
         for (int u = 0; u < nst && ok; ++u) {
             const int xs = u % XS, b = u % AB;
             ok = __all_sync(0xffffffffu, mbar_wait(&xfull[xs], (u / XS) & 1, L.status));
             if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&a_full[b], (u / AB) & 1, L.status));
             if (!ok) break;
             tc_fence_after();
+            if (kFold && u == 0) fo = s_fold != 0;
             const int n = nkb - u * SKB < SKB ? nkb - u * SKB : SKB;
-            const uint32_t a0 = tmem + C::kAcol + b * SKB * CPB;
+            const uint32_t a0 = tmem + kAcol + b * SKB * kBlkCols;
             const unsigned char* xb = xring + xs * xsb;
             if (elect_one()) {
                 for (int k = 0; k < n; ++k) {
                     const uint64_t bd = desc_kmajor_sw128(xb + k * xbb);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)  // K step i: 16 columns = 32 B further along the rows
-                        tc_mma_ts(tmem, a0 + k * CPB + i * 8, bd + static_cast<uint64_t>(2 * i), idesc,
+                        tc_mma_ts(tmem, a0 + k * kBlkCols + i * 8, bd + static_cast<uint64_t>(2 * i), idesc,
                                   (u | k | i) ? 1u : 0u);
+                    if (kFold && fo) {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            tc_mma_ts(tmem + 64, a0 + k * kBlkCols + CPB + i * 8, bd + static_cast<uint64_t>(2 * i),
+                                      idesc, (u | k | i) ? 1u : 0u);
+                    }
                 }
                 tc_commit(&a_empty[b]);
                 tc_commit(&xempty[xs]);
@@ -462,11 +487,19 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         __syncwarp();
     } else if (warp < C::kDqWarps) {
         const uint32_t lane_addr = static_cast<uint32_t>(32 * warp) << 16;
+        bool fo = false;
         for (int u = 0; u < nst; ++u) {
-            const int ws = u % WS, b = u % AB;
+            const int ws = u % WS, b = u % AB, xs = u % XS;
             if (!mbar_wait(&wfull[ws], (u / WS) & 1, L.status)) {
                 s_abort = 1;
                 break;
+            }
+            if (kFold && (u == 0 || fo)) {  // the stage's fold lists (and whether there are any) come with its tokens
+                if (!mbar_wait(&xfull[xs], (u / XS) & 1, L.status)) {
+                    s_abort = 1;
+                    break;
+                }
+                if (u == 0) fo = s_fold != 0;
             }
             const int n = nkb - u * SKB < SKB ? nkb - u * SKB : SKB;
             uint4 wv[SKB][2];  // [block][tile 2w, 2w + 1]
@@ -490,13 +523,28 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
                 for (int q = 0; q < 2; ++q) {
                     if (k < n) {
                         const uint32_t words[4] = {wv[k][q].x, wv[k][q].y, wv[k][q].z, wv[k][q].w};
-                        const uint32_t col = tmem + lane_addr + (static_cast<uint32_t>(16 * q) << 16) + C::kAcol +
-                                             (b * SKB + k) * CPB;
+                        const uint32_t col = tmem + lane_addr + (static_cast<uint32_t>(16 * q) << 16) + kAcol +
+                                             (b * SKB + k) * kBlkCols;
+                        uint32_t h[4][4];
 #pragma unroll
                         for (int st = 0; st < 4; ++st) {
-                            uint32_t h[4];
-                            dequant_word(words[st], h);
-                            tc_st_16x256b(col + st * 8, h[0], h[2], h[1], h[3]);
+                            dequant_word(words[st], h[st]);
+                            tc_st_16x256b(col + st * 8, h[st][0], h[st][2], h[st][1], h[st][3]);
+                        }
+                        if (kFold && fo) {
+                            // A' = (q - 8) + dW/s: this lane's entries of 16-row tile 2 warp + q
+                            const unsigned char* lst = dring + (xs * SKB + k) * dslot;
+                            const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + (2 * warp + q) * 33 + lane;
+                            const uint32_t* ent = reinterpret_cast<const uint32_t*>(lst + kFoldHdr);
+                            const int e1 = offs[1];
+                            for (int e = offs[0]; e < e1; ++e) {
+                                const uint32_t w = ent[e];
+                                fold_add(h, static_cast<int>((w >> 5) & 15u), static_cast<int>((w >> 9) & 1u),
+                                         static_cast<uint16_t>(w >> 16));
+                            }
+#pragma unroll
+                            for (int st = 0; st < 4; ++st)
+                                tc_st_16x256b(col + CPB + st * 8, h[st][0], h[st][2], h[st][1], h[st][3]);
                         }
                     }
                 }
@@ -504,7 +552,10 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
             tc_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[b]);
+            if (lane == 0) {
+                mbar_arrive(&a_full[b]);
+                if (kFold) mbar_arrive(&xempty[xs]);  // its fold lists are read (or none were loaded)
+            }
         }
     } else {
         // ---- auxiliary warps: thread `at` owns row `at` of the tile; dW of the routed tokens
@@ -521,7 +572,8 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
             s_ridx[at] = tk;
             s_pos[tk] = at;
         }
-        for (int i = 0; i < nr; ++i) corr[i] = 0.0f;
+        if (!kFold)  // folding: no dW sums (their shared memory is not allocated)
+            for (int i = 0; i < nr; ++i) corr[i] = 0.0f;
         aux_bar();
         // the first kRegTok routed tokens' sums stay in registers (the x values of an entry are all
         // loaded before the FMAs); any further ones are added in shared memory
@@ -541,10 +593,10 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
             for (int j = 0; j < kRegTok; ++j) cr[j] = __fmaf_rn(xv[j], v, cr[j]);
             for (int i = kRegTok; i < nr; ++i) corr[i] = __fmaf_rn(staged_x(blk, s_ridx[i], c), v, corr[i]);
         };
-        const bool segs = dslot > 0 && L.dseg != nullptr && nr > 0;
+        const bool segs = !kFold && dslot > 0 && L.dseg != nullptr && nr > 0;
         // without segments: this row's CSR entries in the split, one entry loaded ahead of its use
         int64_t e = 0, e_end = 0;
-        if (!segs && nr > 0 && row < L.N && L.nnz > 0) {
+        if (!kFold && !segs && nr > 0 && row < L.N && L.nnz > 0) {
             e = L.rowptr[row];
             e_end = L.rowptr[row + 1];
             if (ks > 1) {
@@ -554,7 +606,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         }
         int64_t nc = e < e_end ? static_cast<int64_t>(L.col[e]) : INT64_MAX;
         int nv = e < e_end ? static_cast<int>(L.val[e]) : 0;
-        for (int u = 0; u < nst; ++u) {
+        for (int u = 0; u < (kFold ? 0 : nst); ++u) {  // folding: the dequantising warps apply dW
             const int xs = u % XS;
             if (!mbar_wait(&xfull[xs], (u / XS) & 1, L.status)) {
                 s_abort = 1;
@@ -590,7 +642,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         }
 #pragma unroll
         for (int j = 0; j < kRegTok; ++j)
-            if (j < nr) corr[j] = cr[j];
+            if (!kFold && j < nr) corr[j] = cr[j];
     }
 
     // ---- epilogue (auxiliary warps): y = acc * s + dW of routed tokens
@@ -599,22 +651,30 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
         const int64_t row = rt * 128 + at;
         const float* corr = corr_s + at * (T + 1);
         const float sc = row < L.N ? __ldg(L.scale + row) : 0.0f;
+        // the producer's condition for the fold lists (route_all: s_nr = T)
+        const bool fo = kFold && dslot > 0 && L.fold != nullptr && s_nr > 0;
         const bool ok = mbar_wait(done, 0, L.status);
         if (!ok) s_abort = 1;
         tc_fence_after();
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
 #pragma unroll 1
         for (int t0 = 0; t0 < Tp; t0 += 16) {
-            uint32_t d[16];
+            uint32_t d[16], d2[16];
             tc_ld16(lane_base + t0, d);
+            if (fo) tc_ld16(lane_base + 64 + t0, d2);
             tc_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int t = t0 + j;
                 if (t >= T) break;
-                const float base = __fmul_rn(__uint_as_float(d[j]), sc);
                 const int p = s_pos[t];
-                const float v = p >= 0 ? __fadd_rn(base, corr[p]) : base;
+                float v;
+                if (kFold) {
+                    v = __fmul_rn(__uint_as_float(fo && p >= 0 ? d2[j] : d[j]), sc);
+                } else {
+                    const float base = __fmul_rn(__uint_as_float(d[j]), sc);
+                    v = p >= 0 ? __fadd_rn(base, corr[p]) : base;
+                }
                 if (ks == 1) {
                     if (row < L.N && !s_abort) {
                         const int64_t oi = static_cast<int64_t>(t) * L.N + row;
@@ -633,7 +693,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, 2) k_ctarq_mid(const __grid_
     if (warp == C::kMmaWarp) {
         if (s_abort) mbar_wait(done, 0, nullptr, kDrainNs);
         tc_fence_after();
-        tmem_dealloc(tmem, C::kTmemCols);
+        tmem_dealloc(tmem, kTmemCols);
     }
     if (s_abort && warp == C::kWProducerWarp && lane == 0)
         for (int it = wissued > WS ? wissued - WS : 0; it < wissued; ++it)
@@ -769,11 +829,11 @@ static int mid_ctas_per_sm(int64_t m) {
     if (have > 0) return have;
     int ws, xs;
     const int T = static_cast<int>(m), Tp = mid_tp(m);
-    mid_stages(T, Tp, MidCfg::kMaxSlot / 4, &ws, &xs);
+    mid_stages(T, Tp, MidCfg::kMaxSlot / 4, false, &ws, &xs);
     // shared memory decides (a block's registers and threads fit twice; two CTAs share the 512
-    // tensor-memory columns of an SM)
-    const int smem = MidCfg::total_bytes(ws, xs, T, Tp, MidCfg::kMaxSlot / 4);
-    const int n = smem + 2048 <= 112 * 1024 ? 2 : 1;
+    // tensor-memory columns of an SM); the folding variant takes all 512 columns
+    const int smem = MidCfg::total_bytes(ws, xs, T, Tp, MidCfg::kMaxSlot / 4, false);
+    const int n = m >= kMidFoldMinTokens ? 1 : smem + 2048 <= 112 * 1024 ? 2 : 1;
     cache[dev][m].store(n);
     return n;
 }
@@ -821,7 +881,17 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
         r.rc = route_consts(a.x_stride);
         r.xcopy = copy ? a.xconv : nullptr;
         r.counter = a.counter;
-        e = launch_pdl(k_mid_route<256>, dim3(static_cast<unsigned>(T)), dim3(256), 0, s, r);
+        const size_t row_bytes = static_cast<size_t>((a.x_stride * 2 + 15) / 16 * 16);
+        static std::atomic<uint64_t> rflags{0};
+        int rdev = 0;
+        cudaGetDevice(&rdev);
+        if (!(rflags.load() & (1ull << (rdev & 63)))) {
+            e = cudaFuncSetAttribute(k_mid_route<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRouterMaxRowBytes);
+            if (e != cudaSuccess) return e;
+            rflags.fetch_or(1ull << (rdev & 63));
+        }
+        if (row_bytes > static_cast<size_t>(kRouterMaxRowBytes)) return cudaErrorInvalidValue;
+        e = launch_pdl(k_mid_route<256>, dim3(static_cast<unsigned>(T)), dim3(256), row_bytes, s, r);
         if (e != cudaSuccess) return e;
     }
     MidParams* Pp = new MidParams();  // large and 64-byte aligned
@@ -843,16 +913,28 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
     P.ks = a.ks;
     P.T = T;
     P.Tp = Tp;
-    // dW segment slot: the group's largest segment, if it fits the slot limit
-    int dmax = 0;
-    bool dok = true;
+    // from 17 tokens the dequantising warps fold dW/s into a second A (every layer needs its lists);
+    // else a dW segment slot: the group's largest segment, if it fits the slot limit
+    bool fold = T >= kMidFoldMinTokens;
+    int fcap = 0;
     for (int i = 0; i < n; ++i) {
         const Layer& L = *a.layer[i];
-        if (L.nnz > 0 && !L.dseg) dok = false;
-        dmax = std::max(dmax, L.dseg_max);
+        if (L.nnz > 0 && !L.fold) fold = false;
+        if (L.fold) fcap = std::max(fcap, L.fold_cap);
     }
-    P.dslot = (dok && dmax > 0 && dmax <= MidCfg::kMaxSlot) ? dmax : 0;
-    mid_stages(T, Tp, P.dslot, &P.wstages, &P.xstages);
+    if (fold) {
+        P.dslot = fcap;
+    } else {
+        int dmax = 0;
+        bool dok = true;
+        for (int i = 0; i < n; ++i) {
+            const Layer& L = *a.layer[i];
+            if (L.nnz > 0 && !L.dseg) dok = false;
+            dmax = std::max(dmax, L.dseg_max);
+        }
+        P.dslot = (dok && dmax > 0 && dmax <= MidCfg::kMaxSlot) ? dmax : 0;
+    }
+    mid_stages(T, Tp, P.dslot, fold, &P.wstages, &P.xstages);
     P.route_all = a.route_all;
     P.x_col0 = a.x_col0;
     int ctas = 0;
@@ -881,6 +963,8 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
         M.nrouted = a.nrouted[i];
         M.dseg = L.dseg;
         M.dsegoff = L.dsegoff;
+        M.fold = L.fold;
+        M.foldoff = L.foldoff;
         M.cta0 = ctas;
         ctas += static_cast<int>(M.RT * a.ks);
         rt_off += M.RT;
@@ -889,19 +973,19 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
         P.L[i] = P.L[0];
         P.L[i].cta0 = ctas;
     }
-    const int smem = MidCfg::total_bytes(P.wstages, P.xstages, T, Tp, P.dslot);
-    static std::atomic<uint64_t> flags{0};
+    const int smem = MidCfg::total_bytes(P.wstages, P.xstages, T, Tp, P.dslot, fold);
+    static std::atomic<uint64_t> flags[2] = {{0}, {0}};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
+    auto kern = fold ? k_ctarq_mid<true> : k_ctarq_mid<false>;
     e = cudaSuccess;
-    if (!(flags.load() & bit)) {
-        e = cudaFuncSetAttribute(k_ctarq_mid, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(k_ctarq_mid, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-        if (e == cudaSuccess) flags.fetch_or(bit);
+    if (!(flags[fold ? 1 : 0].load() & bit)) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e == cudaSuccess) flags[fold ? 1 : 0].fetch_or(bit);
     }
-    if (e == cudaSuccess)
-        e = launch_pdl(k_ctarq_mid, dim3(static_cast<unsigned>(ctas)), dim3(MidCfg::kThreads), smem, s, P);
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(MidCfg::kThreads), smem, s, P);
     delete Pp;
     return e;
 }

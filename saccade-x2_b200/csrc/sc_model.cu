@@ -182,13 +182,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
         }
     }
     __syncthreads();
-    // unnormalised output of this block: threads over (g, d), keys in order
+    // unnormalised output of this block: thread (d, head group) adds its heads' p * v over the keys in
+    // order, so each V element is read by kAttnThreads / hd threads instead of once per query head
     const int64_t pbase = (t * nkv + h) * static_cast<int64_t>(nblk) + kb;
-    for (int i = tid; i < G * hd; i += kAttnThreads) {
-        const int g = i / hd, d = i % hd;
-        float o = 0.0f;
-        for (int j = 0; j < nk; ++j) o = __fadd_rn(o, __fmul_rn(s_p[g][j], vbase[static_cast<int64_t>(k0 + j) * hd + d]));
-        part_o[(pbase * G + g) * hd + d] = o;
+    {
+        const int ngrp = kAttnThreads / hd;
+        const int d = tid % hd, grp = tid / hd;
+        float o[kAttnMaxG / 2] = {};
+        const float* vcol = vbase + static_cast<int64_t>(k0) * hd + d;
+        for (int j = 0; j < nk; ++j) {
+            const float vv = vcol[static_cast<int64_t>(j) * hd];
+#pragma unroll
+            for (int r = 0; r < kAttnMaxG / 2; ++r) {
+                const int g = grp + r * ngrp;
+                if (g < G) o[r] = __fadd_rn(o[r], __fmul_rn(s_p[g][j], vv));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kAttnMaxG / 2; ++r) {
+            const int g = grp + r * ngrp;
+            if (g < G) part_o[(pbase * G + g) * hd + d] = o[r];
+        }
     }
     if (tid < G) {
         part_ml[(pbase * G + tid) * 2] = s_m[tid];
@@ -197,28 +211,41 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
 }
 
 // Rescales the key blocks of every (token, head) to their common max, adds them in block order and
-// writes out = o / l as f16 [T][nh * hd] (the o projection's input).
+// writes out = o / l as f16 [T][nh * hd] (the o projection's input).  The factors exp(m_b - m) and
+// the sum l depend on the head only: one thread per head computes them first.
+constexpr int kCombineMaxHeads = 128;
+constexpr int kCombineMaxBlk = 32;
 __global__ void k_attn_combine(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                const int32_t* __restrict__ pos, int nh, int nkv, int hd, int nblk,
                                uint16_t* __restrict__ out) {
     pdl_launch_dependents();
     pdl_wait();
+    __shared__ float s_f[kCombineMaxHeads][kCombineMaxBlk];
+    __shared__ float s_l[kCombineMaxHeads];
     const int64_t t = blockIdx.x;
     const int G = nh / nkv;
     const int nb = (pos[t] + kAttnKeys) / kAttnKeys;  // blocks holding keys of this token
-    for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) {
-        const int hq = i / hd, d = i % hd;
+    for (int hq = threadIdx.x; hq < nh; hq += blockDim.x) {
         const int h = hq / G, g = hq % G;
         const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
         float m = -INFINITY;
         for (int b = 0; b < nb; ++b) m = fmaxf(m, part_ml[((pb + b) * G + g) * 2]);
-        float l = 0.0f, o = 0.0f;
+        float l = 0.0f;
         for (int b = 0; b < nb; ++b) {
             const float f = nb == 1 ? 1.0f : exp_f32(__fsub_rn(part_ml[((pb + b) * G + g) * 2], m));
+            s_f[hq][b] = f;
             l = __fadd_rn(l, __fmul_rn(part_ml[((pb + b) * G + g) * 2 + 1], f));
-            o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], f));
         }
-        out[t * nh * hd + i] = f32_to_f16_bits(__fdiv_rn(o, l));
+        s_l[hq] = l;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) {
+        const int hq = i / hd, d = i % hd;
+        const int h = hq / G, g = hq % G;
+        const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
+        float o = 0.0f;
+        for (int b = 0; b < nb; ++b) o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], s_f[hq][b]));
+        out[t * nh * hd + i] = f32_to_f16_bits(__fdiv_rn(o, s_l[hq]));
     }
 }
 
@@ -303,7 +330,8 @@ sc_status sc_qwen2_attention(const float* q, const float* k_cache, const float* 
     if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
     if (!q || !k_cache || !v_cache || !slot || !pos || !scratch || !out_f16 || num_kv_heads <= 0 ||
         num_heads % num_kv_heads || num_heads / num_kv_heads > kAttnMaxG || head_dim > kAttnMaxHd ||
-        max_query_pos >= max_pos)
+        kAttnThreads % head_dim != 0 || head_dim % 32 != 0 || num_heads > kCombineMaxHeads ||
+        max_query_pos >= max_pos || (max_query_pos + kAttnKeys) / kAttnKeys > kCombineMaxBlk)
         return SC_EINVAL;
     if (scratch_bytes < sc_qwen2_attention_scratch(tokens, num_heads, num_kv_heads, head_dim, max_pos))
         return SC_ENOMEM;

@@ -20,6 +20,8 @@
 //
 // The staged layout xk is the tcgen05 K-major core-matrix layout of sc_device.cuh:
 // xk_index, with tokens padded to a multiple of 16 (the MMA N granularity).
+#include <atomic>
+
 #include "sc_device.cuh"
 #include "sc_internal.h"
 
@@ -54,6 +56,7 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
     __shared__ int s_wsum[kWarps];
     __shared__ int s_open;
     __shared__ ReplayShared s_replay;
+    extern __shared__ __align__(16) uint16_t s_row[];  // the token as f16 bits [Kfull]
     const int64_t t = blockIdx.x;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -101,6 +104,7 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
                 s2 += v * v;
                 sa += fabs(v);
             }
+            *reinterpret_cast<uint4*>(&s_row[ch * 8]) = *reinterpret_cast<const uint4*>(h);
             if (ch >= ch_lo && ch < ch_hi)
                 *reinterpret_cast<uint4*>(&a.xk[xk_index((ch - ch_lo) * 8, static_cast<int>(t), static_cast<int>(a.Mp))]) =
                     *reinterpret_cast<const uint4*>(h);
@@ -121,7 +125,6 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
             red[2][warp] = sa;
         }
         __syncthreads();
-        const void* xrow = static_cast<const unsigned char*>(a.x) + row_off * 2;
         if (tid == 0) {
             double S1 = 0.0, S2 = 0.0, SA = 0.0;
             for (int w = 0; w < kWarps; ++w) {
@@ -140,13 +143,13 @@ __global__ void __launch_bounds__(kThreads) k_router(RouterKernelArgs a) {
         __syncthreads();
         if (s_open) {
             // the f64 score is inside the f32 error band: the CTA replays the reference's chains
-            replay_score<kThreads>(xrow, a.x_dtype, a.Kfull, s_replay);
+            replay_score<kThreads>(s_row, a.Kfull, s_replay);
             if (tid == 0) {
                 const bool rl = route_rule_f32(s_replay.lo, a.t4, a.t8), rh = route_rule_f32(s_replay.hi, a.t4, a.t8);
                 float score = s_replay.lo;
                 bool routed = rl;
                 if (rl != rh || !(s_replay.lo == s_replay.lo)) {  // a threshold within an ulp, or inf / nan
-                    score = exact_variance(xrow, a.x_dtype, a.Kfull);
+                    score = exact_variance_row(s_row, a.Kfull);
                     routed = route_rule_f32(score, a.t4, a.t8);
                 }
                 a.mask[t] = routed ? 1 : 0;
@@ -232,7 +235,20 @@ cudaError_t launch_router(const RouterArgs& r, cudaStream_t s) {
     a.perm = r.perm;
     a.counter = r.counter;
     a.status = r.status;
-    return launch_pdl(k_router<256>, dim3(static_cast<unsigned>(r.Mp)), dim3(256), 0, s, a);
+    // dynamic shared memory: the token row (f16), for the replay of tokens inside the error band
+    const size_t row_bytes = static_cast<size_t>((a.Kfull * 2 + 15) / 16 * 16);
+    static std::atomic<uint64_t> flags{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(flags.load() & bit)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(k_router<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRouterMaxRowBytes);
+        if (e != cudaSuccess) return e;
+        flags.fetch_or(bit);
+    }
+    if (row_bytes > static_cast<size_t>(kRouterMaxRowBytes)) return cudaErrorInvalidValue;
+    return launch_pdl(k_router<256>, dim3(static_cast<unsigned>(r.Mp)), dim3(256), row_bytes, s, a);
 }
 
 }  // namespace sc

@@ -1,5 +1,7 @@
 """The 9..64-token path (batched decode): the router kernel, then the tcgen05 f16 GEMM with the
-tokens as the MMA's N side and dW of the routed tokens taken from the staged token tiles.
+tokens as the MMA's N side; dW of the routed tokens from the staged token tiles (9..16 tokens), or
+from 17 tokens folded into a second tensor-memory A, (q - 8) + dW/s, whose products the routed
+tokens take (layers whose fold lists exceed 8 KB, e.g. 30 % dW, keep the staged-tile path).
 
 The products are exact (f16 tokens times integers q - 8, f32 accumulation); these cases cover wide
 dynamic ranges, tiny and huge values, a single outlier, subnormals, non-finite inputs, groups with
