@@ -572,7 +572,7 @@ def build_decode(args, rank, world, dev, group):
     g = torch.Generator()
     g.manual_seed(7)
     calib = torch.randint(0, cfg.vocab, (1, args.prompt), generator=g)
-    Q.calibrate(ck, calib.to(dev), max_pos=args.prompt)
+    Q.calibrate(ck, calib.to(dev), device=dev, max_pos=args.prompt)
     if world > 1:  # every rank calibrates the same model; rank 0's thresholds are the ones used
         import torch.distributed as dist
         th = torch.tensor([ck.thresholds[li][n] for li in range(len(ck.blocks)) for n in DECODE_PROJ],

@@ -203,6 +203,9 @@ WsLayout plan_workspace(const Layer& L, int64_t m) {
         w.ksplit = static_cast<int>(ks);
         w.partial = take(static_cast<size_t>(ks > 1 ? RT * ks * 128 * 32 * 4 : 16));
     }
+    // a ROWS shard's exchange (sc_forward_split) also needs its slice transposed, [K][tokens to 16],
+    // after everything its base product's own layout (an unsharded one, never larger) may use
+    if (L.shard_kind == SC_SHARD_ROWS) w.xt = take(static_cast<size_t>(L.KB * 64 * ((m + 15) / 16 * 16) * 2));
     w.total = off;
     return w;
 }
@@ -945,17 +948,23 @@ sc_status sc_forward_split(const sc_layer* layer, const void* x, int x_dtype, in
     B.t4 = B.t8 = std::numeric_limits<float>::quiet_NaN();
     void* ws = workspace;
     size_t wsb = workspace_bytes;
+    const size_t need = plan_workspace(layer->L, m).total;
     if (!ws) {
-        wsb = plan_workspace(B, m).total;
+        wsb = need;
         sc_status st = default_workspace(B.device, wsb, &ws);
         if (st != SC_OK) return st;
+    } else if (wsb < need || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) {
+        set_error("sc_forward_split: workspace of " + std::to_string(wsb) + " bytes (256-byte aligned), need " +
+                  std::to_string(need));
+        return SC_ENOMEM;
     }
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     sc_status st = forward_impl(B, x, x_dtype, m, exchange, SC_F32, nullptr, nullptr, nullptr, nullptr, ws, wsb, s,
                                 true, true);
     if (st != SC_OK) return st;
     const int64_t mn = m * layer->L.N;
-    cudaError_t e = launch_split_extras(layer->L, x, x_dtype, m, exchange + mn, exchange + 2 * mn, s);
+    uint16_t* xt = reinterpret_cast<uint16_t*>(static_cast<unsigned char*>(ws) + plan_workspace(layer->L, m).xt);
+    cudaError_t e = launch_split_extras(layer->L, x, x_dtype, m, exchange + mn, exchange + 2 * mn, xt, s);
     if (e != cudaSuccess) return cuda_fail(e, "sc_forward_split launch");
     return SC_OK;
 }

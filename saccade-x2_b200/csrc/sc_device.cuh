@@ -637,13 +637,15 @@ __device__ __forceinline__ void fold_add(uint32_t (&h)[4][4], int slot, int hi, 
 constexpr int kReplayItems = 4;
 constexpr int kReplayMaxThreads = 256;
 struct ReplayShared {
-    int4 item[kReplayMaxThreads][kReplayItems];  // {0, B, R even, R odd} or {1, i0, i1, 0}
+    // {0 | end parity after an even start << 1 | after an odd start << 2, B, R even, R odd} or {1, i0, i1, 0}
+    int4 item[kReplayMaxThreads][kReplayItems];
     int4 flat[kReplayMaxThreads * kReplayItems];  // the items of all threads in order
     int count[kReplayMaxThreads];
     double w2[kReplayMaxThreads / 32];
     long long w1[kReplayMaxThreads / 32];
     double wabs[kReplayMaxThreads / 32];
     int wcnt[kReplayMaxThreads / 32];
+    int wstart[kReplayMaxThreads / 32], wmerged[kReplayMaxThreads / 32];
     float lo, hi;
 };
 
@@ -729,7 +731,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         if (Pp > 0.0) {
             B = static_cast<int>((__double_as_longlong(Pp) >> 52) & 0x7FF) - 1023;
             const double iu = static_cast<double>(i + 1) * 5.9604644775390625e-08;
-            const double d = iu / (1.0 - iu) + 1e-9;
+            const double d = iu * (1.0 + 2.0 * iu) + 1e-9;  // >= gamma = iu / (1 - iu) for iu <= 1/2
             const double base = __longlong_as_double(static_cast<long long>(B + 1023) << 52);
             if (Pp * (1.0 - d) >= base && P2 + d * Pp < 2.0 * base) {
                 sc = __fmul_rn(v, __int_as_float((127 + 23 - B) << 23));  // v / g, exact
@@ -739,7 +741,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         if (certain) {
             if (!(kind == 0 && curB == B)) {
                 if (kind == 0) {
-                    sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+                    sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
                 } else if (kind == 1) {
                     sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(seq1), 0);
                 }
@@ -767,7 +769,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
             par1 = (par1 + static_cast<int>(r1)) & 1;
         } else {
             if (kind != 1) {
-                if (kind == 0) sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+                if (kind == 0) sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
                 if (n_it == kReplayItems - 1) tail = true;
                 kind = 1;
                 seq0 = i;
@@ -776,7 +778,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         }
     }
     if (kind == 0) {
-        sh.item[tid][n_it++] = make_int4(0, curB, __float_as_int(R0), __float_as_int(R1));
+        sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
     } else if (kind == 1) {
         sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(tail ? i1 : seq1), 0);
     }
@@ -798,20 +800,46 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         total += sh.wcnt[w];
     }
     for (int j = 0; j < n_it; ++j) sh.flat[at + j] = sh.item[tid][j];
+    if (lane == 0) sh.wstart[warp] = at;
+    __syncthreads();
+    // each warp's lane 0 composes consecutive runs of one binade (the parity after a run is a function
+    // of the parity before it), in place; thread 0 then walks what remains
+    if (lane == 0) {
+        const int b0 = sh.wstart[warp], b1 = warp + 1 < kWarps ? sh.wstart[warp + 1] : total;
+        int out = b0;
+        for (int j = b0; j < b1; ++j) {
+            const int4 it = sh.flat[j];
+            if (out > b0) {
+                int4& pv = sh.flat[out - 1];
+                if (it.x != 1 && (pv.x & 1) == 0 && pv.y == it.y) {
+                    const int e0 = (pv.x >> 1) & 1, e1 = (pv.x >> 2) & 1;  // parity after pv from an even / odd start
+                    const float R0 = __fadd_rn(__int_as_float(pv.z), __int_as_float(e0 ? it.w : it.z));
+                    const float R1 = __fadd_rn(__int_as_float(pv.w), __int_as_float(e1 ? it.w : it.z));
+                    const int f0 = e0 ? (it.x >> 2) & 1 : (it.x >> 1) & 1;
+                    const int f1 = e1 ? (it.x >> 2) & 1 : (it.x >> 1) & 1;
+                    pv = make_int4((f0 << 1) | (f1 << 2), pv.y, __float_as_int(R0), __float_as_int(R1));
+                    continue;
+                }
+            }
+            sh.flat[out++] = it;
+        }
+        sh.wmerged[warp] = out;
+    }
     __syncthreads();
     if (tid == 0) {
         float q = 0.0f;
-        int4 nx = sh.flat[0];
-        for (int j = 0; j < total; ++j) {
-            const int4 it = nx;
-            if (j + 1 < total) nx = sh.flat[j + 1];  // the next item loaded ahead
-            if (it.x == 0) {
-                const float R = __int_as_float((__float_as_uint(q) & 1u) ? it.w : it.z);
-                q = __fadd_rn(q, __fmul_rn(R, __int_as_float((127 + it.y - 23) << 23)));
-            } else {
-                for (int i = it.y; i < it.z; ++i) {
-                    const float xf = h2f(row[i]);
-                    q = __fadd_rn(q, __fmul_rn(xf, xf));
+        for (int w = 0; w < kWarps; ++w) {
+            const int b0 = sh.wstart[w], b1 = sh.wmerged[w];
+            for (int j = b0; j < b1; ++j) {
+                const int4 it = sh.flat[j];
+                if ((it.x & 1) == 0) {
+                    const float R = __int_as_float((__float_as_uint(q) & 1u) ? it.w : it.z);
+                    q = __fadd_rn(q, __fmul_rn(R, __int_as_float((127 + it.y - 23) << 23)));
+                } else {
+                    for (int i = it.y; i < it.z; ++i) {
+                        const float xf = h2f(row[i]);
+                        q = __fadd_rn(q, __fmul_rn(xf, xf));
+                    }
                 }
             }
         }

@@ -94,6 +94,7 @@ struct WsLayout {
     int gemm_ks = 0;             // prefill GEMM column splits (0: the GEMM does not serve the call)
     size_t xconv = 0;            // 9..64-token GEMM: f16 copy of bf16 (or unaligned) tokens
     int mid_ks = 0;              // its column splits (0: it does not serve the call)
+    size_t xt = 0;               // ROWS shards: the slice transposed for sc_forward_split
     size_t total = 0;
     int ksplit = 1;
     int chunk_tokens = 0;        // tokens per decode launch
@@ -283,7 +284,7 @@ void set_drop_weight_copy(int on);
 
 // Exchange step of a ROWS shard that holds only its input slice (sc_split.cu).
 cudaError_t launch_split_extras(const Layer& L, const void* x, int x_dtype, int64_t m, float* y_delta, float* stats,
-                                cudaStream_t s);
+                                uint16_t* xt, cudaStream_t s);
 cudaError_t launch_split_finalize(const Layer& L, const float* exch, int64_t m, int ranks, int route_all, void* y,
                                   int y_dtype, const float* bias, uint8_t* mask_out, uint32_t* undecided,
                                   cudaStream_t s);

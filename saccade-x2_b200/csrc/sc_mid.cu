@@ -843,8 +843,8 @@ int mid_ksplit(int64_t rt_total, int64_t kb, int sms, int64_t m) {
     int64_t ks = (wave + rt_total / 2) / rt_total;
     const int64_t kmax = kb / 4 > 0 ? kb / 4 : 1;  // at least four blocks (two stages) per split
     if (ks > kmax) ks = kmax;
-    // the last CTA of a row tile reads ks x m partial rows: fewer splits as the tokens grow
-    const int64_t cap = m <= 16 ? 16 : m <= 32 ? 8 : 4;
+    // the last CTA of a row tile reads ks x m partial rows: fewer splits beyond 16 tokens
+    const int64_t cap = m <= 16 ? 16 : 8;
     if (ks > cap) ks = cap;
     if (ks < 1) ks = 1;
     return static_cast<int>(ks);

@@ -122,6 +122,7 @@ constexpr int kAttnThreads = 256;
 constexpr int kAttnKeys = 256;      // keys per CTA
 constexpr int kAttnMaxG = 8;        // query heads per kv head
 constexpr int kAttnMaxHd = 128;
+constexpr int kAttnChunk = 32;      // keys staged in shared memory at a time (coalesced 16-byte loads)
 
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q, const float* __restrict__ kc,
                                                        const float* __restrict__ vc, const int32_t* __restrict__ slot,
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
     __shared__ float s_q[kAttnMaxG][kAttnMaxHd];
     __shared__ float s_p[kAttnMaxG][kAttnKeys];
     __shared__ float s_m[kAttnMaxG], s_l[kAttnMaxG];
+    __shared__ __align__(16) float s_kv[kAttnChunk * kAttnMaxHd];  // K or V rows [chunk][hd]
     const int64_t t = blockIdx.x / (nkv * nblk);
     const int rem = blockIdx.x % (nkv * nblk);
     const int h = rem / nblk, kb = rem % nblk;
@@ -145,23 +147,34 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
     for (int i = tid; i < G * hd; i += kAttnThreads) s_q[i / hd][i % hd] = q[(t * nh + h * G + i / hd) * hd + i % hd];
     __syncthreads();
     const int nk = k1 > k0 ? k1 - k0 : 0;
+    // stages rows [c0, c0 + cn) of a K or V block into s_kv, 16 bytes per thread and load
+    auto stage = [&](const float* base, int c0, int cn) {
+        const float4* src = reinterpret_cast<const float4*>(base + static_cast<int64_t>(k0 + c0) * hd);
+        float4* dst = reinterpret_cast<float4*>(s_kv);
+        for (int i = tid; i < cn * hd / 4; i += kAttnThreads) dst[i] = __ldg(src + i);
+    };
     // scores: one warp per key, lanes over head_dim, a fixed shuffle tree
-    for (int j = warp; j < nk; j += kAttnThreads / 32) {
-        const float* kr = kbase + static_cast<int64_t>(k0 + j) * hd;
-        float kv[kAttnMaxHd / 32];
+    for (int c0 = 0; c0 < nk; c0 += kAttnChunk) {
+        const int cn = min(kAttnChunk, nk - c0);
+        stage(kbase, c0, cn);
+        __syncthreads();
+        for (int j = warp; j < cn; j += kAttnThreads / 32) {
+            const float* kr = s_kv + j * hd;
+            float kv[kAttnMaxHd / 32];
 #pragma unroll
-        for (int e = 0; e < kAttnMaxHd / 32; ++e) kv[e] = (lane + 32 * e < hd) ? kr[lane + 32 * e] : 0.0f;
-        for (int g = 0; g < G; ++g) {
-            float d = 0.0f;
+            for (int e = 0; e < kAttnMaxHd / 32; ++e) kv[e] = (lane + 32 * e < hd) ? kr[lane + 32 * e] : 0.0f;
+            for (int g = 0; g < G; ++g) {
+                float d = 0.0f;
 #pragma unroll
-            for (int e = 0; e < kAttnMaxHd / 32; ++e)
-                if (lane + 32 * e < hd) d = __fadd_rn(d, __fmul_rn(s_q[g][lane + 32 * e], kv[e]));
+                for (int e = 0; e < kAttnMaxHd / 32; ++e)
+                    if (lane + 32 * e < hd) d = __fadd_rn(d, __fmul_rn(s_q[g][lane + 32 * e], kv[e]));
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
-            if (lane == 0) s_p[g][j] = __fmul_rn(d, scale);
+                for (int o = 16; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+                if (lane == 0) s_p[g][c0 + j] = __fmul_rn(d, scale);
+            }
         }
+        __syncthreads();
     }
-    __syncthreads();
     // per head: block max, exp, block sum (one warp per head)
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float m = -INFINITY;
@@ -189,13 +202,18 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
         const int ngrp = kAttnThreads / hd;
         const int d = tid % hd, grp = tid / hd;
         float o[kAttnMaxG / 2] = {};
-        const float* vcol = vbase + static_cast<int64_t>(k0) * hd + d;
-        for (int j = 0; j < nk; ++j) {
-            const float vv = vcol[static_cast<int64_t>(j) * hd];
+        for (int c0 = 0; c0 < nk; c0 += kAttnChunk) {
+            const int cn = min(kAttnChunk, nk - c0);
+            __syncthreads();  // the previous chunk is read
+            stage(vbase, c0, cn);
+            __syncthreads();
+            for (int j = 0; j < cn; ++j) {
+                const float vv = s_kv[j * hd + d];
 #pragma unroll
-            for (int r = 0; r < kAttnMaxG / 2; ++r) {
-                const int g = grp + r * ngrp;
-                if (g < G) o[r] = __fadd_rn(o[r], __fmul_rn(s_p[g][j], vv));
+                for (int r = 0; r < kAttnMaxG / 2; ++r) {
+                    const int g = grp + r * ngrp;
+                    if (g < G) o[r] = __fadd_rn(o[r], __fmul_rn(s_p[g][c0 + j], vv));
+                }
             }
         }
 #pragma unroll

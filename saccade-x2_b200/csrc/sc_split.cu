@@ -17,27 +17,72 @@
 
 namespace sc {
 
-// y_delta[t][r] for one 128-row tile and 8 tokens per CTA: thread r walks row r's entries in order.
-__global__ void __launch_bounds__(128) k_split_delta(const void* __restrict__ x, int x_dtype, int64_t m, int64_t K,
-                                                     const uint32_t* __restrict__ rowptr, const uint16_t* __restrict__ col,
-                                                     const int8_t* __restrict__ val, float ds, int64_t N,
-                                                     float* __restrict__ y_delta) {
+// The slice transposed, xt[c][t] (f16 bits; tokens padded with zeros to a multiple of 16), so that one
+// dW entry reads the values of 16 tokens with two 16-byte loads.
+__global__ void __launch_bounds__(256) k_split_transpose(const void* __restrict__ x, int x_dtype, int64_t m, int64_t K,
+                                                         int64_t Tp, uint16_t* __restrict__ xt) {
     pdl_launch_dependents();
     pdl_wait();
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * 128 + threadIdx.x;
-    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * 8;
+    __shared__ uint16_t tile[32][33];
+    const int64_t c0 = static_cast<int64_t>(blockIdx.x) * 32, t0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int r = ty; r < 32; r += 8) {
+        const int64_t t = t0 + r, c = c0 + tx;
+        tile[r][tx] = (t < m && c < K) ? x_f16_bits(x, x_dtype, t * K + c) : 0;
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int64_t c = c0 + r, t = t0 + tx;
+        if (c < K && t < Tp) xt[c * Tp + t] = tile[tx][r];
+    }
+}
+
+// y_delta[t][r] for 64 rows and 16 tokens per CTA: thread r walks row r's entries in column order, 8 at a
+// time (their columns, values and the 16 tokens' values of each column loaded before any is used).
+constexpr int kDeltaRows = 64;
+__global__ void __launch_bounds__(kDeltaRows) k_split_delta(const uint16_t* __restrict__ xt, int64_t Tp, int64_t m,
+                                                            const uint32_t* __restrict__ rowptr,
+                                                            const uint16_t* __restrict__ col,
+                                                            const int8_t* __restrict__ val, float ds, int64_t N,
+                                                            float* __restrict__ y_delta) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kDeltaRows + threadIdx.x;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * 16;
     if (row >= N) return;
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const int64_t e1 = rowptr[row + 1];
-    for (int64_t e = rowptr[row]; e < e1; ++e) {
-        const int64_t c = col[e];
-        const float v = __fmul_rn(static_cast<float>(val[e]), ds);
+    float acc[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (t0 + j < m) acc[j] = __fadd_rn(acc[j], __fmul_rn(h2f(x_f16_bits(x, x_dtype, (t0 + j) * K + c)), v));
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
+    const int64_t e1 = rowptr[row + 1];
+    for (int64_t e = rowptr[row]; e < e1; e += 8) {
+        int64_t c[8];
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const bool ok = e + i < e1;
+            c[i] = ok ? static_cast<int64_t>(col[e + i]) : 0;
+            v[i] = ok ? __fmul_rn(static_cast<float>(val[e + i]), ds) : 0.0f;
+        }
+        uint4 xa[8], xb[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint4* p = reinterpret_cast<const uint4*>(xt + c[i] * Tp + t0);
+            xa[i] = __ldg(p);
+            xb[i] = __ldg(p + 1);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (e + i >= e1) break;
+            const uint32_t w[8] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w, xb[i].x, xb[i].y, xb[i].z, xb[i].w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(h2f(static_cast<uint16_t>(w[j] & 0xFFFFu)), v[i]));
+                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(h2f(static_cast<uint16_t>(w[j] >> 16)), v[i]));
+            }
+        }
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < 16; ++j)
         if (t0 + j < m) y_delta[(t0 + j) * N + row] = acc[j];
 }
 
@@ -109,12 +154,17 @@ __global__ void __launch_bounds__(256) k_split_finalize(const float* __restrict_
 }
 
 cudaError_t launch_split_extras(const Layer& L, const void* x, int x_dtype, int64_t m, float* y_delta, float* stats,
-                                cudaStream_t s) {
+                                uint16_t* xt, cudaStream_t s) {
     cudaError_t e = cudaSuccess;
     if (L.nnz > 0) {
-        const dim3 grid(static_cast<unsigned>((L.N + 127) / 128), static_cast<unsigned>((m + 7) / 8));
-        e = launch_pdl(k_split_delta, grid, dim3(128), 0, s, x, x_dtype, m, L.K, L.rowptr, L.col, L.val, L.ds, L.N,
-                       y_delta);
+        const int64_t Tp = (m + 15) / 16 * 16;
+        e = launch_pdl(k_split_transpose, dim3(static_cast<unsigned>((L.K + 31) / 32), static_cast<unsigned>((Tp + 31) / 32)),
+                       dim3(256), 0, s, x, x_dtype, m, L.K, Tp, xt);
+        if (e == cudaSuccess) {
+            const dim3 grid(static_cast<unsigned>((L.N + kDeltaRows - 1) / kDeltaRows), static_cast<unsigned>(Tp / 16));
+            e = launch_pdl(k_split_delta, grid, dim3(kDeltaRows), 0, s, static_cast<const uint16_t*>(xt), Tp, m, L.rowptr,
+                           L.col, L.val, L.ds, L.N, y_delta);
+        }
     } else {
         e = cudaMemsetAsync(y_delta, 0, static_cast<size_t>(m * L.N * 4), s);
     }

@@ -137,7 +137,7 @@ class SaccadeLinearOp:
             if t is None:
                 return None
             t = t.contiguous()
-            if on_dev and not t.is_cuda:
+            if on_dev and t.device != self.device:  # host tensors, or another GPU's: the layer's device
                 t = t.to(self.device)
             if not on_dev and t.is_cuda:
                 t = t.cpu()

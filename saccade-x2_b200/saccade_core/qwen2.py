@@ -182,10 +182,10 @@ class Qwen2Model:
     """Qwen2Model::forward on one GPU, or one rank of a tensor-parallel group (tp = (rank, world,
     process_group) with NCCL).  Serves up to `max_batch` sequences of up to `max_pos` positions."""
 
-    def __init__(self, ck: Checkpoint, device="cuda:0", max_batch: int = 1, max_pos: int = 512, mode: str = "fast",
+    def __init__(self, ck: Checkpoint, device=None, max_batch: int = 1, max_pos: int = 512, mode: str = "fast",
                  tp=None):
         self.cfg = cfg = ck.cfg
-        self.device = dev = torch.device(device)
+        self.device = dev = torch.device(ck.embed.device if device is None else device)
         self.max_batch, self.max_pos = max_batch, max_pos
         self.rank, self.world, self.group = tp if tp is not None else (0, 1, None)
         self.q0, self.q1, self.k0, self.k1 = head_split(cfg, self.rank, self.world)
@@ -213,16 +213,16 @@ class Qwen2Model:
             L["qkv"] = SaccadeLinearGroup([L["q"], L["k"], L["v"]])
             L["gateup"] = SaccadeLinearGroup([L["gate"], L["up"]])
             bq = ck.biases[li]
-            L["bias"] = [bq["q"][self.q0 * hd:self.q1 * hd].contiguous().float(),
-                         bq["k"][self.k0 * hd:self.k1 * hd].contiguous().float(),
-                         bq["v"][self.k0 * hd:self.k1 * hd].contiguous().float()]
-            L["norm_in"] = ck.norms[li]["input"].float().contiguous()
-            L["norm_post"] = ck.norms[li]["post"].float().contiguous()
+            L["bias"] = [bq["q"][self.q0 * hd:self.q1 * hd].to(dev, torch.float32).contiguous(),
+                         bq["k"][self.k0 * hd:self.k1 * hd].to(dev, torch.float32).contiguous(),
+                         bq["v"][self.k0 * hd:self.k1 * hd].to(dev, torch.float32).contiguous()]
+            L["norm_in"] = ck.norms[li]["input"].to(dev, torch.float32).contiguous()
+            L["norm_post"] = ck.norms[li]["post"].to(dev, torch.float32).contiguous()
             self.layers.append(L)
-        self.final_norm = ck.final_norm.float().contiguous()
-        self.embed = ck.embed.contiguous()
+        self.final_norm = ck.final_norm.to(dev, torch.float32).contiguous()
+        self.embed = ck.embed.to(dev).contiguous()
         self.v0, self.v1 = vocab_split(cfg, self.rank, self.world)
-        table = ck.embed if ck.lm_head is None else ck.lm_head
+        table = (ck.embed if ck.lm_head is None else ck.lm_head).to(dev)
         if self.world > 1:
             table = table[self.v0:self.v1].contiguous()
         self.lm_head_t = table.t()  # [hidden, vocab slice] view, f16
@@ -345,11 +345,13 @@ class Qwen2Model:
 
 # ------------------------------------------------------------------ calibration and generation
 
-def calibrate(ck: Checkpoint, prompt: torch.Tensor, pct=(0.75, 0.95), device="cuda:0", mode="fast",
+def calibrate(ck: Checkpoint, prompt: torch.Tensor, pct=(0.75, 0.95), device=None, mode="fast",
               max_pos: Optional[int] = None) -> None:
     """ProfileRunner::calibrate per projection (calibration.rs:10-47) on the inputs each projection
-    sees while `prompt` [B, S] runs through the model with nothing routed; writes ck.thresholds."""
+    sees while `prompt` [B, S] runs through the model with nothing routed; writes ck.thresholds.
+    The model runs on `device` (default: the checkpoint's)."""
     B, S = prompt.shape
+    device = ck.embed.device if device is None else device
     model = Qwen2Model(ck, device, max_batch=B, max_pos=max_pos or S, mode=mode)
     acts = {}
     orig = {}
@@ -406,9 +408,7 @@ class GreedyDecoder:
         self.logits = None
         self.graph = None
         self.stream = torch.cuda.Stream(device=dev)
-        if model.world > 1:
-            self._cand = torch.zeros(batch, 2, dtype=torch.float32, device=dev)
-            self._gath = torch.zeros(model.world, batch, 2, dtype=torch.float32, device=dev)
+        self._xchg = {}  # rows -> ((rows, 2), (world, rows, 2)) f32 buffers of the tensor-parallel argmax
 
     def argmax(self, logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """Greedy token of each row: over this rank's vocabulary slice, then (tensor parallel) the
@@ -416,12 +416,17 @@ class GreedyDecoder:
         m = self.model
         if m.world == 1:
             return torch.argmax(logits, dim=-1, out=out)
+        n = logits.shape[0]
+        if n not in self._xchg:
+            self._xchg[n] = (torch.zeros(n, 2, dtype=torch.float32, device=m.device),
+                             torch.zeros(m.world, n, 2, dtype=torch.float32, device=m.device))
+        cand, gath = self._xchg[n]
         val, idx = torch.max(logits, dim=-1)
-        self._cand[:, 0].copy_(val)
-        self._cand[:, 1].copy_(idx + m.v0)  # ids < 2^24 are exact in f32
-        torch.distributed.all_gather_into_tensor(self._gath, self._cand, group=m.group)
-        best = torch.argmax(self._gath[:, :, 0], dim=0)  # first rank holding the maximum
-        out.copy_(self._gath[:, :, 1].gather(0, best[None, :])[0].to(torch.int64))
+        cand[:, 0].copy_(val)
+        cand[:, 1].copy_(idx + m.v0)  # ids < 2^24 are exact in f32
+        torch.distributed.all_gather_into_tensor(gath, cand, group=m.group)
+        best = torch.argmax(gath[:, :, 0], dim=0)  # first rank holding the maximum
+        out.copy_(gath[:, :, 1].gather(0, best[None, :])[0].to(torch.int64))
         return out
 
     def prefill(self, prompt: torch.Tensor, chunk: int = 0) -> torch.Tensor:
