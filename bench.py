@@ -777,8 +777,10 @@ def run_decode(args, rank, world):
                    "setup_s": round(setup_s, 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": f"gate+up C-TARQ call unit at M={B} ({gu_launches} launches: router, token gather, "
-                               f"tcgen05 GEMM), {us_gu:.1f} us per layer, {gu_bytes} algorithmic bytes",
+                     "kernel": f"gate+up C-TARQ call unit at M={B} ({gu_launches} launches: "
+                               + ("k_mid_route, then k_ctarq_mid (tcgen05, routed tokens' dW folded into a second A)"
+                                  if 9 <= B <= 64 else "router, token gather, prefill tcgen05 GEMM")
+                               + f"), {us_gu:.1f} us per layer, {gu_bytes} algorithmic bytes",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
         "e2e": {"value": round(B / (ms_e2e / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 8,

@@ -167,7 +167,7 @@ def _mlp_rank(rank, world, port, q):
     try:
         gate, up, down, xb = _mlp_layers()
         inter = gate.out_features
-        r0, r1 = inter * rank // world, inter * (rank + 1) // world
+        r0, r1 = rows_shard_columns(inter, rank, world)  # down's ROWS shard; gate/up keep the same rows
         # column-parallel gate and up: this rank's rows, x replicated, no exchange
         g, _, _ = O.OracleLinear(row_slice(gate, r0, r1), 8.0, 3e38).forward(xb)
         u, _, _ = O.OracleLinear(row_slice(up, r0, r1), 8.0, 3e38).forward(xb)
@@ -211,7 +211,7 @@ def test_tensor_parallel_mlp_two_ranks():
     assert rd.tolist() == [0, 0, 0, 1, 0]
     inter = gate.out_features
     for rank, g_r, u_r, h_r, routed_r, y_r, undecided in results:
-        r0, r1 = inter * rank // world, inter * (rank + 1) // world
+        r0, r1 = rows_shard_columns(inter, rank, world)
         assert np.array_equal(g_r, g[:, r0:r1]) and np.array_equal(u_r, u[:, r0:r1]), "rows are independent"
         assert np.array_equal(h_r, h[:, r0:r1])
         assert undecided == 0 and np.array_equal(routed_r, rd), "routed on the summed sums as on whole tokens"
