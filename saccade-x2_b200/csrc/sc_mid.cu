@@ -14,7 +14,8 @@
 //   x producer       one TMA box per 64-column block: 64 f16 (128 B) of every token, landing in the
 //                    128-byte-swizzled K-major operand layout (rows past the last token and columns
 //                    past the last one zero-filled);
-//   4 warps          dequantise the weights into tensor memory (A), three stages deep;
+//   4 warps          dequantise the weights into tensor memory (A), three stages deep (from 17 tokens
+//                    two sets of 4, taking alternate stages);
 //   MMA warp         one elected lane issues 4 MMAs per 64-column block;
 //   4 aux warps      one thread per row: the row's dW entries of each staged block (op.rs:152-170,
 //                    CSR columns ascending) for the routed tokens, from the staged x; then the
@@ -238,12 +239,6 @@ struct alignas(64) MidParams {
 };
 
 struct MidCfg {
-    static constexpr int kDqWarps = 4;           // warp w: TMEM lanes 32w..32w+31 (two 16-row tiles)
-    static constexpr int kWProducerWarp = 4;
-    static constexpr int kXProducerWarp = 5;
-    static constexpr int kMmaWarp = 6;
-    static constexpr int kAuxWarp0 = 7;          // four warps, one thread per row
-    static constexpr int kThreads = 11 * 32;
     static constexpr int SKB = 2;                // 64-column blocks per ring stage
     static constexpr int AB = 3;                 // tensor-memory A buffers (one stage each)
     static constexpr int kColsPerBlock = 32;     // TMEM columns of one block of f16 A (128 rows x 128 B)
@@ -312,9 +307,21 @@ __device__ __forceinline__ float staged_x(const unsigned char* blk, int t, int c
     return h2f(*reinterpret_cast<const uint16_t*>(blk + t * 128 + ((((c >> 3) ^ t) & 7) << 4) + (c & 7) * 2));
 }
 
+// Warps of the two variants: the folding one has two sets of 4 dequantising warps taking alternate
+// stages (one set's hand-off latency hides behind the other's work); roles follow the dequantisers.
 template <bool kFold>
-__global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(const __grid_constant__ MidParams P) {
+struct MidRoles {
+    static constexpr int kDq = kFold ? 8 : 4;    // dequantising warps; warp w: TMEM lanes 32 (w % 4)
+    static constexpr int kSets = kDq / 4;
+    static constexpr int kWProducer = kDq, kXProducer = kDq + 1, kMma = kDq + 2, kAux0 = kDq + 3;
+    static constexpr int kThreads = (kDq + 7) * 32;
+};
+
+template <bool kFold>
+__global__ void __launch_bounds__(MidRoles<kFold>::kThreads, kFold ? 1 : 2)
+    k_ctarq_mid(const __grid_constant__ MidParams P) {
     using C = MidCfg;
+    using R = MidRoles<kFold>;
     constexpr int SKB = C::SKB, AB = C::AB, CPB = C::kColsPerBlock;
     // folding: D (plain weights) at TMEM column 0, D' (folded) at 64, per block A then A' from 128
     constexpr uint32_t kTmemCols = kFold ? 512u : C::kTmemCols;
@@ -366,14 +373,14 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
     if (tid == 0) {
         for (int i = 0; i < WS; ++i) {
             mbar_init(&wfull[i], 1);
-            mbar_init(&wempty[i], C::kDqWarps);
+            mbar_init(&wempty[i], 4);  // the set of dequantising warps of that stage
         }
         for (int i = 0; i < XS; ++i) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xempty[i], 1 + 4);  // the MMA commit and the four auxiliary (folding: dequantising) warps
         }
         for (int i = 0; i < AB; ++i) {
-            mbar_init(&a_full[i], C::kDqWarps);
+            mbar_init(&a_full[i], 4);
             mbar_init(&a_empty[i], 1);
         }
         mbar_init(done, 1);
@@ -382,7 +389,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
         s_last = 0;
         s_fold = 0;
     }
-    if (warp == C::kMmaWarp) {
+    if (warp == R::kMma) {
         tmem_alloc(tmem_slot, kTmemCols);
         tmem_relinquish();
     }
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
     const uint32_t tmem = *tmem_slot;
 
     int wissued = 0, xissued = 0;
-    if (warp == C::kWProducerWarp) {
+    if (warp == R::kWProducer) {
         if (lane == 0) {
             // the weights do not depend on the previous kernels: no dependency wait
             const uint64_t pol = policy_evict_first();
@@ -410,7 +417,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
                 ++wissued;
             }
         }
-    } else if (warp == C::kXProducerWarp) {
+    } else if (warp == R::kXProducer) {
         pdl_wait();  // the tokens (and their routing) are the previous kernels' output
         // with a routed token, each stage also brings the blocks' dW segments (fold lists)
         const uint8_t* lists = kFold ? L.fold : L.dseg;
@@ -449,7 +456,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
                 ++xissued;
             }
         }
-    } else if (warp == C::kMmaWarp) {
+    } else if (warp == R::kMma) {
         const uint32_t idesc = idesc_f16_f32(128, Tp);
         bool ok = true;
         bool fo = false;  // folding: the routed tokens' products on A' as well
@@ -485,21 +492,22 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
         if (!ok && lane == 0) s_abort = 1;
         if (elect_one()) tc_commit(done);  // also after an abort, so that the TMEM can be released
         __syncwarp();
-    } else if (warp < C::kDqWarps) {
-        const uint32_t lane_addr = static_cast<uint32_t>(32 * warp) << 16;
+    } else if (warp < R::kDq) {
+        const int qw = warp & 3, set = warp >> 2;  // lane quadrant, stage set
+        const uint32_t lane_addr = static_cast<uint32_t>(32 * qw) << 16;
         bool fo = false;
-        for (int u = 0; u < nst; ++u) {
+        for (int u = set; u < nst; u += R::kSets) {
             const int ws = u % WS, b = u % AB, xs = u % XS;
             if (!mbar_wait(&wfull[ws], (u / WS) & 1, L.status)) {
                 s_abort = 1;
                 break;
             }
-            if (kFold && (u == 0 || fo)) {  // the stage's fold lists (and whether there are any) come with its tokens
+            if (kFold && (u == set || fo)) {  // the stage's fold lists (and whether there are any) come with its tokens
                 if (!mbar_wait(&xfull[xs], (u / XS) & 1, L.status)) {
                     s_abort = 1;
                     break;
                 }
-                if (u == 0) fo = s_fold != 0;
+                if (u == set) fo = s_fold != 0;
             }
             const int n = nkb - u * SKB < SKB ? nkb - u * SKB : SKB;
             uint4 wv[SKB][2];  // [block][tile 2w, 2w + 1]
@@ -509,7 +517,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
                 for (int q = 0; q < 2; ++q)
                     if (k < n)
                         wv[k][q] = *reinterpret_cast<const uint4*>(wring + ws * C::kWStage + k * 4096 +
-                                                                   (2 * warp + q) * 512 + lane * 16);
+                                                                   (2 * qw + q) * 512 + lane * 16);
             __syncwarp();
             if (lane == 0) mbar_arrive(&wempty[ws]);
             if (u >= AB && !mbar_wait(&a_empty[b], ((u / AB) - 1) & 1, L.status)) {
@@ -534,7 +542,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
                         if (kFold && fo) {
                             // A' = (q - 8) + dW/s: this lane's entries of 16-row tile 2 warp + q
                             const unsigned char* lst = dring + (xs * SKB + k) * dslot;
-                            const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + (2 * warp + q) * 33 + lane;
+                            const uint16_t* offs = reinterpret_cast<const uint16_t*>(lst) + (2 * qw + q) * 33 + lane;
                             const uint32_t* ent = reinterpret_cast<const uint32_t*>(lst + kFoldHdr);
                             const int e1 = offs[1];
                             for (int e = offs[0]; e < e1; ++e) {
@@ -646,7 +654,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
     }
 
     // ---- epilogue (auxiliary warps): y = acc * s + dW of routed tokens
-    if (warp >= C::kAuxWarp0) {
+    if (warp >= R::kAux0) {
         const int at = 32 * (warp & 3) + lane;
         const int64_t row = rt * 128 + at;
         const float* corr = corr_s + at * (T + 1);
@@ -690,15 +698,15 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
     __syncwarp();  // single-lane roles rejoin their warp before the warp-wide TMEM release below
     tc_fence_before();
     __syncthreads();
-    if (warp == C::kMmaWarp) {
+    if (warp == R::kMma) {
         if (s_abort) mbar_wait(done, 0, nullptr, kDrainNs);
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (s_abort && warp == C::kWProducerWarp && lane == 0)
+    if (s_abort && warp == R::kWProducer && lane == 0)
         for (int it = wissued > WS ? wissued - WS : 0; it < wissued; ++it)
             mbar_wait(&wfull[it % WS], (it / WS) & 1, nullptr, kDrainNs);
-    if (s_abort && warp == C::kXProducerWarp && lane == 0)
+    if (s_abort && warp == R::kXProducer && lane == 0)
         for (int it = xissued > XS ? xissued - XS : 0; it < xissued; ++it)
             mbar_wait(&xfull[it % XS], (it / XS) & 1, nullptr, kDrainNs);
     if (ks == 1) return;
@@ -716,7 +724,7 @@ __global__ void __launch_bounds__(MidCfg::kThreads, kFold ? 1 : 2) k_ctarq_mid(c
     // four splits at a time and added in split order
     const float* pr = L.partial + (rt * ks * T) * 128;
     const int items = T * 32;
-    for (int it2 = tid; it2 < items && !s_abort; it2 += C::kThreads) {
+    for (int it2 = tid; it2 < items && !s_abort; it2 += R::kThreads) {
         const int t = it2 >> 5, r4 = (it2 & 31) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int s0 = 0; s0 < ks; s0 += 4) {
@@ -985,7 +993,8 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e == cudaSuccess) flags[fold ? 1 : 0].fetch_or(bit);
     }
-    if (e == cudaSuccess) e = launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(MidCfg::kThreads), smem, s, P);
+    const int threads = fold ? MidRoles<true>::kThreads : MidRoles<false>::kThreads;
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(threads), smem, s, P);
     delete Pp;
     return e;
 }
