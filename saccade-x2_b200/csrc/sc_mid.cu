@@ -15,7 +15,7 @@
 //                    128-byte-swizzled K-major operand layout (rows past the last token and columns
 //                    past the last one zero-filled);
 //   4 warps          dequantise the weights into tensor memory (A), three stages deep (from 17 tokens
-//                    two sets of 4, taking alternate stages);
+//                    three sets of 4, taking the stages in turn);
 //   MMA warp         one elected lane issues 4 MMAs per 64-column block;
 //   4 aux warps      one thread per row: the row's dW entries of each staged block (op.rs:152-170,
 //                    CSR columns ascending) for the routed tokens, from the staged x; then the
@@ -307,11 +307,12 @@ __device__ __forceinline__ float staged_x(const unsigned char* blk, int t, int c
     return h2f(*reinterpret_cast<const uint16_t*>(blk + t * 128 + ((((c >> 3) ^ t) & 7) << 4) + (c & 7) * 2));
 }
 
-// Warps of the two variants: the folding one has two sets of 4 dequantising warps taking alternate
-// stages (one set's hand-off latency hides behind the other's work); roles follow the dequantisers.
+// Warps of the two variants: the folding one has three sets of 4 dequantising warps taking stages in
+// turn (a set's hand-off latency hides behind the others' work; three A buffers allow three stages in
+// flight); roles follow the dequantisers.
 template <bool kFold>
 struct MidRoles {
-    static constexpr int kDq = kFold ? 8 : 4;    // dequantising warps; warp w: TMEM lanes 32 (w % 4)
+    static constexpr int kDq = kFold ? 12 : 4;   // dequantising warps; warp w: TMEM lanes 32 (w % 4)
     static constexpr int kSets = kDq / 4;
     static constexpr int kWProducer = kDq, kXProducer = kDq + 1, kMma = kDq + 2, kAux0 = kDq + 3;
     static constexpr int kThreads = (kDq + 7) * 32;
@@ -561,8 +562,10 @@ __global__ void __launch_bounds__(MidRoles<kFold>::kThreads, kFold ? 1 : 2)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
+                // the stage's fold lists are read (or none were loaded): release the token slot before
+                // the MMA can run, so the slot's phase completes before another set reaches stage u + XS
+                if (kFold) mbar_arrive(&xempty[xs]);
                 mbar_arrive(&a_full[b]);
-                if (kFold) mbar_arrive(&xempty[xs]);  // its fold lists are read (or none were loaded)
             }
         }
     } else {
