@@ -9,9 +9,27 @@ made before capture), and completion counters that each call returns to zero.
 """
 from __future__ import annotations
 
+import contextlib
+import gc
 from typing import Callable, Optional
 
 import torch
+
+from .op import flush_deferred
+
+
+@contextlib.contextmanager
+def no_gc():
+    """Collects garbage, then keeps the collector off: a destructor that frees device memory must not
+    run inside a CUDA graph capture (it would invalidate the capture)."""
+    gc.collect()
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
 
 
 class CapturedStep:
@@ -24,10 +42,11 @@ class CapturedStep:
                 fn()  # sizes workspaces and sets kernel attributes outside the capture
         self.stream.synchronize()
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.device(self.device):
+        with torch.cuda.device(self.device), no_gc():
             with torch.cuda.graph(self.graph, stream=self.stream):
                 fn()
         self.stream.synchronize()
+        flush_deferred()
 
     def replay(self) -> None:
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):

@@ -92,6 +92,30 @@ class _Workspaces:
 
 WORKSPACES = _Workspaces()
 
+# Handles whose release (cudaFree inside the library) would fall into a CUDA graph capture: freeing
+# device memory while a stream captures invalidates the capture, and the garbage collector may run
+# a destructor at any point of the captured Python code.  They are released after the capture.
+_DEFERRED = []
+
+
+def release_handle(destroy, h) -> None:
+    try:
+        capturing = torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+    except Exception:  # noqa: BLE001 - interpreter shutdown
+        capturing = False
+    if capturing:
+        _DEFERRED.append((destroy, h))
+    else:
+        destroy(h)
+        flush_deferred()
+
+
+def flush_deferred() -> None:
+    """Releases the handles deferred during a capture (call outside of any capture)."""
+    while _DEFERRED:
+        destroy, h = _DEFERRED.pop()
+        destroy(h)
+
 
 def _u32(t: torch.Tensor) -> torch.Tensor:
     """Reinterpret a u32/i32/i64 index tensor as contiguous 32-bit words."""
@@ -201,7 +225,7 @@ class SaccadeLinearOp:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
-            LIB.sc_layer_destroy(h)
+            release_handle(LIB.sc_layer_destroy, h)
             self._h = None
 
     @property
@@ -372,7 +396,7 @@ class SaccadeLinearGroup:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and LIB is not None:
-            LIB.sc_group_destroy(h)
+            release_handle(LIB.sc_group_destroy, h)
             self._h = None
 
     def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16, outs=None,

@@ -37,7 +37,8 @@ import torch
 from . import _lib
 from ._lib import LIB, check
 from .compress import ProfileRunner, compress_tensor_to_saccade, compute_percentile_threshold
-from .op import SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDeltaMatrix
+from .graph import no_gc
+from .op import SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDeltaMatrix, flush_deferred
 
 PROJ = ("q", "k", "v", "o", "gate", "up", "down")
 
@@ -469,10 +470,11 @@ class GreedyDecoder:
         self.stream.synchronize()
         self.launches_per_step = int(LIB.sc_launch_count())
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=self.stream):
+        with no_gc(), torch.cuda.graph(self.graph, stream=self.stream):
             self._step()
         self.launches_per_step = int(LIB.sc_launch_count()) - self.launches_per_step
         self.stream.synchronize()
+        flush_deferred()
 
     def step(self, ids: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One decode step on the decoder's stream: ids [B] (device or pinned host; default: the
