@@ -124,6 +124,13 @@ constexpr int kAttnMaxG = 8;        // query heads per kv head
 constexpr int kAttnMaxHd = 128;
 constexpr int kAttnChunk = 32;      // keys staged in shared memory at a time (coalesced 16-byte loads)
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__ q, const float* __restrict__ kc,
                                                        const float* __restrict__ vc, const int32_t* __restrict__ slot,
                                                        const int32_t* __restrict__ pos, int nh, int nkv, int hd,
@@ -134,7 +141,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
     __shared__ float s_q[kAttnMaxG][kAttnMaxHd];
     __shared__ float s_p[kAttnMaxG][kAttnKeys];
     __shared__ float s_m[kAttnMaxG], s_l[kAttnMaxG];
-    __shared__ __align__(16) float s_kv[kAttnChunk * kAttnMaxHd];  // K or V rows [chunk][hd]
+    __shared__ __align__(16) float s_kv[2][kAttnChunk * kAttnMaxHd];  // K or V rows [chunk][hd], two buffers
     const int64_t t = blockIdx.x / (nkv * nblk);
     const int rem = blockIdx.x % (nkv * nblk);
     const int h = rem / nblk, kb = rem % nblk;
@@ -147,19 +154,33 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
     for (int i = tid; i < G * hd; i += kAttnThreads) s_q[i / hd][i % hd] = q[(t * nh + h * G + i / hd) * hd + i % hd];
     __syncthreads();
     const int nk = k1 > k0 ? k1 - k0 : 0;
-    // stages rows [c0, c0 + cn) of a K or V block into s_kv, 16 bytes per thread and load
-    auto stage = [&](const float* base, int c0, int cn) {
+    // issues the asynchronous copy of rows [c0, c0 + cn) of a K or V block into buffer `buf` (16 bytes
+    // per thread and copy); the next chunk streams in while the current one is used
+    auto issue = [&](const float* base, int c0, int buf) {
+        const int cn = min(kAttnChunk, nk - c0);
         const float4* src = reinterpret_cast<const float4*>(base + static_cast<int64_t>(k0 + c0) * hd);
-        float4* dst = reinterpret_cast<float4*>(s_kv);
-        for (int i = tid; i < cn * hd / 4; i += kAttnThreads) dst[i] = __ldg(src + i);
+        float4* dst = reinterpret_cast<float4*>(s_kv[buf]);
+        for (int i = tid; i < cn * hd / 4; i += kAttnThreads) cp_async16(dst + i, src + i);
+        cp_async_commit();
+    };
+    // waits for chunk c0's copy (buffer c0 / kAttnChunk & 1), issuing chunk c0 + kAttnChunk first
+    auto next = [&](const float* base, int c0) {
+        if (c0 + kAttnChunk < nk) {
+            issue(base, c0 + kAttnChunk, ((c0 / kAttnChunk) + 1) & 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
     };
     // scores: one warp per key, lanes over head_dim, a fixed shuffle tree
+    if (nk > 0) issue(kbase, 0, 0);
     for (int c0 = 0; c0 < nk; c0 += kAttnChunk) {
         const int cn = min(kAttnChunk, nk - c0);
-        stage(kbase, c0, cn);
-        __syncthreads();
+        next(kbase, c0);
+        const float* kvbuf = s_kv[(c0 / kAttnChunk) & 1];
         for (int j = warp; j < cn; j += kAttnThreads / 32) {
-            const float* kr = s_kv + j * hd;
+            const float* kr = kvbuf + j * hd;
             float kv[kAttnMaxHd / 32];
 #pragma unroll
             for (int e = 0; e < kAttnMaxHd / 32; ++e) kv[e] = (lane + 32 * e < hd) ? kr[lane + 32 * e] : 0.0f;
@@ -202,19 +223,20 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
         const int ngrp = kAttnThreads / hd;
         const int d = tid % hd, grp = tid / hd;
         float o[kAttnMaxG / 2] = {};
+        if (nk > 0) issue(vbase, 0, 0);
         for (int c0 = 0; c0 < nk; c0 += kAttnChunk) {
             const int cn = min(kAttnChunk, nk - c0);
-            __syncthreads();  // the previous chunk is read
-            stage(vbase, c0, cn);
-            __syncthreads();
+            next(vbase, c0);
+            const float* kvbuf = s_kv[(c0 / kAttnChunk) & 1];
             for (int j = 0; j < cn; ++j) {
-                const float vv = s_kv[j * hd + d];
+                const float vv = kvbuf[j * hd + d];
 #pragma unroll
                 for (int r = 0; r < kAttnMaxG / 2; ++r) {
                     const int g = grp + r * ngrp;
                     if (g < G) o[r] = __fadd_rn(o[r], __fmul_rn(s_p[g][c0 + j], vv));
                 }
             }
+            __syncthreads();  // this buffer is read before the next chunk but one is copied into it
         }
 #pragma unroll
         for (int r = 0; r < kAttnMaxG / 2; ++r) {
@@ -229,21 +251,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const float* __restrict__
 }
 
 // Rescales the key blocks of every (token, head) to their common max, adds them in block order and
-// writes out = o / l as f16 [T][nh * hd] (the o projection's input).  The factors exp(m_b - m) and
-// the sum l depend on the head only: one thread per head computes them first.
-constexpr int kCombineMaxHeads = 128;
+// writes out = o / l as f16 [T][nh * hd] (the o projection's input).  One CTA per token and 256
+// outputs; the factors exp(m_b - m) and the sum l depend on the head only, so the CTA's heads get
+// them first, one thread per head.
+constexpr int kCombineThreads = 256;
+constexpr int kCombineMaxHeads = 8;   // heads one CTA's 256 outputs span (head_dim >= 32)
 constexpr int kCombineMaxBlk = 32;
-__global__ void k_attn_combine(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                               const int32_t* __restrict__ pos, int nh, int nkv, int hd, int nblk,
-                               uint16_t* __restrict__ out) {
+__global__ void __launch_bounds__(kCombineThreads) k_attn_combine(const float* __restrict__ part_o,
+                                                                  const float* __restrict__ part_ml,
+                                                                  const int32_t* __restrict__ pos, int nh, int nkv,
+                                                                  int hd, int nblk, uint16_t* __restrict__ out) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float s_f[kCombineMaxHeads][kCombineMaxBlk];
     __shared__ float s_l[kCombineMaxHeads];
     const int64_t t = blockIdx.x;
+    const int i0 = blockIdx.y * kCombineThreads;
+    const int hq0 = i0 / hd, hq1 = min(nh, (i0 + kCombineThreads - 1) / hd + 1);
     const int G = nh / nkv;
     const int nb = (pos[t] + kAttnKeys) / kAttnKeys;  // blocks holding keys of this token
-    for (int hq = threadIdx.x; hq < nh; hq += blockDim.x) {
+    if (static_cast<int>(threadIdx.x) < hq1 - hq0) {
+        const int hq = hq0 + threadIdx.x;
         const int h = hq / G, g = hq % G;
         const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
         float m = -INFINITY;
@@ -251,20 +279,20 @@ __global__ void k_attn_combine(const float* __restrict__ part_o, const float* __
         float l = 0.0f;
         for (int b = 0; b < nb; ++b) {
             const float f = nb == 1 ? 1.0f : exp_f32(__fsub_rn(part_ml[((pb + b) * G + g) * 2], m));
-            s_f[hq][b] = f;
+            s_f[threadIdx.x][b] = f;
             l = __fadd_rn(l, __fmul_rn(part_ml[((pb + b) * G + g) * 2 + 1], f));
         }
-        s_l[hq] = l;
+        s_l[threadIdx.x] = l;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < nh * hd; i += blockDim.x) {
-        const int hq = i / hd, d = i % hd;
-        const int h = hq / G, g = hq % G;
-        const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
-        float o = 0.0f;
-        for (int b = 0; b < nb; ++b) o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], s_f[hq][b]));
-        out[t * nh * hd + i] = f32_to_f16_bits(__fdiv_rn(o, s_l[hq]));
-    }
+    const int i = i0 + threadIdx.x;
+    if (i >= nh * hd) return;
+    const int hq = i / hd, d = i % hd;
+    const int h = hq / G, g = hq % G;
+    const int64_t pb = (t * nkv + h) * static_cast<int64_t>(nblk);
+    float o = 0.0f;
+    for (int b = 0; b < nb; ++b) o = __fadd_rn(o, __fmul_rn(part_o[((pb + b) * G + g) * hd + d], s_f[hq - hq0][b]));
+    out[t * nh * hd + i] = f32_to_f16_bits(__fdiv_rn(o, s_l[hq - hq0]));
 }
 
 // ---------------------------------------------------------------- SiLU(gate) * up (model.rs:295-299)
@@ -348,7 +376,7 @@ sc_status sc_qwen2_attention(const float* q, const float* k_cache, const float* 
     if (tokens <= 0) return tokens == 0 ? SC_OK : SC_EINVAL;
     if (!q || !k_cache || !v_cache || !slot || !pos || !scratch || !out_f16 || num_kv_heads <= 0 ||
         num_heads % num_kv_heads || num_heads / num_kv_heads > kAttnMaxG || head_dim > kAttnMaxHd ||
-        kAttnThreads % head_dim != 0 || head_dim % 32 != 0 || num_heads > kCombineMaxHeads ||
+        kAttnThreads % head_dim != 0 || head_dim % 32 != 0 || num_heads > 128 ||
         max_query_pos >= max_pos || (max_query_pos + kAttnKeys) / kAttnKeys > kCombineMaxBlk)
         return SC_EINVAL;
     if (scratch_bytes < sc_qwen2_attention_scratch(tokens, num_heads, num_kv_heads, head_dim, max_pos))
@@ -366,7 +394,10 @@ sc_status sc_qwen2_attention(const float* q, const float* k_cache, const float* 
                                q, k_cache, v_cache, slot, pos, num_heads, num_kv_heads, head_dim, max_pos, scale, nblk,
                                part_o, part_ml);
     if (e == cudaSuccess)
-        e = launch_pdl(k_attn_combine, dim3(static_cast<unsigned>(tokens)), dim3(256), 0, s, part_o, part_ml, pos,
+        e = launch_pdl(k_attn_combine,
+                       dim3(static_cast<unsigned>(tokens),
+                            static_cast<unsigned>((num_heads * head_dim + kCombineThreads - 1) / kCombineThreads)),
+                       dim3(kCombineThreads), 0, s, part_o, part_ml, pos,
                        num_heads, num_kv_heads, head_dim, nblk, out_f16);
     return e == cudaSuccess ? SC_OK : cuda_fail(e, "sc_qwen2_attention");
 }
