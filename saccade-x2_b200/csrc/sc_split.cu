@@ -37,53 +37,49 @@ __global__ void __launch_bounds__(256) k_split_transpose(const void* __restrict_
     }
 }
 
-// y_delta[t][r] for 64 rows and 16 tokens per CTA: thread r walks row r's entries in column order, 8 at a
-// time (their columns, values and the 16 tokens' values of each column loaded before any is used).
-constexpr int kDeltaRows = 64;
-__global__ void __launch_bounds__(kDeltaRows) k_split_delta(const uint16_t* __restrict__ xt, int64_t Tp, int64_t m,
-                                                            const uint32_t* __restrict__ rowptr,
-                                                            const uint16_t* __restrict__ col,
-                                                            const int8_t* __restrict__ val, float ds, int64_t N,
-                                                            float* __restrict__ y_delta) {
+// y_delta[t][r] for 8 rows (one warp each) and 16 tokens per CTA.  A row's dW entries are spread over
+// its warp's lanes (lane l takes entries l, l + 32, ...: coalesced column and value loads, and rows
+// whose counts differ widely -- a percentile threshold keeps the largest errors, which gather in
+// the rows with large scales -- cost their own length / 32, not the longest row's length); each lane
+// reads the 16 tokens' values of an entry's column from xt with two 16-byte loads, and the lanes'
+// sums meet in a fixed xor butterfly (deterministic).
+constexpr int kDeltaRowsPerCta = 8;
+__global__ void __launch_bounds__(32 * kDeltaRowsPerCta) k_split_delta(const uint16_t* __restrict__ xt, int64_t Tp,
+                                                                       int64_t m, const uint32_t* __restrict__ rowptr,
+                                                                       const uint16_t* __restrict__ col,
+                                                                       const int8_t* __restrict__ val, float ds,
+                                                                       int64_t N, float* __restrict__ y_delta) {
     pdl_launch_dependents();
     pdl_wait();
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kDeltaRows + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kDeltaRowsPerCta + (threadIdx.x >> 5);
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * 16;
-    if (row >= N) return;
+    if (row >= N) return;  // the whole warp
     float acc[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[j] = 0.0f;
     const int64_t e1 = rowptr[row + 1];
-    for (int64_t e = rowptr[row]; e < e1; e += 8) {
-        int64_t c[8];
-        float v[8];
+    for (int64_t e = rowptr[row] + lane; e < e1; e += 32) {
+        const int64_t c = col[e];
+        const float v = __fmul_rn(static_cast<float>(val[e]), ds);
+        const uint4* p = reinterpret_cast<const uint4*>(xt + c * Tp + t0);
+        const uint4 a = __ldg(p), b = __ldg(p + 1);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const bool ok = e + i < e1;
-            c[i] = ok ? static_cast<int64_t>(col[e + i]) : 0;
-            v[i] = ok ? __fmul_rn(static_cast<float>(val[e + i]), ds) : 0.0f;
-        }
-        uint4 xa[8], xb[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint4* p = reinterpret_cast<const uint4*>(xt + c[i] * Tp + t0);
-            xa[i] = __ldg(p);
-            xb[i] = __ldg(p + 1);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (e + i >= e1) break;
-            const uint32_t w[8] = {xa[i].x, xa[i].y, xa[i].z, xa[i].w, xb[i].x, xb[i].y, xb[i].z, xb[i].w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(h2f(static_cast<uint16_t>(w[j] & 0xFFFFu)), v[i]));
-                acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(h2f(static_cast<uint16_t>(w[j] >> 16)), v[i]));
-            }
+        for (int j = 0; j < 8; ++j) {
+            acc[2 * j] = __fadd_rn(acc[2 * j], __fmul_rn(h2f(static_cast<uint16_t>(w[j] & 0xFFFFu)), v));
+            acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], __fmul_rn(h2f(static_cast<uint16_t>(w[j] >> 16)), v));
         }
     }
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-        if (t0 + j < m) y_delta[(t0 + j) * N + row] = acc[j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[j] = __fadd_rn(acc[j], __shfl_xor_sync(0xffffffffu, acc[j], o));
+    float out = acc[0];
+#pragma unroll
+    for (int j = 1; j < 16; ++j)
+        if (lane == j) out = acc[j];
+    if (lane < 16 && t0 + lane < m) y_delta[(t0 + lane) * N + row] = out;
 }
 
 // The slice's router sums of each token (one CTA per token), in f64.
@@ -161,8 +157,10 @@ cudaError_t launch_split_extras(const Layer& L, const void* x, int x_dtype, int6
         e = launch_pdl(k_split_transpose, dim3(static_cast<unsigned>((L.K + 31) / 32), static_cast<unsigned>((Tp + 31) / 32)),
                        dim3(256), 0, s, x, x_dtype, m, L.K, Tp, xt);
         if (e == cudaSuccess) {
-            const dim3 grid(static_cast<unsigned>((L.N + kDeltaRows - 1) / kDeltaRows), static_cast<unsigned>(Tp / 16));
-            e = launch_pdl(k_split_delta, grid, dim3(kDeltaRows), 0, s, static_cast<const uint16_t*>(xt), Tp, m, L.rowptr,
+            const dim3 grid(static_cast<unsigned>((L.N + kDeltaRowsPerCta - 1) / kDeltaRowsPerCta),
+                            static_cast<unsigned>(Tp / 16));
+            e = launch_pdl(k_split_delta, grid, dim3(32 * kDeltaRowsPerCta), 0, s, static_cast<const uint16_t*>(xt), Tp,
+                           m, L.rowptr,
                            L.col, L.val, L.ds, L.N, y_delta);
         }
     } else {
