@@ -6,7 +6,7 @@ seeded sample of output rows (fast tolerance), with the oracle's routing mask an
 token; each buffer's router sums must equal f64 sums of the slice.
 
 Shapes: Qwen2-7B down (3584 x 18944, intermediate split over 2 or 8 ranks) and o (3584 x 3584,
-28 heads of 128 split 4,4,4,4,3,3,3,3 as at 8 ranks), M from 1 (router-fused decode) over 4, 16
+28 heads of 128 split unevenly over 8 ranks, 4,4,4,4,3,3,3,3), M from 1 (router-fused decode) over 4, 16
 (the 9..16-token GEMM) to 64 and 200 (the prefill GEMM), f16 and bf16 inputs, bypass.
 """
 import numpy as np
