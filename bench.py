@@ -71,6 +71,8 @@ def parse(argv=None):
     ap.add_argument("--mode", default="fast", choices=["fast", "fast_tc", "fast_tc8", "exact"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fused-route", default="none", choices=["none", "norm", "all"],
+                    help="decode: routers fused into the RMSNorm kernels (norm), also into SiLU * up (all)")
     ap.add_argument("--no-group", action="store_true",
                     help="one launch per projection, the reference's calling pattern (no grouped q/k/v, gate/up)")
     ap.add_argument("--sweep", metavar="PATH",
@@ -546,7 +548,7 @@ def decode_config(args, world):
             "layers": args.layers, "global_batch": args.batch, "prompt_tokens": args.prompt,
             "decode_steps": args.decode_steps, "dw_fill": args.fill,
             "thresholds": "per projection at the 75th / 95th percentile of a 512-token calibration prompt",
-            "parallelism": f"tp{world}" if world > 1 else "tp1"}
+            "parallelism": f"tp{world}" if world > 1 else "tp1", "fused_route": args.fused_route}
 
 
 def decode_step_bytes(cfg, model, batch, pos):
@@ -585,7 +587,7 @@ def build_decode(args, rank, world, dev, group):
     need = 1 + 2 * (args.warmup + args.steps) + 3
     max_pos = args.prompt + max(args.decode_steps, need)
     model = Q.Qwen2Model(ck, dev, max_batch=args.batch, max_pos=max_pos, mode=args.mode,
-                         tp=(rank, world, group) if world > 1 else None)
+                         tp=(rank, world, group) if world > 1 else None, fused_route=args.fused_route)
     # reference-format buffers of the last layer's gate and up for the parity check, then free the rest
     last = {n: {k: v.cpu() for k, v in ck.blocks[-1][n].items()} for n in ("gate", "up")}
     last_thr = {n: ck.thresholds[-1][n] for n in ("gate", "up")}

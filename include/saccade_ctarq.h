@@ -188,6 +188,18 @@ SC_API sc_status sc_forward_group(const sc_group* group, const void* x, int x_dt
                                   int32_t* const* n_routed_out, void* workspace, size_t workspace_bytes,
                                   void* stream);
 
+/* sc_forward_group with the routing already computed for x (by sc_qwen2_add_rmsnorm_route or
+ * sc_qwen2_silu_mul_route, which wrote x): mask, routed_idx and n_routed are INPUTS, one array
+ * per layer as those kernels wrote them.  Only where the group runs the 9..64-token launch for m
+ * tokens with this workspace (sc_group_takes_routing == 1; a group of one layer counts); x is f16,
+ * 16-byte aligned, [m, in_features].  Outputs equal sc_forward_group's on the same x, bit for bit.
+ * No reference counterpart (the reference routes inside each projection, op.rs:64-73). */
+SC_API int sc_group_takes_routing(const sc_group* group, int64_t m, size_t workspace_bytes);
+SC_API sc_status sc_forward_group_routed(const sc_group* group, const uint16_t* x, int64_t m, void* const* y,
+                                         int y_dtype, const float* const* bias, const uint8_t* const* mask,
+                                         const int32_t* const* routed_idx, const int32_t* const* n_routed,
+                                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* sc_forward_static has no counterpart in the reference.  It is sc_forward without any
  * allocation: its scratch is a file-scope __device__ array of SC_STATIC_SCRATCH_BYTES inside
  * this library, one per device, placed when the library's device code is loaded.  It serves

@@ -7,6 +7,10 @@
  *   sc_qwen2_rope_append   <- RotaryEmbedding::apply + the KV-cache concat  model.rs:111-154, 225-236
  *   sc_qwen2_attention     <- scores, softmax, attn . v (GQA)  model.rs:238-257
  *   sc_qwen2_silu_mul      <- Mlp::forward's silu(gate) * up    model.rs:295-299
+ *   sc_qwen2_add_rmsnorm_route, sc_qwen2_silu_mul_route
+ *                          <- the two above with the next linears' router (op.rs:64-73,
+ *                             heuristics.rs:3-14) in their epilogue, consumed by
+ *                             sc_forward_group_routed
  *   sc_qwen2_f16_to_f32    <- ProjectionLayer::forward's to_dtype back to f32  model.rs:61
  *
  * The linears themselves are sc_forward / sc_forward_group calls (saccade_ctarq.h).  Everything is
@@ -63,6 +67,29 @@ SC_API sc_status sc_qwen2_silu_mul(const uint16_t* gate, const uint16_t* up, int
                                    void* stream);
 
 /* out[i] = f32(x[i]) for f16 x. */
+/* The router of the linears that read the output, fused into the kernel that writes it.  Each
+ * kernel is one CTA per token: it writes the token's f16 row exactly as the plain kernel does
+ * (same bits), keeps it in shared memory, and routes the token for every layer of `group`
+ * (heuristics.rs:3-14, op.rs:64-73: f64 sums decide when the thresholds lie outside the f32 error
+ * band, else the reference's f32 chains are replayed), writing mask[l][t] (0/1); the last CTA to
+ * finish writes the ascending routed list routed_idx[l][0..n) and n_routed[l][0] of each layer.
+ * These are the routing sc_forward_group would compute on the same row, and sc_forward_group_routed
+ * takes them instead of routing again.  `counter` is one uint32 in device memory that is zero
+ * before the call (the kernel leaves it zero).  The group's layers must read the whole row:
+ * in_features == hidden (norm) or width (silu); set_bypass_c_tarq routes every token.
+ * add_rmsnorm_route: resid += delta (nullable), out_f16 = f16 RMSNorm as sc_qwen2_add_rmsnorm
+ * (hidden <= 16384).  silu_mul_route: out_f16 [tokens, width] = f16(silu(gate) * up) as
+ * sc_qwen2_silu_mul (width a multiple of 8, width <= 65536).  No reference counterpart: the
+ * reference routes inside each projection (op.rs:64-73). */
+SC_API sc_status sc_qwen2_add_rmsnorm_route(float* resid, const float* delta, const float* weight, int64_t tokens,
+                                            int64_t hidden, float eps, uint16_t* out_f16, const sc_group* group,
+                                            uint8_t* const* mask, int32_t* const* routed_idx,
+                                            int32_t* const* n_routed, uint32_t* counter, void* stream);
+SC_API sc_status sc_qwen2_silu_mul_route(const uint16_t* gate, const uint16_t* up, int64_t tokens, int64_t width,
+                                         uint16_t* out_f16, const sc_group* group, uint8_t* const* mask,
+                                         int32_t* const* routed_idx, int32_t* const* n_routed, uint32_t* counter,
+                                         void* stream);
+
 SC_API sc_status sc_qwen2_f16_to_f32(const uint16_t* x, int64_t n, float* out, void* stream);
 
 #ifdef __cplusplus

@@ -1055,11 +1055,12 @@ struct MidGroupPlan {
     size_t xconv = 0, mask = 0, ridx = 0, nrouted = 0, partial = 0, total = 0;
 };
 
-static MidGroupPlan plan_mid_group(const sc_group* g, int64_t m) {
+// single: a group of one layer plans too (sc_forward_group runs a lone layer through sc_forward_ws)
+static MidGroupPlan plan_mid_group(const sc_group* g, int64_t m, bool single = false) {
     MidGroupPlan p;
     const int n = static_cast<int>(g->layers.size());
     const Layer& L0 = g->layers[0]->L;
-    bool ok = n > 1;
+    bool ok = n > 1 || (single && n == 1);
     for (int i = 0; i < n && ok; ++i) ok = use_mid(g->layers[i]->L, m);
     if (!ok) return p;
     for (int i = 0; i < n; ++i) p.rt += g->layers[i]->L.Np / 128;
@@ -1081,13 +1082,106 @@ static MidGroupPlan plan_mid_group(const sc_group* g, int64_t m) {
     return p;
 }
 
+// The 9..64-token launch of a group (plan mp): the routing into the caller's arrays where given,
+// else into the workspace; routed_in: the caller's arrays hold the routing already.
+static sc_status forward_group_mid(const sc_group* group, const MidGroupPlan& mp, const void* x, int x_dtype,
+                                   int64_t m, void* const* y, int y_dtype, const float* const* bias,
+                                   uint8_t* const* mask, int32_t* const* ridx, int32_t* const* nrouted, bool routed_in,
+                                   void* workspace, cudaStream_t s, const char* who) {
+    const int n = static_cast<int>(group->layers.size());
+    unsigned char* base = static_cast<unsigned char*>(workspace);
+    MidArgs a = {};
+    a.n = n;
+    for (int i = 0; i < n; ++i) {
+        if (!y[i]) {
+            set_error(std::string(who) + ": null output " + std::to_string(i));
+            return SC_EINVAL;
+        }
+        a.layer[i] = &group->layers[i]->L;
+        a.mask[i] = (mask && mask[i]) ? mask[i] : base + mp.mask + i * ceil_to(m, 16);
+        a.ridx[i] = (ridx && ridx[i]) ? ridx[i] : reinterpret_cast<int32_t*>(base + mp.ridx) + i * m;
+        a.nrouted[i] = (nrouted && nrouted[i]) ? nrouted[i] : reinterpret_cast<int32_t*>(base + mp.nrouted) + i * 4;
+        a.y[i] = y[i];
+        a.bias[i] = bias ? bias[i] : nullptr;
+    }
+    a.x = x;
+    a.x_dtype = x_dtype;
+    a.x_stride = group->layers[0]->L.K;
+    a.x_col0 = 0;
+    a.m = m;
+    a.route_all = g_bypass.load() != 0 ? 1 : 0;
+    a.routed_in = routed_in ? 1 : 0;
+    a.ks = mp.ks;
+    a.xconv = reinterpret_cast<uint16_t*>(base + mp.xconv);
+    a.y_dtype = y_dtype;
+    a.partial_out = 0;
+    a.partial = reinterpret_cast<float*>(base + mp.partial);
+    a.counter = reinterpret_cast<uint32_t*>(base);
+    a.rtcount = reinterpret_cast<uint32_t*>(base + 256);
+    const cudaError_t e = launch_mid(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, (std::string(who) + ": 9..64-token GEMM launch").c_str());
+    return SC_OK;
+}
+
+namespace sc {
+int group_layers(const sc_group* g, const Layer** out) {
+    const int n = std::min(static_cast<int>(g->layers.size()), SC_GROUP_MAX);
+    for (int i = 0; i < n; ++i) out[i] = &g->layers[i]->L;
+    return n;
+}
+
+int bypass_on() { return g_bypass.load() != 0 ? 1 : 0; }
+}  // namespace sc
+
 extern "C" {
+
+int sc_group_takes_routing(const sc_group* group, int64_t m, size_t workspace_bytes) {
+    if (!group || m <= 0) return 0;
+    const MidGroupPlan mp = plan_mid_group(group, m, true);
+    return (mp.use && workspace_bytes >= mp.total) ? 1 : 0;
+}
+
+sc_status sc_forward_group_routed(const sc_group* group, const uint16_t* x, int64_t m, void* const* y, int y_dtype,
+                                  const float* const* bias, const uint8_t* const* mask,
+                                  const int32_t* const* routed_idx, const int32_t* const* n_routed, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (!group || !y || !x || !mask || !routed_idx || !n_routed) {
+        set_error("sc_forward_group_routed: null group, x, output or routing array");
+        return SC_EINVAL;
+    }
+    const int n = static_cast<int>(group->layers.size());
+    for (int i = 0; i < n; ++i) {
+        if (!mask[i] || !routed_idx[i] || !n_routed[i]) {
+            set_error("sc_forward_group_routed: null routing of layer " + std::to_string(i));
+            return SC_EINVAL;
+        }
+    }
+    if (y_dtype != SC_F16 && y_dtype != SC_BF16 && y_dtype != SC_F32) {
+        set_error("sc_forward_group_routed: y dtype must be F16, BF16 or F32");
+        return SC_EINVAL;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0) {
+        set_error("sc_forward_group_routed: x must be 16-byte aligned");
+        return SC_EINVAL;
+    }
+    const MidGroupPlan mp = plan_mid_group(group, m, true);
+    if (!mp.use || !workspace || workspace_bytes < mp.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+        set_error("sc_forward_group_routed: the group does not run the 9..64-token launch for this call "
+                  "(sc_group_takes_routing), or the workspace is too small or not 256-byte aligned");
+        return SC_EINVAL;
+    }
+    DeviceGuard guard(group->layers[0]->L.device);
+    if (!guard.ok) return cuda_fail(cudaErrorInvalidDevice, "sc_forward_group_routed: set device");
+    return forward_group_mid(group, mp, x, SC_F16, m, y, y_dtype, bias, const_cast<uint8_t* const*>(mask),
+                             const_cast<int32_t* const*>(routed_idx), const_cast<int32_t* const*>(n_routed), true,
+                             workspace, static_cast<cudaStream_t>(stream), "sc_forward_group_routed");
+}
 
 size_t sc_group_workspace_size(const sc_group* group, int64_t m) {
     if (!group || m < 0) return 0;
     size_t need = 0;
     for (const sc_layer* l : group->layers) need = std::max(need, plan_workspace(l->L, m).total);
-    const MidGroupPlan p = plan_mid_group(group, m);
+    const MidGroupPlan p = plan_mid_group(group, m, true);
     if (p.use) need = std::max(need, p.total);
     return need;
 }
@@ -1167,39 +1261,8 @@ sc_status sc_forward_group(const sc_group* group, const void* x, int x_dtype, in
             set_error("sc_forward_group: bad x / y dtype or null x");
             return SC_EINVAL;
         }
-        unsigned char* base = static_cast<unsigned char*>(workspace);
-        MidArgs a = {};
-        a.n = n;
-        for (int i = 0; i < n; ++i) {
-            if (!y[i]) {
-                set_error("sc_forward_group: null output " + std::to_string(i));
-                return SC_EINVAL;
-            }
-            a.layer[i] = &group->layers[i]->L;
-            a.mask[i] = (mask_out && mask_out[i]) ? mask_out[i] : base + mp.mask + i * ceil_to(m, 16);
-            a.ridx[i] = (routed_idx_out && routed_idx_out[i]) ? routed_idx_out[i]
-                                                              : reinterpret_cast<int32_t*>(base + mp.ridx) + i * m;
-            a.nrouted[i] = (n_routed_out && n_routed_out[i]) ? n_routed_out[i]
-                                                             : reinterpret_cast<int32_t*>(base + mp.nrouted) + i * 4;
-            a.y[i] = y[i];
-            a.bias[i] = bias ? bias[i] : nullptr;
-        }
-        a.x = x;
-        a.x_dtype = x_dtype;
-        a.x_stride = L0.K;
-        a.x_col0 = 0;
-        a.m = m;
-        a.route_all = g_bypass.load() != 0 ? 1 : 0;
-        a.ks = mp.ks;
-        a.xconv = reinterpret_cast<uint16_t*>(base + mp.xconv);
-        a.y_dtype = y_dtype;
-        a.partial_out = 0;
-        a.partial = reinterpret_cast<float*>(base + mp.partial);
-        a.counter = reinterpret_cast<uint32_t*>(base);
-        a.rtcount = reinterpret_cast<uint32_t*>(base + 256);
-        const cudaError_t e = launch_mid(a, s);
-        if (e != cudaSuccess) return cuda_fail(e, "grouped 9..64-token GEMM launch");
-        return SC_OK;
+        return forward_group_mid(group, mp, x, x_dtype, m, y, y_dtype, bias, mask_out, routed_idx_out, n_routed_out,
+                                 false, workspace, s, "sc_forward_group");
     }
     // prefill GEMM regime: layers reading the same x with the same thresholds share one router and
     // one token gather (their masks are the same); the others reuse what the first left in the workspace

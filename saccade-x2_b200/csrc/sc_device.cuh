@@ -637,10 +637,9 @@ __device__ __forceinline__ void fold_add(uint32_t (&h)[4][4], int slot, int hi, 
 constexpr int kReplayItems = 4;
 constexpr int kReplayMaxThreads = 256;
 struct ReplayShared {
-    // {0 | end parity after an even start << 1 | after an odd start << 2, B, R even, R odd} or {1, i0, i1, 0}
-    int4 item[kReplayMaxThreads][kReplayItems];
+    // items: {0 | end parity after an even start << 1 | after an odd start << 2, B, R even, R odd}
+    // or {1, i0, i1, 0}
     int4 flat[kReplayMaxThreads * kReplayItems];  // the items of all threads in order
-    int count[kReplayMaxThreads];
     double w2[kReplayMaxThreads / 32];
     long long w1[kReplayMaxThreads / 32];
     double wabs[kReplayMaxThreads / 32];
@@ -661,6 +660,16 @@ static __device__ __noinline__ float exact_variance_row(const uint16_t* row, int
     const float mean = __fdiv_rn(sum, hd);
     return __fsub_rn(__fdiv_rn(sq, hd), __fmul_rn(mean, mean));
 }
+
+// A thread's items, in registers until their place in the flat list is known (static indices only).
+struct ReplayItems {
+    int4 v[kReplayItems];
+    __device__ __forceinline__ void put(int n, int4 x) {
+#pragma unroll
+        for (int j = 0; j < kReplayItems; ++j)
+            if (j == n) v[j] = x;
+    }
+};
 
 // `row`: the token's K values as f16 bits, in shared memory (read many times).
 template <int kThreads>
@@ -713,6 +722,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         tot1 += sh.w1[w];
     }
     double absP1 = 0.0;
+    ReplayItems its;
     int n_it = 0, kind = -1, curB = 0, par0 = 0, par1 = 1;
     float R0 = 0.0f, R1 = 0.0f;
     int64_t seq0 = 0, seq1 = 0;
@@ -741,9 +751,9 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         if (certain) {
             if (!(kind == 0 && curB == B)) {
                 if (kind == 0) {
-                    sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
+                    its.put(n_it++, make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1)));
                 } else if (kind == 1) {
-                    sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(seq1), 0);
+                    its.put(n_it++, make_int4(1, static_cast<int>(seq0), static_cast<int>(seq1), 0));
                 }
                 if (n_it == kReplayItems - 1) {  // the rest of the chunk as one range
                     tail = true;
@@ -769,7 +779,7 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
             par1 = (par1 + static_cast<int>(r1)) & 1;
         } else {
             if (kind != 1) {
-                if (kind == 0) sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
+                if (kind == 0) its.put(n_it++, make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1)));
                 if (n_it == kReplayItems - 1) tail = true;
                 kind = 1;
                 seq0 = i;
@@ -778,9 +788,9 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         }
     }
     if (kind == 0) {
-        sh.item[tid][n_it++] = make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1));
+        its.put(n_it++, make_int4((par0 << 1) | (par1 << 2), curB, __float_as_int(R0), __float_as_int(R1)));
     } else if (kind == 1) {
-        sh.item[tid][n_it++] = make_int4(1, static_cast<int>(seq0), static_cast<int>(tail ? i1 : seq1), 0);
+        its.put(n_it++, make_int4(1, static_cast<int>(seq0), static_cast<int>(tail ? i1 : seq1), 0));
     }
     // the items in chunk order: an exclusive scan of the counts places each thread's items
     int cs = n_it;
@@ -799,7 +809,9 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         if (w < warp) at += sh.wcnt[w];
         total += sh.wcnt[w];
     }
-    for (int j = 0; j < n_it; ++j) sh.flat[at + j] = sh.item[tid][j];
+#pragma unroll
+    for (int j = 0; j < kReplayItems; ++j)
+        if (j < n_it) sh.flat[at + j] = its.v[j];
     if (lane == 0) sh.wstart[warp] = at;
     __syncthreads();
     // each warp's lane 0 composes consecutive runs of one binade (the parity after a run is a function
@@ -859,6 +871,122 @@ __device__ void replay_score(const uint16_t* row, int64_t K, ReplayShared& sh) {
         sh.hi = __fsub_rn(qd, mmin);
     }
     __syncthreads();
+}
+
+// ---------------------------------------------------------------- routing one token for a group
+//
+// The per-token router of 1..SC_GROUP_MAX layers that read the same token (heuristics.rs:3-14,
+// op.rs:64-73), run by the CTA that holds the token: every decision the f64 sums settle
+// (route_band), the CTA-parallel replay for the others, the mask byte per layer; the last CTA of
+// the grid to finish compacts every layer's mask into its ascending routed list and count.
+struct TokenRoute {
+    int M;                            // tokens of the call (one CTA each)
+    int nl;                           // layers routed (0..SC_GROUP_MAX)
+    float t4[SC_GROUP_MAX], t8[SC_GROUP_MAX];
+    int route_all;                    // bypass: every token routed
+    RouteConsts rc;                   // of the token's length
+    uint8_t* mask[SC_GROUP_MAX];
+    int32_t* ridx[SC_GROUP_MAX];
+    int32_t* nrouted[SC_GROUP_MAX];
+    uint32_t* counter;                // completion counter, zero between calls (the last CTA resets it)
+};
+
+// Token t of the call, its K values as f16 bits in shared memory `row` (written by this CTA before
+// the call; the first barrier here publishes them); s1, s2, sa: this thread's f64 partial sums of
+// x, x^2, |x| over the values it wrote.  Every thread of the CTA calls it.
+template <int kThreads>
+__device__ void route_row(const TokenRoute& a, int t, const uint16_t* row, int64_t K, double s1, double s2, double sa) {
+    constexpr int kWarps = kThreads / 32;
+    __shared__ double red[3][kWarps];
+    __shared__ int s_last;
+    __shared__ int s_wsum[kWarps];
+    __shared__ int s_open;
+    __shared__ ReplayShared s_replay;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s1 += __shfl_down_sync(0xffffffffu, s1, o);
+        s2 += __shfl_down_sync(0xffffffffu, s2, o);
+        sa += __shfl_down_sync(0xffffffffu, sa, o);
+    }
+    if (lane == 0) {
+        red[0][warp] = s1;
+        red[1][warp] = s2;
+        red[2][warp] = sa;
+    }
+    __syncthreads();
+    double S1 = 0.0, S2 = 0.0, SA = 0.0;
+    if (tid == 0) {
+        for (int w = 0; w < kWarps; ++w) {
+            S1 += red[0][w];
+            S2 += red[1][w];
+            SA += red[2][w];
+        }
+        int open = 0;
+        for (int l = 0; l < a.nl; ++l) {
+            double var;
+            const int d = a.route_all ? 1 : route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var);
+            if (d >= 0) {
+                a.mask[l][t] = static_cast<uint8_t>(d);
+            } else {
+                open = 1;
+            }
+        }
+        s_open = open;
+    }
+    __syncthreads();
+    if (s_open) {
+        // some layer's threshold is inside the f32 error band: the CTA replays the reference's chains
+        // once for the token, then every open decision is taken on that score
+        replay_score<kThreads>(row, K, s_replay);
+        if (tid == 0) {
+            bool have_exact = false;
+            float exact = 0.0f;
+            for (int l = 0; l < a.nl; ++l) {
+                double var;
+                if (route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var) >= 0) continue;
+                const bool rl = route_rule_f32(s_replay.lo, a.t4[l], a.t8[l]);
+                const bool rh = route_rule_f32(s_replay.hi, a.t4[l], a.t8[l]);
+                bool routed = rl;
+                if (rl != rh || !(s_replay.lo == s_replay.lo)) {
+                    if (!have_exact) exact = exact_variance_row(row, K);
+                    have_exact = true;
+                    routed = route_rule_f32(exact, a.t4[l], a.t8[l]);
+                }
+                a.mask[l][t] = routed ? 1 : 0;
+            }
+        }
+    }
+    // completion count; the last CTA compacts every layer's mask
+    if (tid == 0) {
+        __threadfence();
+        const unsigned ticket = atomicAdd(a.counter, 1u);
+        s_last = (ticket == static_cast<unsigned>(a.M) - 1u) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int l = 0; l < a.nl; ++l) {
+        int base = 0;
+        for (int t0 = 0; t0 < a.M; t0 += kThreads) {
+            const int tt = t0 + tid;
+            const int v = (tt < a.M) ? (reinterpret_cast<volatile uint8_t*>(a.mask[l])[tt] != 0) : 0;
+            const unsigned bal = __ballot_sync(0xffffffffu, v);
+            if (lane == 0) s_wsum[warp] = __popc(bal);
+            __syncthreads();
+            int pre = 0, tot = 0;
+            for (int w = 0; w < kWarps; ++w) {
+                if (w < warp) pre += s_wsum[w];
+                tot += s_wsum[w];
+            }
+            pre += __popc(bal & ((1u << lane) - 1u));
+            if (v) a.ridx[l][base + pre] = tt;
+            base += tot;
+            __syncthreads();
+        }
+        if (tid == 0) *a.nrouted[l] = base;
+    }
+    if (tid == 0) *a.counter = 0u;
 }
 
 }  // namespace sc

@@ -276,6 +276,10 @@ struct MidArgs {
     uint32_t* rtcount;                      // [sum RT] counters (zero between calls)
 };
 int mid_ksplit(int64_t rt_total, int64_t kb, int sms, int64_t m);
+// The layers of a group (at most SC_GROUP_MAX into `out`; returns how many) and whether
+// set_bypass_c_tarq is on: what a router outside the library's own launches needs (sc_model.cu).
+int group_layers(const sc_group* g, const Layer** out);
+int bypass_on();
 bool use_mid(const Layer& L, int64_t m);
 cudaError_t launch_mid(const MidArgs& a, cudaStream_t s);
 

@@ -43,16 +43,8 @@ struct MidRouteParams {
     int x_dtype;
     int vec_ok;
     int64_t x_stride;                 // elements per token (the router's length)
-    int M;
-    int nl;                           // layers routed (1..SC_GROUP_MAX)
-    float t4[SC_GROUP_MAX], t8[SC_GROUP_MAX];
-    int route_all;
-    RouteConsts rc;
     uint16_t* xcopy;                  // nullable: f16 copy of the tokens [M][x_stride]
-    uint8_t* mask[SC_GROUP_MAX];
-    int32_t* ridx[SC_GROUP_MAX];
-    int32_t* nrouted[SC_GROUP_MAX];
-    uint32_t* counter;                // completion counter, zero between calls
+    TokenRoute r;
 };
 
 __device__ __forceinline__ void load_f16x8(const void* x, int x_dtype, bool vec, int64_t base, uint16_t (&h)[8]) {
@@ -80,15 +72,9 @@ __device__ __forceinline__ void load_f16x8(const void* x, int x_dtype, bool vec,
 
 template <int kThreads>
 __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
-    constexpr int kWarps = kThreads / 32;
-    __shared__ double red[3][kWarps];
-    __shared__ int s_last;
-    __shared__ int s_wsum[kWarps];
-    __shared__ int s_open;
-    __shared__ ReplayShared s_replay;
     extern __shared__ __align__(16) uint16_t s_row[];  // the token as f16 bits [x_stride]
     const int t = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     pdl_launch_dependents();
     pdl_wait();
     const int64_t row_off = static_cast<int64_t>(t) * a.x_stride;
@@ -106,96 +92,7 @@ __global__ void __launch_bounds__(kThreads) k_mid_route(MidRouteParams a) {
             sa += fabs(v);
         }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        s1 += __shfl_down_sync(0xffffffffu, s1, o);
-        s2 += __shfl_down_sync(0xffffffffu, s2, o);
-        sa += __shfl_down_sync(0xffffffffu, sa, o);
-    }
-    if (lane == 0) {
-        red[0][warp] = s1;
-        red[1][warp] = s2;
-        red[2][warp] = sa;
-    }
-    __syncthreads();
-    if (tid == 0) {
-        double S1 = 0.0, S2 = 0.0, SA = 0.0;
-        for (int w = 0; w < kWarps; ++w) {
-            S1 += red[0][w];
-            S2 += red[1][w];
-            SA += red[2][w];
-        }
-        int open = 0;
-        for (int l = 0; l < a.nl; ++l) {
-            double var;
-            const int d = a.route_all ? 1 : route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var);
-            if (d >= 0) {
-                a.mask[l][t] = static_cast<uint8_t>(d);
-            } else {
-                open = 1;
-            }
-        }
-        s_open = open;
-    }
-    __syncthreads();
-    if (s_open) {
-        // some layer's threshold is inside the f32 error band: the CTA replays the reference's chains
-        // once for the token, then every open decision is taken on that score
-        replay_score<kThreads>(s_row, a.x_stride, s_replay);
-        if (tid == 0) {
-            double S1 = 0.0, S2 = 0.0, SA = 0.0;
-            for (int w = 0; w < kWarps; ++w) {
-                S1 += red[0][w];
-                S2 += red[1][w];
-                SA += red[2][w];
-            }
-            bool have_exact = false;
-            float exact = 0.0f;
-            for (int l = 0; l < a.nl; ++l) {
-                double var;
-                if (route_band(S1, S2, SA, a.rc, a.t4[l], a.t8[l], 0.0, 0.0, &var) >= 0) continue;
-                const bool rl = route_rule_f32(s_replay.lo, a.t4[l], a.t8[l]);
-                const bool rh = route_rule_f32(s_replay.hi, a.t4[l], a.t8[l]);
-                bool routed = rl;
-                if (rl != rh || !(s_replay.lo == s_replay.lo)) {
-                    if (!have_exact) exact = exact_variance_row(s_row, a.x_stride);
-                    have_exact = true;
-                    routed = route_rule_f32(exact, a.t4[l], a.t8[l]);
-                }
-                a.mask[l][t] = routed ? 1 : 0;
-            }
-        }
-    }
-    // completion count; the last CTA compacts every layer's mask
-    if (tid == 0) {
-        __threadfence();
-        const unsigned ticket = atomicAdd(a.counter, 1u);
-        s_last = (ticket == gridDim.x - 1) ? 1 : 0;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int l = 0; l < a.nl; ++l) {
-        int base = 0;
-        for (int t0 = 0; t0 < a.M; t0 += kThreads) {
-            const int tt = t0 + tid;
-            const int v = (tt < a.M) ? (reinterpret_cast<volatile uint8_t*>(a.mask[l])[tt] != 0) : 0;
-            const unsigned bal = __ballot_sync(0xffffffffu, v);
-            if (lane == 0) s_wsum[warp] = __popc(bal);
-            __syncthreads();
-            int pre = 0, tot = 0;
-            for (int w = 0; w < kWarps; ++w) {
-                if (w < warp) pre += s_wsum[w];
-                tot += s_wsum[w];
-            }
-            pre += __popc(bal & ((1u << lane) - 1u));
-            if (v) a.ridx[l][base + pre] = tt;
-            base += tot;
-            __syncthreads();
-        }
-        if (tid == 0) *a.nrouted[l] = base;
-    }
-    if (tid == 0) *a.counter = 0u;
+    route_row<kThreads>(a.r, t, s_row, a.x_stride, s1, s2, sa);
 }
 
 // ---------------------------------------------------------------- the tcgen05 GEMM
@@ -878,20 +775,20 @@ cudaError_t launch_mid(const MidArgs& a, cudaStream_t s) {
         r.x_dtype = a.x_dtype;
         r.vec_ok = ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0 && (a.x_stride % 8) == 0) ? 1 : 0;
         r.x_stride = a.x_stride;
-        r.M = T;
-        r.nl = a.routed_in ? 0 : n;
+        r.r.M = T;
+        r.r.nl = a.routed_in ? 0 : n;
         for (int i = 0; i < SC_GROUP_MAX; ++i) {
             const Layer& L = *a.layer[i < n ? i : 0];
-            r.t4[i] = L.t4;
-            r.t8[i] = L.t8;
-            r.mask[i] = a.mask[i < n ? i : 0];
-            r.ridx[i] = a.ridx[i < n ? i : 0];
-            r.nrouted[i] = a.nrouted[i < n ? i : 0];
+            r.r.t4[i] = L.t4;
+            r.r.t8[i] = L.t8;
+            r.r.mask[i] = a.mask[i < n ? i : 0];
+            r.r.ridx[i] = a.ridx[i < n ? i : 0];
+            r.r.nrouted[i] = a.nrouted[i < n ? i : 0];
         }
-        r.route_all = a.route_all;
-        r.rc = route_consts(a.x_stride);
+        r.r.route_all = a.route_all;
+        r.r.rc = route_consts(a.x_stride);
         r.xcopy = copy ? a.xconv : nullptr;
-        r.counter = a.counter;
+        r.r.counter = a.counter;
         const size_t row_bytes = static_cast<size_t>((a.x_stride * 2 + 15) / 16 * 16);
         static std::atomic<uint64_t> rflags{0};
         int rdev = 0;

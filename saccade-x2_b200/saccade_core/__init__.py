@@ -11,11 +11,11 @@ from .checkpoint import (SaccadeMlp, build_saccade_op, compile_mlp_checkpoint, e
 from .graph import CapturedStep
 from .compress import (ProfileRunner, compress_tensor_to_saccade, compute_percentile_threshold,
                        saccade_op_from_compressed)
-from .op import (SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDeltaMatrix, finalize,
+from .op import (GroupRouting, SaccadeConfig, SaccadeLinearGroup, SaccadeLinearOp, SparseDeltaMatrix, finalize,
                  is_c_tarq_bypassed, set_bypass_c_tarq, variance_heuristic)
 
 __all__ = [
-    "CapturedStep", "CTarqError", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearGroup", "SaccadeLinearOp",
+    "CapturedStep", "CTarqError", "GroupRouting", "LIB_PATH", "ProfileRunner", "SaccadeConfig", "SaccadeLinearGroup", "SaccadeLinearOp",
     "SaccadeMlp", "SparseDeltaMatrix", "build_saccade_op", "compile_mlp_checkpoint", "compress_tensor_to_saccade",
     "compute_percentile_threshold", "extract_scalar_f32", "finalize", "is_c_tarq_bypassed", "load_mlp",
     "load_saccade_checkpoint", "read_safetensors", "saccade_blocks", "saccade_op_from_compressed",

@@ -98,6 +98,8 @@ SIGNATURES = {
     "sc_group_destroy": (None, [_vp]),
     "sc_group_workspace_size": (ctypes.c_size_t, [_vp, _i64]),
     "sc_forward_group": (_int, [_vp, _vp, _int, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "sc_group_takes_routing": (_int, [_vp, _i64, ctypes.c_size_t]),
+    "sc_forward_group_routed": (_int, [_vp, _vp, _i64, _vp, _int, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_forward_partial": (_int, [_vp, _vp, _int, _i64, _vp, _vp, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "sc_finalize": (_int, [_vp, _i64, _i64, _vp, _int, _vp, _vp]),
     "sc_split_exchange_floats": (ctypes.c_size_t, [_vp, _i64]),
@@ -120,6 +122,8 @@ SIGNATURES_QWEN2 = {
     "sc_qwen2_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _int, _int, _vp, ctypes.c_size_t,
                                   _vp, _vp]),
     "sc_qwen2_silu_mul": (_int, [_vp, _vp, _i64, _vp, _vp]),
+    "sc_qwen2_add_rmsnorm_route": (_int, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sc_qwen2_silu_mul_route": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sc_qwen2_f16_to_f32": (_int, [_vp, _i64, _vp, _vp]),
 }
 

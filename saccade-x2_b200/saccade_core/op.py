@@ -399,19 +399,51 @@ class SaccadeLinearGroup:
             release_handle(LIB.sc_group_destroy, h)
             self._h = None
 
+    def _outputs(self, x, out_dtype, outs):
+        shapes = [x.shape[:-1] + (op.out_features,) for op in self.ops]
+        if outs is None:
+            return [torch.empty(sh, dtype=out_dtype, device=self.device) for sh in shapes]
+        ys = list(outs)
+        for y, sh in zip(ys, shapes):
+            if y.shape != sh or y.dtype != out_dtype or not y.is_contiguous() or y.device != self.device:
+                raise ValueError(f"outs must be contiguous {out_dtype} tensors of shapes {shapes}")
+        return ys
+
+    def _bias_ptrs(self, biases):
+        if biases is None:
+            return None
+        bl = [None if b is None else b.to(device=self.device, dtype=torch.float32).contiguous() for b in biases]
+        self._keep_bias = bl
+        return (ctypes.c_void_p * len(bl))(*[None if b is None else b.data_ptr() for b in bl])
+
+    def takes_routing(self, m: int) -> bool:
+        """True when forward_routed serves m tokens: the group runs the 9..64-token launch."""
+        return bool(LIB.sc_group_takes_routing(self._h, m, int(LIB.sc_group_workspace_size(self._h, m))))
+
+    def forward_routed(self, x: torch.Tensor, routing: "GroupRouting", *, out_dtype: torch.dtype = torch.float16,
+                       outs=None, biases=None):
+        """forward(x) with the routing a fused router already wrote for x (sc_forward_group_routed):
+        x is the f16 output of sc_qwen2_add_rmsnorm_route / sc_qwen2_silu_mul_route for this group."""
+        if x.dtype != torch.float16:
+            raise ValueError("forward_routed takes the f16 rows the fused router wrote")
+        m = self.ops[0]._prep_x(x, self.ops[0].in_features)
+        ys = self._outputs(x, out_dtype, outs)
+        if m > 0:
+            stream = torch.cuda.current_stream(self.device)
+            need = int(LIB.sc_group_workspace_size(self._h, m))
+            ws = WORKSPACES.get(self.device, stream, need)
+            yp = (ctypes.c_void_p * len(ys))(*[y.data_ptr() for y in ys])
+            check(LIB.sc_forward_group_routed(self._h, x.data_ptr(), m, yp, _DT[out_dtype], self._bias_ptrs(biases),
+                                              routing.mask_p, routing.ridx_p, routing.count_p, ws.data_ptr(),
+                                              ws.numel(), ctypes.c_void_p(stream.cuda_stream)))
+        return ys
+
     def forward(self, x: torch.Tensor, *, out_dtype: torch.dtype = torch.float16, outs=None,
                 return_routing: bool = False, biases=None):
         """biases: optional per-layer f32 [N] tensors (or None entries), added after the f16 rounding."""
         n = len(self.ops)
         m = self.ops[0]._prep_x(x, self.ops[0].in_features)
-        shapes = [x.shape[:-1] + (op.out_features,) for op in self.ops]
-        if outs is None:
-            ys = [torch.empty(sh, dtype=out_dtype, device=self.device) for sh in shapes]
-        else:
-            ys = list(outs)
-            for y, sh in zip(ys, shapes):
-                if y.shape != sh or y.dtype != out_dtype or not y.is_contiguous() or y.device != self.device:
-                    raise ValueError(f"outs must be contiguous {out_dtype} tensors of shapes {shapes}")
+        ys = self._outputs(x, out_dtype, outs)
         routing = None
         if return_routing:
             routing = [(torch.empty(m, dtype=torch.uint8, device=self.device),
@@ -427,11 +459,7 @@ class SaccadeLinearGroup:
                 mp = (ctypes.c_void_p * n)(*[r[0].data_ptr() for r in routing])
                 rp = (ctypes.c_void_p * n)(*[r[1].data_ptr() for r in routing])
                 np_ = (ctypes.c_void_p * n)(*[r[2].data_ptr() for r in routing])
-            bp = None
-            if biases is not None:
-                bl = [None if b is None else b.to(device=self.device, dtype=torch.float32).contiguous() for b in biases]
-                self._keep_bias = bl
-                bp = (ctypes.c_void_p * n)(*[None if b is None else b.data_ptr() for b in bl])
+            bp = self._bias_ptrs(biases)
             check(LIB.sc_forward_group(self._h, x.data_ptr(), _DT[x.dtype], m, yp, _DT[out_dtype], bp, mp, rp, np_,
                                        ws.data_ptr(), ws.numel(), ctypes.c_void_p(stream.cuda_stream)))
         if return_routing:
@@ -439,3 +467,25 @@ class SaccadeLinearGroup:
         return ys
 
     __call__ = forward
+
+
+class GroupRouting:
+    """The routing of a group's layers for m tokens as a fused router writes it and forward_routed
+    reads it: per layer a mask [m] (u8), the ascending routed list [m] (int32) and its count (int32),
+    plus the router's completion counter (zero between calls; the router leaves it zero)."""
+
+    def __init__(self, n_layers: int, m: int, device):
+        self.n, self.m = n_layers, m
+        self.masks = torch.zeros((n_layers, (m + 15) // 16 * 16), dtype=torch.uint8, device=device)
+        self.ridx = torch.zeros((n_layers, max(m, 1)), dtype=torch.int32, device=device)
+        self.counts = torch.zeros((n_layers, 4), dtype=torch.int32, device=device)
+        self.counter = torch.zeros(4, dtype=torch.int32, device=device)
+        arr = ctypes.c_void_p * n_layers
+        self.mask_p = arr(*[self.masks[i].data_ptr() for i in range(n_layers)])
+        self.ridx_p = arr(*[self.ridx[i].data_ptr() for i in range(n_layers)])
+        self.count_p = arr(*[self.counts[i].data_ptr() for i in range(n_layers)])
+
+    def layer(self, i: int):
+        """(mask [m], routed list, count) of layer i, read back to the host."""
+        c = int(self.counts[i, 0].item())
+        return self.masks[i, :self.m], self.ridx[i, :c], c
