@@ -8,6 +8,9 @@ random prompts, then greedy decoding.  One step = one decode step of the 64 sequ
 replayed as one CUDA graph; tensor parallel over --gpus N (column-sharded q/k/v/gate/up, row-sharded
 o/down with one NCCL all-reduce of [y_base | y_delta | router sums] each, vocab-parallel lm_head).
 value = 64 tokens per step / max-over-ranks device time per step.
+--model qwen2-72b: the Qwen2-72B architecture (hidden 8192, intermediate 29568, 80 layers, 64 query /
+8 KV heads), batch 8, 2048-token prompts (the prefill's device time reported beside), 128 steps;
+--route-pct 0.9 / 0.5 places t4 so that ~10 % / ~50 % of the tokens route.
 
 --workload linear: one step = one decode pass of M tokens through every C-TARQ linear of Qwen2-7B
 (28 layers x {q 3584->3584, k 3584->512, v 3584->512, o 3584->3584, gate 3584->18944,
@@ -19,6 +22,7 @@ Effective bytes per call (the metric's numerator, independent of the device layo
 value = bytes of all calls of all ranks / max-over-ranks device time (CUDA events).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]          # decode tok/s
+  python bench.py --model qwen2-72b [--route-pct 0.9|0.5] [--gpus N]                # 72B prefill + decode
   python bench.py --workload linear [--tokens M] [--impl reference]                # linear GB/s
   python bench.py --sweep OUT.md [--sweep-fills 0.005,0.01,0.04]
                                       # single calls: 4 shapes x M 1..4096 x routed 0/10/25/100 %
@@ -48,6 +52,19 @@ for _p in (ROOT, os.path.join(ROOT, "saccade-x2_b200")):
 HIDDEN, INTER, LAYERS, KV_DIM = 3584, 18944, 28, 512
 PROJ = [("q", 3584, HIDDEN), ("k", KV_DIM, HIDDEN), ("v", KV_DIM, HIDDEN), ("o", HIDDEN, 3584),
         ("gate", INTER, HIDDEN), ("up", INTER, HIDDEN), ("down", HIDDEN, INTER)]  # (name, N, K)
+
+# decode workloads: label, hidden, intermediate, layers, KV width (KV heads x head_dim), and the
+# defaults of batch, prompt tokens, decode steps and sequences per prefill pass
+DECODE_MODELS = {
+    "qwen2-7b": ("Qwen2-7B", 3584, 18944, 28, 512, 64, 512, 256, 16),
+    "qwen2-72b": ("Qwen2-72B", 8192, 29568, 80, 1024, 8, 2048, 128, 2),
+}
+
+
+def model_proj(model):
+    """(name, N, K) of the seven linears of one decoder layer of `model`."""
+    _, h, i, _, kv = DECODE_MODELS[model][:5]
+    return [("q", h, h), ("k", kv, h), ("v", kv, h), ("o", h, h), ("gate", i, h), ("up", i, h), ("down", h, i)]
 T4_BOOSTED = 8.0        # between the variance of N(0,1) tokens (~1) and x8 tokens (~64)
 T8_NEVER = float(np.finfo(np.float32).max)
 METRIC = "C-TARQ linear effective HBM GB/s"
@@ -59,12 +76,17 @@ def parse(argv=None):
     ap.add_argument("--workload", default="decode", choices=["decode", "linear"])
     ap.add_argument("--steps", type=int, default=None, help="timed steps (decode 100, linear 20)")
     ap.add_argument("--warmup", type=int, default=None, help="untimed steps (decode 5, linear 3)")
-    ap.add_argument("--batch", type=int, default=64, help="decode: sequences")
-    ap.add_argument("--prompt", type=int, default=512, help="decode: prompt tokens per sequence")
-    ap.add_argument("--decode-steps", type=int, default=256, help="decode: greedy steps of the workload")
-    ap.add_argument("--prefill-chunk", type=int, default=16, help="decode: sequences per prefill pass")
+    ap.add_argument("--model", default="qwen2-7b", choices=sorted(DECODE_MODELS),
+                    help="decode: the architecture (qwen2-72b: batch 8, 2048-token prompts, 128 steps)")
+    ap.add_argument("--batch", type=int, default=None, help="decode: sequences (7B 64, 72B 8)")
+    ap.add_argument("--prompt", type=int, default=None, help="decode: prompt tokens per sequence (512, 2048)")
+    ap.add_argument("--decode-steps", type=int, default=None, help="decode: greedy steps of the workload (256, 128)")
+    ap.add_argument("--prefill-chunk", type=int, default=None, help="decode: sequences per prefill pass (16, 2)")
+    ap.add_argument("--route-pct", type=float, default=0.75,
+                    help="decode: percentile of the calibration scores at t4 (0.75 routes ~25 %% of tokens, "
+                         "0.9 ~10 %%, 0.5 ~50 %%); t8 at the 95th (99th above 0.9)")
     ap.add_argument("--tokens", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--layers", type=int, default=None, help="decoder layers (default: the model's)")
     ap.add_argument("--fill", type=float, default=0.01)
     ap.add_argument("--route-frac", type=float, default=0.25)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -87,6 +109,14 @@ def parse(argv=None):
     ap.add_argument("--sweep-routed", default=None, metavar="LIST",
                     help="comma-separated routed fractions for --sweep (default: 0,0.1,0.25,1)")
     a = ap.parse_args(argv)
+    _, _, _, layers, _, batch, prompt, dsteps, chunk = DECODE_MODELS[a.model]
+    if a.workload != "decode":
+        layers = LAYERS
+    a.layers = layers if a.layers is None else a.layers
+    a.batch = batch if a.batch is None else a.batch
+    a.prompt = prompt if a.prompt is None else a.prompt
+    a.decode_steps = dsteps if a.decode_steps is None else a.decode_steps
+    a.prefill_chunk = chunk if a.prefill_chunk is None else a.prefill_chunk
     if a.steps is None:
         a.steps = 100 if a.workload == "decode" else 20
     if a.warmup is None:
@@ -126,7 +156,7 @@ def call_bytes(n, k, m, nnz, routed):
 INPUT_OF = {"q": "attn", "k": "attn", "v": "attn", "o": "o", "gate": "mlp", "up": "mlp", "down": "down"}
 
 
-def stack_spec(layers, m, route_frac, seed):
+def stack_spec(layers, m, route_frac, seed, proj=PROJ):
     """(layer, proj, N, K, boosted-token list) for every call of one step; calls that read the
     same activations share their boosted tokens (each token of each input is boosted with
     probability route_frac)."""
@@ -134,7 +164,7 @@ def stack_spec(layers, m, route_frac, seed):
     calls = []
     for li in range(layers):
         boosted_of = {}
-        for name, n, k in PROJ:
+        for name, n, k in proj:
             inp = INPUT_OF[name]
             if inp not in boosted_of:
                 boosted_of[inp] = [t for t in range(m) if rng.random() < route_frac]
@@ -539,15 +569,27 @@ def run_linear(args, rank, world):
 
 # ------------------------------------------------------------------ Qwen2-7B decode
 
-DECODE_METRIC = "Qwen2-7B decode tok/s"
 DECODE_PROJ = ("q", "k", "v", "o", "gate", "up", "down")
 
 
+def decode_metric(args):
+    return f"{DECODE_MODELS[args.model][0]} decode tok/s"
+
+
+def route_pct(args):
+    """Percentiles of the calibration scores where t4 and t8 sit."""
+    p = args.route_pct
+    return p, (0.95 if p < 0.9 else 0.99)
+
+
 def decode_config(args, world):
-    return {"workload": "qwen2-7b batched greedy decode", "model": "qwen2-7b (random init, every linear C-TARQ)",
+    p4, p8 = route_pct(args)
+    return {"workload": f"{args.model} batched greedy decode",
+            "model": f"{args.model} (random init, every linear C-TARQ)",
             "layers": args.layers, "global_batch": args.batch, "prompt_tokens": args.prompt,
             "decode_steps": args.decode_steps, "dw_fill": args.fill,
-            "thresholds": "per projection at the 75th / 95th percentile of a 512-token calibration prompt",
+            "thresholds": f"per projection at the {p4 * 100:g}th / {p8 * 100:g}th percentile of a "
+                          f"{args.prompt}-token calibration prompt",
             "parallelism": f"tp{world}" if world > 1 else "tp1", "fused_route": args.fused_route}
 
 
@@ -569,12 +611,12 @@ def build_decode(args, rank, world, dev, group):
     import torch
 
     from saccade_core import qwen2 as Q
-    cfg = Q.Qwen2Config.qwen2_7b(layers=args.layers)
+    cfg = (Q.Qwen2Config.qwen2_72b if args.model == "qwen2-72b" else Q.Qwen2Config.qwen2_7b)(layers=args.layers)
     ck = Q.random_checkpoint(cfg, seed=42, fill=args.fill, device=dev)
     g = torch.Generator()
     g.manual_seed(7)
     calib = torch.randint(0, cfg.vocab, (1, args.prompt), generator=g)
-    Q.calibrate(ck, calib.to(dev), device=dev, max_pos=args.prompt)
+    Q.calibrate(ck, calib.to(dev), pct=route_pct(args), device=dev, max_pos=args.prompt)
     if world > 1:  # every rank calibrates the same model; rank 0's thresholds are the ones used
         import torch.distributed as dist
         th = torch.tensor([ck.thresholds[li][n] for li in range(len(ck.blocks)) for n in DECODE_PROJ],
@@ -653,9 +695,14 @@ def run_decode(args, rank, world):
     g.manual_seed(11)
     prompts = torch.randint(0, cfg.vocab, (B, S), generator=g)
     dec = Q.GreedyDecoder(model, B)
+    prompts = prompts.to(dev)
+    pf0, pf1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(dec.stream):
-        dec.prefill(prompts.to(dev), chunk=args.prefill_chunk)
+        pf0.record()
+        dec.prefill(prompts, chunk=args.prefill_chunk)
+        pf1.record()
     dec.stream.synchronize()
+    prefill_ms_rank = pf0.elapsed_time(pf1)
     dec.capture()
     setup_s = time.perf_counter() - t_setup
 
@@ -692,6 +739,7 @@ def run_decode(args, rank, world):
     barrier()
     torch.cuda.synchronize()
     ms = max_over_ranks(s_ev.elapsed_time(e_ev) / args.steps)
+    prefill_ms = max_over_ranks(prefill_ms_rank)
 
     # end to end: token ids from pinned host memory in, next ids to pinned host memory out, every step
     ids_host = torch.empty(B, dtype=torch.int64).pin_memory()
@@ -761,13 +809,13 @@ def run_decode(args, rank, world):
     value = B / (ms / 1e3)
     traffic = None
     tp = os.path.join(ROOT, "profiles", "decode_gateup_m64_traffic.json")
-    if os.path.exists(tp):
+    if args.model == "qwen2-7b" and B == 64 and os.path.exists(tp):  # the capture's workload
         try:
             traffic = json.load(open(tp)).get("dram_bytes_per_launch_unit")
         except ValueError:
             pass
     out = {
-        "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": decode_metric(args), "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights, random prompt ids)",
         "config": {**decode_config(args, world), "mode": args.mode, "positions_timed": [pos0, pos0 + args.steps],
@@ -781,7 +829,9 @@ def run_decode(args, rank, world):
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "kernel": f"gate+up C-TARQ call unit at M={B} ({gu_launches} launches: "
                                + ("k_mid_route, then k_ctarq_mid (tcgen05, routed tokens' dW folded into a second A)"
-                                  if 9 <= B <= 64 else "router, token gather, prefill tcgen05 GEMM")
+                                  if 9 <= B <= 64 else
+                                  "the router-fused decode kernel, gate and up in one launch" if B <= 8 else
+                                  "router, token gather, prefill tcgen05 GEMM")
                                + f"), {us_gu:.1f} us per layer, {gu_bytes} algorithmic bytes",
                      "peak_kind": f"{peak_kind} hbm copy"},
         "clocks": clk,
@@ -789,6 +839,10 @@ def run_decode(args, rank, world):
                 "d2h_bytes_per_step": B * 8,
                 "how": "per step: token ids from pinned host memory, the step graph, next ids to pinned host "
                        "memory, host synchronisation"},
+        "prefill": {"tokens": B * S, "ms": round(prefill_ms, 2), "tok_s": round(B * S / (prefill_ms / 1e3), 1),
+                    "sequences_per_pass": args.prefill_chunk,
+                    "how": "device time of the process's first prefill (CUDA events, max over ranks): includes "
+                           "workspace allocation and one-time kernel setup"},
         "gpu_launches": dec.launches_per_step * args.steps,
         "undecided_split_routes": undecided,
         "parity_check": parity,
@@ -800,9 +854,9 @@ def run_decode(args, rank, world):
 
 
 def decode_layer_items(args, tokens):
-    """One Qwen2-7B decoder layer's seven linears on the oracle (synthetic reference-format weights),
-    `tokens` tokens with a seeded 25 % boosted over the router threshold."""
-    calls = stack_spec(1, tokens, args.route_frac, seed=4321)
+    """One decoder layer's seven linears of the model on the oracle (synthetic reference-format
+    weights), `tokens` tokens with a seeded 25 % boosted over the router threshold."""
+    calls = stack_spec(1, tokens, args.route_frac, seed=4321, proj=model_proj(args.model))
     return build_oracle_stack(calls, args.fill, 98, tokens)
 
 
@@ -818,22 +872,23 @@ def cpu_decode_rate(args, seconds):
     reps = max(1, int(seconds / max(dt1, 1e-4)))
     _, dt = time_oracle(items, reps, native)
     per_layer = dt / reps
-    return 1.0 / (per_layer * LAYERS), reps, dt, native
+    return 1.0 / (per_layer * args.layers), reps, dt, native
 
 
 def cpu_baseline_decode(args):
     """The oracle's op.rs restatement on the host cores, per layer (the seven linears of one decoder
-    layer, one token), scaled to 28 layers: tokens per second of the linears alone."""
+    layer, one token), scaled to the model's layers: tokens per second of the linears alone."""
     rate, reps, dt, native = cpu_decode_rate(args, args.cpu_seconds)
+    label = DECODE_MODELS[args.model][0]
     return {"value": round(rate, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 Qwen2-7B decoder layer (7 C-TARQ linears, 1 token) x {reps} reps in {dt:.1f} s, scaled "
-                      f"x{LAYERS} layers (linears only: no attention, norms or lm_head); C restatement of op.rs, "
+            "sample": f"1 {label} decoder layer (7 C-TARQ linears, 1 token) x {reps} reps in {dt:.1f} s, scaled "
+                      f"x{args.layers} layers (linears only: no attention, norms or lm_head); C restatement of op.rs, "
                       f"OpenMP over rows ({'-march=native' if native else 'x86-64-v3'})"}
 
 
 def run_reference_decode(args, rank):
     """--impl reference: the reference's CPU algorithm for the decode step's linears (the oracle's
-    op.rs restatement; the Rust reference cannot be built here), per layer, scaled to 28 layers."""
+    op.rs restatement; the Rust reference cannot be built here), per layer, scaled to the model's layers."""
     if rank != 0:
         return
     from oracle import oracle as O
@@ -853,11 +908,12 @@ def run_reference_decode(args, rank):
         time_oracle(items, reps, native)
     dt = time.perf_counter() - t0
     per_layer = dt / (args.steps * reps)
-    value = 1.0 / (per_layer * LAYERS)
-    sample = (f"each step: 1 Qwen2-7B decoder layer (7 C-TARQ linears, 1 token) x {reps}, scaled x{LAYERS} layers "
+    value = 1.0 / (per_layer * args.layers)
+    sample = (f"each step: 1 {DECODE_MODELS[args.model][0]} decoder layer (7 C-TARQ linears, 1 token) x {reps}, "
+              f"scaled x{args.layers} layers "
               f"(linears only); C restatement of op.rs (Rust reference not buildable here), OpenMP over rows")
-    out = {"metric": DECODE_METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_layer * LAYERS * 1e3, 3),
+    out = {"metric": decode_metric(args), "value": round(value, 3), "unit": "tok/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_layer * args.layers * 1e3, 3),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
            "data": "synthetic", "config": decode_config(args, args.gpus), "impl": "reference",
            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",

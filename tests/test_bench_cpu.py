@@ -79,3 +79,19 @@ def test_sweep_flags_parse(flags):
     a = bench.parse(["--sweep", "out.md"] + flags)
     assert a.sweep == "out.md"
     assert (a.sweep_fills or a.sweep_tokens)
+
+
+def test_decode_model_options():
+    """--model picks the architecture and its workload defaults; --route-pct places t4 (and t8)."""
+    a = bench.parse(["--model", "qwen2-72b", "--route-pct", "0.5"])
+    assert (a.layers, a.batch, a.prompt, a.decode_steps, a.prefill_chunk) == (80, 8, 2048, 128, 2)
+    assert bench.decode_metric(a) == "Qwen2-72B decode tok/s"
+    assert bench.route_pct(a) == (0.5, 0.95)
+    assert bench.route_pct(bench.parse(["--route-pct", "0.9"])) == (0.9, 0.99)
+    proj = {n: (N, K) for n, N, K in bench.model_proj("qwen2-72b")}
+    assert proj == {"q": (8192, 8192), "k": (1024, 8192), "v": (1024, 8192), "o": (8192, 8192),
+                    "gate": (29568, 8192), "up": (29568, 8192), "down": (8192, 29568)}
+    assert bench.model_proj("qwen2-7b") == bench.PROJ
+    d = bench.parse([])
+    assert (d.model, d.layers, d.batch, d.prompt, d.decode_steps) == ("qwen2-7b", 28, 64, 512, 256)
+    assert bench.parse(["--workload", "linear"]).layers == bench.LAYERS
