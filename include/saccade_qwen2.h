@@ -36,7 +36,8 @@ SC_API sc_status sc_qwen2_embed(const int64_t* ids, int64_t tokens, const uint16
 
 /* resid [tokens, hidden] += delta (nullable); out = resid / sqrt(mean(resid^2) + eps) * w, written as
  * f16 (SC_F16: the input of the next linears) or f32 (SC_F32: the final norm before lm_head).  The
- * mean is a fixed-order f32 sum (256 strided partial sums, then those in order). */
+ * mean is a fixed-order f32 sum (256 strided partial sums, then those in order).  hidden <= 16384
+ * (the row is staged in shared memory); SC_EINVAL otherwise. */
 SC_API sc_status sc_qwen2_add_rmsnorm(float* resid, const float* delta, const float* weight, int64_t tokens,
                                       int64_t hidden, float eps, void* out, int out_dtype, void* stream);
 
