@@ -481,6 +481,12 @@ static sc_status make_route(const sc_group* group, int64_t K, int64_t tokens, ui
         set_error(std::string(who) + ": empty group or too many tokens");
         return SC_EINVAL;
     }
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != Ls[0]->device) {
+        set_error(std::string(who) + ": the group's layers live on device " + std::to_string(Ls[0]->device) +
+                  ", which is not the current device");
+        return SC_EINVAL;
+    }
     *r = TokenRoute{};
     r->M = static_cast<int>(tokens);
     r->nl = n;
