@@ -72,3 +72,41 @@ def test_error_type_is_raised():
     from saccade_core import _lib
     with pytest.raises(_lib.CTarqError):
         _lib.check(_lib.SC_EINVAL)
+
+
+def test_routed_group_entry_points_validate_on_the_host():
+    """The fused-router entry points reject missing groups, routing arrays or counters, and the
+    routed GEMM rejects missing routing, before any device call."""
+    from saccade_core import _lib
+    L = _lib.LIB
+    arr = (ctypes.c_void_p * 1)(None)
+    buf = ctypes.create_string_buffer(64)
+    assert L.sc_group_takes_routing(None, 16, 1 << 20) == 0
+    assert L.sc_forward_group_routed(None, buf, 16, arr, _lib.SC_F16, None, arr, arr, arr, None, 0, None) == _lib.SC_EINVAL
+    assert L.sc_qwen2_add_rmsnorm_route(buf, None, buf, 16, 896, ctypes.c_float(1e-6), buf, None, arr, arr, arr, buf,
+                                        None) == _lib.SC_EINVAL
+    assert "null group" in _lib.last_error()
+    assert L.sc_qwen2_add_rmsnorm_route(buf, None, buf, 16, 900, ctypes.c_float(1e-6), buf, None, arr, arr, arr, buf,
+                                        None) == _lib.SC_EINVAL  # hidden not a multiple of 8
+    assert L.sc_qwen2_silu_mul_route(buf, buf, 16, 1020, buf, None, arr, arr, arr, buf, None) == _lib.SC_EINVAL
+    assert L.sc_qwen2_add_rmsnorm_route(buf, None, buf, 0, 896, ctypes.c_float(1e-6), buf, None, arr, arr, arr, buf,
+                                        None) == _lib.SC_OK  # no tokens: nothing to do
+
+
+def test_group_routing_buffers_layout():
+    """GroupRouting: per layer a 16-byte-padded mask row, a routed list and a 16-byte count slot,
+    and pointer arrays that address exactly those rows."""
+    torch = pytest.importorskip("torch")
+    from saccade_core import GroupRouting
+    r = GroupRouting(3, 21, "cpu")
+    assert r.masks.shape == (3, 32) and r.masks.dtype == torch.uint8
+    assert r.ridx.shape == (3, 21) and r.counts.shape == (3, 4)
+    assert int(r.counter.sum()) == 0
+    for i in range(3):
+        assert r.mask_p[i] == r.masks[i].data_ptr()
+        assert r.ridx_p[i] == r.ridx[i].data_ptr()
+        assert r.count_p[i] == r.counts[i].data_ptr()
+    r.counts[1, 0] = 2
+    r.ridx[1, :2] = torch.tensor([4, 9], dtype=torch.int32)
+    mask, ridx, c = r.layer(1)
+    assert c == 2 and ridx.tolist() == [4, 9] and mask.shape == (21,)
